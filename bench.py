@@ -1,0 +1,349 @@
+#!/usr/bin/env python3
+"""Benchmark: Qwen3-8B BF16 decode tokens/s (batch 1) and prefill tokens/s.
+
+Workload ("config 2"): full Qwen3-8B (36 blocks,
+vocabulary 151,936, untied lm_head), synthetic BF16 weights ~N(0, 0.02) from
+seed 1 (Philox4x32-10 / Irwin-Hall generator, norms = 1), one prompt of 512
+token IDs uniform in [0, 151936), then 256 greedy decode steps with a fresh KV
+cache.  One "step" is one such generation (prompt pass + 256 decode passes).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+* `value` = decode tokens/s over the K timed steps (device time of the decode
+  passes, CUDA events on the engine's stream), summed over ranks.
+* `e2e` = generated tokens/s measured around the public generate() call with
+  host prompt IDs in and host token IDs out (copies inside the region).
+* `roofline` = the dominant kernel (the streaming decode GEMV on each block's
+  gate|up matrix, 24576 x 4096 BF16, 201.4 MB per launch) timed with CUDA
+  events on its own stream over 36 distinct matrices (inputs larger than L2).
+* `cpu_baseline` = the CPU restatement of the reference laws (oracle/) timed
+  on this host's cores on a bounded sample (2 decode passes of the full model).
+* `--impl reference` times the reference's host numerical path (the oracle
+  port; the reference has no whole-model CPU engine) on the same workload.
+Under torchrun with N > 1 every rank runs an independent replica (batch-1
+decode does not shard): scaling "weak", value = sum over ranks of tokens /
+max over ranks of the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PROMPT, DECODE, SEED = 512, 256, 1
+METRIC = "Qwen3-8B bf16 decode tok/s (batch 1, % HBM roofline); prefill tok/s"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def model_dims():
+    D, Hq, Hkv, d, F, V, L = 4096, 32, 8, 128, 12288, 151936, 36
+    return D, Hq * d, Hkv * d, F, V, L, d
+
+
+def decode_bytes(S):
+    """Algorithmic bytes of one decode pass at KV length S (after append)."""
+    D, Q, G, F, V, L, d = model_dims()
+    weights = 2 * (L * (D * (Q + 2 * G) + Q * D + 3 * D * F) + D * V)
+    norms = 2 * (L * (2 * D + 2 * d) + D)
+    kv_read = 2 * 2 * L * G * S
+    kv_write = 2 * 2 * L * G
+    return weights + norms + kv_read + kv_write + 2 * D + 2 * V
+
+
+def prefill_flops(P):
+    D, Q, G, F, V, L, d = model_dims()
+    linear = 2 * P * L * (D * (Q + 2 * G) + Q * D + 3 * D * F)
+    attn = L * 4 * Q * sum(p + 1 for p in range(P))
+    return linear + attn + 2 * D * V
+
+
+def prompt_ids(V):
+    return np.random.Generator(np.random.Philox(SEED)).integers(0, V, PROMPT, dtype=np.uint32)
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.flush()
+        rows = []
+        with open(self.file.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9 or parts[0] != str(self.index):
+                    continue
+                try:
+                    rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+                except ValueError:
+                    continue
+        os.unlink(self.file.name)
+        if not rows:
+            return None
+        loaded = [r for r in rows if r[2] > 250.0] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in loaded for n, v in zip(names, r[3]) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows), "samples_under_load": len(loaded)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle's restatement of the reference laws on host cores
+# ---------------------------------------------------------------------------
+def cpu_decode_sample(tensors_fn, steps=2):
+    from oracle import oracle
+    D, Q, G, F, V, L, d = model_dims()
+    cfg = oracle.Config(D, 32, 8, 128, F, V, L, 1e-6, 1e6)
+    tensors = tensors_fn(cfg)
+    model = oracle.OracleModel(cfg, tensors, capacity=steps + 1)
+    ids = prompt_ids(V)
+    t0 = time.perf_counter()
+    for p in range(steps):
+        model.forward([int(ids[p])], p)
+    dt = time.perf_counter() - t0
+    return {"value": steps / dt, "unit": "tok/s", "cores": oracle.lib().or_max_threads(), "kind": "port",
+            "sample": f"{steps} decode passes of full Qwen3-8B (36 blocks, V=151936) at positions 0..{steps - 1} "
+                      "through the oracle's reference-law restatement; weight streaming dominates (attention at "
+                      "640 keys adds <0.1% of the bytes)"}
+
+
+def cpu_tensors_generated(cfg):
+    """Same seeded weights as the GPU engine, generated on the host."""
+    from oracle import oracle
+    glob, block = cfg.shapes()
+    scale = np.float32(0.02 / np.sqrt(8 * (65536.0 ** 2 - 1) / 12))
+    shapes = [s for _, s in glob] + [s for _ in range(cfg.layers) for _, s in block]
+    out = []
+    for i, shp in enumerate(shapes):
+        n = int(np.prod(shp))
+        if len(shp) == 1:
+            out.append(np.full(shp, 0x3F80, np.uint16))
+        else:
+            out.append(oracle.fill_normal_bf16(n, SEED, i, scale).reshape(shp))
+    return out
+
+
+def run_reference(args):
+    world, rank, local = dist_setup()
+    if rank != 0:
+        return 0
+    t0 = time.perf_counter()
+    per = []
+    from oracle import oracle
+    D, Q, G, F, V, L, d = model_dims()
+    cfg = oracle.Config(D, 32, 8, 128, F, V, L, 1e-6, 1e6)
+    tensors = cpu_tensors_generated(cfg)
+    model = oracle.OracleModel(cfg, tensors, capacity=args.warmup + args.steps + 2)
+    ids = prompt_ids(V)
+    for p in range(args.warmup):
+        model.forward([int(ids[p])], p)
+    t1 = time.perf_counter()
+    for i in range(args.steps):
+        p = args.warmup + i
+        s = time.perf_counter()
+        model.forward([int(ids[p])], p)
+        per.append(time.perf_counter() - s)
+    total = time.perf_counter() - t1
+    value = args.steps / total
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights, uniform prompt IDs)",
+            "config": {"workload": "Qwen3-8B config 2 decode (batch 1), one decode pass per step on host cores",
+                       "prompt": PROMPT, "decode_steps": DECODE},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": oracle.lib().or_max_threads(),
+                             "kind": "port",
+                             "sample": f"{args.steps} timed decode passes (after {args.warmup} warm-up) of full "
+                                       "Qwen3-8B through the reference-law restatement (the reference has no "
+                                       "whole-model host engine; its host numerical path is per-operation)"},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "setup_s": t1 - t0}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# Our arm
+# ---------------------------------------------------------------------------
+def dominant_kernel_roofline(engine, cfg, hbm, kind):
+    """Time the decode GEMV on each block's gate|up matrix with CUDA events."""
+    import torch
+    import dolittle_b200 as dl
+    D, F = cfg.hidden, cfg.mlp_width
+    stream = torch.cuda.Stream()
+    x = torch.randn(D, device="cuda").to(torch.bfloat16)
+    y = torch.empty(2 * F, device="cuda", dtype=torch.bfloat16)
+    ptrs = [engine.tensor_device(3 + 11 * l + 8) for l in range(cfg.layers)]
+    L = dl.lib()
+    with torch.cuda.stream(stream):
+        for p in ptrs[:4]:
+            L.dl_projection(dl.DL_BF16, x.data_ptr(), p, y.data_ptr(), 1, D, 2 * F, stream.cuda_stream, None)
+        stream.synchronize()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        reps = 2
+        for _ in range(reps):
+            for p in ptrs:
+                L.dl_projection(dl.DL_BF16, x.data_ptr(), p, y.data_ptr(), 1, D, 2 * F, stream.cuda_stream, None)
+        stop.record(stream)
+        stop.synchronize()
+    ms = start.elapsed_time(stop) / (reps * len(ptrs))
+    algo = 2 * F * D * 2 + D * 2 + 2 * F * 2
+    achieved = algo / (ms * 1e-3) / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+            "traffic": None, "kernel": "gemv_kernel<1> (gate|up 24576x4096, P=16 law)",
+            "bytes_per_launch": algo, "ms_per_launch": ms, "peak_kind": kind}
+
+
+def run_ours(args):
+    world, rank, local = dist_setup()
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600))
+    import dolittle_b200 as dl
+    hbm, tflops, kind = peaks()
+    cfg = dl.QWEN3_8B
+    engine = dl.Engine(cfg, device=local, capacity=PROMPT + DECODE + 8, max_rows=8)
+    engine.init_random(SEED, 0.02)
+    prompt = prompt_ids(cfg.vocabulary)
+    for _ in range(args.warmup):
+        engine.generate(prompt, DECODE + 1)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    clocks = Clocks(local)
+    barrier()
+    gens, walls = [], []
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        g = engine.generate(prompt, DECODE + 1)
+        walls.append(time.perf_counter() - t)
+        gens.append(g)
+    barrier()
+    clk = clocks.stop()
+    decode_s = sum(g.decode_ms for g in gens) / 1000.0
+    prefill_s = sum(g.prefill_ms for g in gens) / 1000.0
+    wall_s = sum(walls)
+    step_s = decode_s + prefill_s
+    if dist is not None:
+        t = torch.tensor([decode_s, prefill_s, wall_s, step_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        decode_s, prefill_s, wall_s, step_s = t.tolist()
+    steps_decoded = gens[0].decode_steps
+    tokens = world * args.steps * steps_decoded
+    value = tokens / decode_s
+    e2e_value = world * args.steps * (DECODE + 1) / wall_s
+    per_rank = steps_decoded * args.steps / (decode_s)
+    mean_S = PROMPT + 1 + (steps_decoded - 1) / 2.0
+    bytes_step = decode_bytes(mean_S)
+    roof = None
+    cpu = None
+    if rank == 0:
+        roof = dominant_kernel_roofline(engine, cfg, hbm, kind)
+        roof["decode_step_gbs"] = bytes_step * per_rank / 1e9
+        roof["decode_step_frac"] = roof["decode_step_gbs"] / hbm
+        roof["decode_step_frac_of_8tbs"] = roof["decode_step_gbs"] / 8000.0
+        if world == 1 and not args.no_cpu_baseline:
+            def from_engine(ocfg):
+                return [engine.get_tensor(i) for i in range(cfg.tensor_count())]
+            cpu = cpu_decode_sample(from_engine)
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        prefill_tok_s = world * args.steps * PROMPT / prefill_s
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000 * step_s / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init BF16 weights ~N(0,0.02), uniform prompt IDs)",
+            "config": {"workload": "Qwen3-8B config 2: 36 blocks, V=151936, prompt 512, 256 greedy decode steps, "
+                                   "batch 1, fresh KV cache per step",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "prefill": "parity (reference reduction order)",
+                       "l2": "weights (16.4 GB) exceed L2; streamed once per decode pass"},
+            "decode_tok_s_per_gpu": per_rank,
+            "prefill_tok_s": prefill_tok_s,
+            "decode_ms_per_token": 1000 * decode_s / (args.steps * steps_decoded),
+            "decode_bytes_per_token": bytes_step,
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "generated tok/s (prompt pass + decode, host IDs in/out)",
+                    "h2d_bytes_per_step": PROMPT * 4 + cfg.vocabulary + 64,
+                    "d2h_bytes_per_step": (DECODE + 1) * 4 + 64},
+            "gpu_launches": sum(g.kernels_total for g in gens),
+            "kernels_per_decode_step": gens[0].kernels_per_decode_step,
+            "clocks": clk,
+            "tokens_check": gens[0].tokens[:8],
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

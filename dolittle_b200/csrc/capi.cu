@@ -1,0 +1,423 @@
+// C ABI entry points (include/dolittle_b200.h).  Validation mirrors the
+// reference's prepared-operation checks (src/kernels/operations.cpp:192-202,
+// src/kernels/cuda/common.cuh:57-65): unsupported dtypes and shapes are
+// rejected, never silently converted.  Exceptions become dl_status codes and
+// a thread-local message.
+#include <cstring>
+#include <exception>
+#include <new>
+#include <stdexcept>
+#include <string>
+
+#include "../../include/dolittle_b200.h"
+#include "engine.h"
+#include "gemv.cuh"
+#include "launch.h"
+#include "sampler.h"
+#include "steering.h"
+
+namespace {
+thread_local std::string g_error;
+
+dl_status fail(dl_status s, const std::string& msg) {
+  g_error = msg;
+  return s;
+}
+dl_status cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return DL_OK;
+  return fail(DL_CUDA_ERROR, std::string(what) + ": " + cudaGetErrorString(e));
+}
+template <class F>
+dl_status guarded(F&& f) {
+  try {
+    return f();
+  } catch (const std::invalid_argument& e) {
+    return fail(DL_INVALID_ARGUMENT, e.what());
+  } catch (const std::length_error& e) {
+    return fail(DL_OUT_OF_MEMORY, e.what());
+  } catch (const std::bad_alloc& e) {
+    return fail(DL_OUT_OF_MEMORY, e.what());
+  } catch (const std::exception& e) {
+    const std::string m = e.what();
+    return fail(m.find("device fault") != std::string::npos ? DL_DEVICE_FAULT : DL_CUDA_ERROR, m);
+  }
+}
+cudaStream_t st(void* s) { return static_cast<cudaStream_t>(s); }
+using dl::bf16;
+}  // namespace
+
+struct dl_engine {
+  dl::Engine* impl;
+};
+struct dl_sampler {
+  dl::Sampler s;
+};
+
+extern "C" {
+
+DL_API const char* dl_last_error(void) { return g_error.c_str(); }
+DL_API const char* dl_version(void) { return "dolittle_b200 0.1 (sm_100a)"; }
+
+DL_API dl_status dl_projection(dl_dtype type, const void* input, const void* weight, void* output,
+                               size_t rows, size_t input_width, size_t output_width, void* stream,
+                               const size_t* output_position) {
+  if (type != DL_BF16) return fail(DL_UNSUPPORTED, "projection: only BF16 storage is supported");
+  if (!input || !weight || !output || !rows || !input_width || !output_width)
+    return fail(DL_INVALID_ARGUMENT, "projection: null pointer or empty shape");
+  if (input_width % 8 || reinterpret_cast<uintptr_t>(weight) % 16)
+    return fail(DL_UNSUPPORTED, "projection: input width must be a multiple of 8, weight 16-byte aligned");
+  if (output_width > (1u << 30) || input_width > (1u << 20)) return fail(DL_UNSUPPORTED, "projection: shape");
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int I = int(input_width);
+  const int rt = dl::gemv_rows_template(int(rows), I);
+  for (size_t g0 = 0; g0 < rows; g0 += rt) {
+    dl::GemvArgs a = {};
+    a.x = static_cast<const bf16*>(input) + g0 * input_width;
+    a.x_stride = I;
+    a.in_width = I;
+    a.nrows = int(std::min<size_t>(rt, rows - g0));
+    a.prologue = dl::kProloguePlain;
+    a.epilogue = dl::kEpilogueStore;
+    a.nseg = 1;
+    a.seg[0].w = static_cast<const bf16*>(weight);
+    a.seg[0].out = static_cast<bf16*>(output) + g0 * output_width;
+    a.seg[0].out_row = reinterpret_cast<const long long*>(output_position);
+    a.seg[0].rows = int(output_width);
+    a.seg[0].partials = dl::projection_partials(input_width, output_width);
+    a.seg[0].out_stride = int(output_width);
+    const dl_status s = cuda_status(dl::launch_gemv(a, rt, sms, st(stream), false), "projection");
+    if (s != DL_OK) return s;
+  }
+  return DL_OK;
+}
+
+DL_API dl_status dl_rms_norm(dl_dtype type, const void* input, const void* weight, void* output,
+                             size_t rows, size_t width, float epsilon, void* stream) {
+  if (type != DL_BF16) return fail(DL_UNSUPPORTED, "rms_norm: only BF16 storage is supported");
+  if (!input || !weight || !output || !rows || !width) return fail(DL_INVALID_ARGUMENT, "rms_norm: arguments");
+  if (width > 8192) return fail(DL_UNSUPPORTED, "rms_norm: width above 8192");
+  return cuda_status(dl::launch_rms_norm(static_cast<const bf16*>(input), static_cast<const bf16*>(weight),
+                                         static_cast<bf16*>(output), rows, int(width), epsilon, st(stream)),
+                     "rms_norm");
+}
+
+DL_API dl_status dl_rotary(dl_dtype type, const void* input, void* output, size_t positions, size_t heads,
+                           size_t width, size_t first_position, double theta, void* stream,
+                           const size_t* device_position, int positioned_output) {
+  if (type != DL_BF16) return fail(DL_UNSUPPORTED, "rotary: only BF16 storage is supported");
+  if (!input || !output || !positions || !heads || !width || width % 2)
+    return fail(DL_INVALID_ARGUMENT, "rotary: arguments");
+  dl::RowPositions pos{reinterpret_cast<const long long*>(device_position), (long long)first_position};
+  return cuda_status(dl::launch_rotary(static_cast<const bf16*>(input), static_cast<bf16*>(output), positions,
+                                       int(heads), int(width), pos, theta, positioned_output != 0, st(stream)),
+                     "rotary");
+}
+
+DL_API dl_status dl_attention_scale(float* output, size_t width, void* stream) {
+  if (!output || !width) return fail(DL_INVALID_ARGUMENT, "attention_scale: arguments");
+  const float v = dl::attention_scale(int(width));
+  return cuda_status(cudaMemcpyAsync(output, &v, 4, cudaMemcpyHostToDevice, st(stream)), "attention_scale");
+}
+
+DL_API size_t dl_attention_workspace_bytes(size_t positions, size_t query_heads, size_t capacity) {
+  return positions * query_heads * capacity * sizeof(float);
+}
+
+DL_API dl_status dl_attention(dl_dtype type, const void* query, const void* key, const void* value,
+                              void* output, size_t positions, size_t query_heads, size_t kv_heads,
+                              size_t width, void* stream, size_t first_position,
+                              const size_t* device_position, size_t capacity, const float* scale,
+                              void* workspace) {
+  (void)scale;  // the scale law float(1/sqrt(double(d))) is applied in-kernel
+  if (type != DL_BF16) return fail(DL_UNSUPPORTED, "attention: only BF16 storage is supported");
+  if (!query || !key || !value || !output || !workspace || !positions || !kv_heads || !width)
+    return fail(DL_INVALID_ARGUMENT, "attention: arguments");
+  if (query_heads % kv_heads || query_heads / kv_heads > 8 || width > 128 || width % 8)
+    return fail(DL_UNSUPPORTED, "attention: GQA group <= 8 and head width <= 128 (multiple of 8)");
+  const size_t cap = device_position ? capacity : first_position + positions;
+  if (cap * 4 > 200 * 1024) return fail(DL_UNSUPPORTED, "attention: more than 51200 keys");
+  dl::RowPositions pos{reinterpret_cast<const long long*>(device_position), (long long)first_position};
+  const int ctas = positions == 1 ? 16 : 8;
+  dl_status s = cuda_status(
+      dl::launch_attention_scores(static_cast<const bf16*>(query), static_cast<const bf16*>(key),
+                                  static_cast<float*>(workspace), pos, int(positions), int(query_heads),
+                                  int(kv_heads), int(width), int(cap), dl::attention_scale(int(width)), ctas,
+                                  st(stream), false),
+      "attention scores");
+  if (s != DL_OK) return s;
+  return cuda_status(dl::launch_attention_pv(static_cast<const float*>(workspace), static_cast<const bf16*>(value),
+                                             static_cast<bf16*>(output), pos, int(positions), int(query_heads),
+                                             int(kv_heads), int(width), int(cap), st(stream), false),
+                     "attention pv");
+}
+
+DL_API dl_status dl_embedding(dl_dtype type, const uint32_t* tokens, const void* weight, void* output,
+                              size_t rows, size_t width, void* stream) {
+  if (type != DL_BF16) return fail(DL_UNSUPPORTED, "embedding: only BF16 storage is supported");
+  if (!tokens || !weight || !output || !rows || !width) return fail(DL_INVALID_ARGUMENT, "embedding: arguments");
+  return cuda_status(dl::launch_embedding(tokens, static_cast<const bf16*>(weight), static_cast<bf16*>(output),
+                                          int(rows), int(width), st(stream), false),
+                     "embedding");
+}
+
+DL_API dl_status dl_add(dl_dtype type, const void* left, const void* right, void* output, size_t count,
+                        void* stream) {
+  if (type != DL_BF16) return fail(DL_UNSUPPORTED, "add: only BF16 storage is supported");
+  if (!left || !right || !output || !count) return fail(DL_INVALID_ARGUMENT, "add: arguments");
+  return cuda_status(dl::launch_add(static_cast<const bf16*>(left), static_cast<const bf16*>(right),
+                                    static_cast<bf16*>(output), count, st(stream)),
+                     "add");
+}
+
+DL_API dl_status dl_silu_multiply(dl_dtype type, const void* gate, const void* up, void* output, size_t count,
+                                  void* stream) {
+  if (type != DL_BF16) return fail(DL_UNSUPPORTED, "silu_multiply: only BF16 storage is supported");
+  if (!gate || !up || !output || !count) return fail(DL_INVALID_ARGUMENT, "silu_multiply: arguments");
+  return cuda_status(dl::launch_silu_multiply(static_cast<const bf16*>(gate), static_cast<const bf16*>(up),
+                                              static_cast<bf16*>(output), count, st(stream)),
+                     "silu_multiply");
+}
+
+DL_API dl_status dl_qkv_projection(const void* residual, const void* norm_weight, float epsilon,
+                                   const void* wqkv, size_t rows, size_t input_width, size_t q_rows,
+                                   size_t kv_rows, void* q_out, void* k_out, void* v_out,
+                                   const int64_t* v_position, void* stream) {
+  if (!residual || !norm_weight || !wqkv || !q_out || !k_out || !v_out || !rows || rows > 8)
+    return fail(DL_INVALID_ARGUMENT, "qkv_projection: arguments (rows 1..8)");
+  if (input_width % 8 || input_width * 2 * rows > 64 * 1024 && rows > 1)
+    return fail(DL_UNSUPPORTED, "qkv_projection: input width");
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  dl::GemvArgs a = {};
+  const int I = int(input_width), Qr = int(q_rows), Kr = int(kv_rows);
+  const bf16* w = static_cast<const bf16*>(wqkv);
+  a.x = static_cast<const bf16*>(residual);
+  a.x_stride = I;
+  a.in_width = I;
+  a.nrows = int(rows);
+  a.prologue = dl::kPrologueRmsNorm;
+  a.norm_w = static_cast<const bf16*>(norm_weight);
+  a.eps = epsilon;
+  a.epilogue = dl::kEpilogueStore;
+  a.nseg = 3;
+  a.seg[0] = {w, static_cast<bf16*>(q_out), nullptr, Qr, dl::projection_partials(I, Qr), 0, 0, Qr};
+  a.seg[1] = {w + size_t(Qr) * I, static_cast<bf16*>(k_out), nullptr, Kr, dl::projection_partials(I, Kr), 0, 0, Kr};
+  a.seg[2] = {w + size_t(Qr + Kr) * I, static_cast<bf16*>(v_out), reinterpret_cast<const long long*>(v_position),
+              Kr, dl::projection_partials(I, Kr), 0, 0, Kr};
+  return cuda_status(dl::launch_gemv(a, dl::gemv_rows_template(int(rows), I), sms, st(stream), false),
+                     "qkv_projection");
+}
+
+DL_API dl_status dl_rope_inverse_frequency(float* output, size_t width, double theta, void* stream) {
+  if (!output || !width || width % 2) return fail(DL_INVALID_ARGUMENT, "rope_inverse_frequency: arguments");
+  return cuda_status(dl::launch_inv_freq(output, int(width), theta, st(stream)), "rope_inverse_frequency");
+}
+
+DL_API dl_status dl_qk_norm_rope_append(const void* q_raw, const void* k_raw, const void* q_norm_weight,
+                                        const void* k_norm_weight, const float* inv_freq, void* q_out,
+                                        void* k_cache, const int64_t* position, size_t rows,
+                                        size_t query_heads, size_t kv_heads, size_t width, float epsilon,
+                                        void* stream) {
+  if (!q_raw || !k_raw || !q_norm_weight || !k_norm_weight || !inv_freq || !q_out || !k_cache || !position ||
+      !rows || !query_heads || !kv_heads)
+    return fail(DL_INVALID_ARGUMENT, "qk_norm_rope_append: arguments");
+  if (width > 128 || width % 2) return fail(DL_UNSUPPORTED, "qk_norm_rope_append: head width <= 128, even");
+  dl::RowPositions pos{reinterpret_cast<const long long*>(position), 0};
+  return cuda_status(dl::launch_qk_norm_rope(static_cast<const bf16*>(q_raw), static_cast<const bf16*>(k_raw),
+                                             static_cast<const bf16*>(q_norm_weight),
+                                             static_cast<const bf16*>(k_norm_weight), inv_freq,
+                                             static_cast<bf16*>(q_out), static_cast<bf16*>(k_cache), pos,
+                                             int(rows), int(query_heads), int(kv_heads), int(width), epsilon,
+                                             st(stream), false),
+                     "qk_norm_rope_append");
+}
+
+DL_API dl_status dl_projection_residual(const void* input, const void* weight, void* residual, size_t rows,
+                                        size_t input_width, size_t output_width, void* stream) {
+  if (!input || !weight || !residual || !rows || input_width % 8)
+    return fail(DL_INVALID_ARGUMENT, "projection_residual: arguments");
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int I = int(input_width);
+  const int rt = dl::gemv_rows_template(int(rows), I);
+  for (size_t g0 = 0; g0 < rows; g0 += rt) {
+    dl::GemvArgs a = {};
+    a.x = static_cast<const bf16*>(input) + g0 * input_width;
+    a.x_stride = I;
+    a.in_width = I;
+    a.nrows = int(std::min<size_t>(rt, rows - g0));
+    a.prologue = dl::kProloguePlain;
+    a.epilogue = dl::kEpilogueResidual;
+    a.nseg = 1;
+    a.seg[0] = {static_cast<const bf16*>(weight), static_cast<bf16*>(residual) + g0 * output_width, nullptr,
+                int(output_width), dl::projection_partials(input_width, output_width), 0, 0, int(output_width)};
+    const dl_status s = cuda_status(dl::launch_gemv(a, rt, sms, st(stream), false), "projection_residual");
+    if (s != DL_OK) return s;
+  }
+  return DL_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Steering / injection
+// ---------------------------------------------------------------------------
+DL_API dl_status dl_intervene(void* residual, const float* direction, const int64_t* position, uint32_t* state,
+                              size_t width, size_t selected, size_t rows, float strength, void* stream) {
+  if (!residual || !direction || !position || !state || !width || !rows)
+    return fail(DL_INVALID_ARGUMENT, "intervene: arguments");
+  return cuda_status(dl::launch_intervene(static_cast<bf16*>(residual), direction,
+                                          reinterpret_cast<const long long*>(position), state, int(width),
+                                          (long long)selected, int(rows), strength, st(stream), false),
+                     "intervene");
+}
+
+DL_API dl_status dl_normalize_injection(const void* source, void* output, float* norm, uint32_t* status,
+                                        size_t width, float scale, void* stream) {
+  if (!source || !output || !norm || !status || !width) return fail(DL_INVALID_ARGUMENT, "normalize: arguments");
+  return cuda_status(dl::launch_normalize_injection(static_cast<const bf16*>(source), static_cast<bf16*>(output),
+                                                    norm, status, int(width), scale, st(stream)),
+                     "normalize_injection");
+}
+
+// ---------------------------------------------------------------------------
+// Sampler
+// ---------------------------------------------------------------------------
+DL_API size_t dl_sampler_required_bytes(size_t vocabulary) { return dl::sampler_required_bytes(vocabulary); }
+
+DL_API dl_status dl_sampler_create(size_t vocabulary, dl_dtype type, dl_sampler** out) {
+  if (!out || !vocabulary || vocabulary > 0x7fffffffu) return fail(DL_INVALID_ARGUMENT, "sampler: vocabulary");
+  auto* s = new dl_sampler;
+  const dl_status r = cuda_status(dl::sampler_init(s->s, vocabulary, type == DL_BF16), "sampler_create");
+  if (r != DL_OK) {
+    dl::sampler_free(s->s);
+    delete s;
+    return r;
+  }
+  *out = s;
+  return DL_OK;
+}
+
+DL_API void dl_sampler_destroy(dl_sampler* s) {
+  if (!s) return;
+  dl::sampler_free(s->s);
+  delete s;
+}
+
+DL_API dl_status dl_sampler_start(dl_sampler* s, const dl_sampling* settings, uint64_t seed,
+                                  const uint32_t* stop_ids, size_t n_stop, void* stream) {
+  if (!s || !settings || (n_stop && !stop_ids)) return fail(DL_INVALID_ARGUMENT, "sampler_start: arguments");
+  return guarded([&] {
+    if (s->s.started) throw std::invalid_argument("invalid or repeated device sampler start");
+    dl::validate_sampling(*settings, s->s.vocabulary);
+    for (size_t i = 0; i < n_stop; ++i)
+      if (stop_ids[i] >= s->s.vocabulary) throw std::invalid_argument("stop ID outside vocabulary");
+    const dl_status r =
+        cuda_status(dl::sampler_start(s->s, *settings, seed, stop_ids, n_stop, st(stream)), "sampler_start");
+    return r;
+  });
+}
+
+DL_API dl_status dl_sampler_submit(dl_sampler* s, const void* row, const dl_sampling* settings, uint64_t bits,
+                                   void* stream, const uint32_t** result) {
+  if (!s || !row || !settings) return fail(DL_INVALID_ARGUMENT, "sampler_submit: arguments");
+  return guarded([&] {
+    dl::validate_sampling(*settings, s->s.vocabulary);
+    const dl_status r =
+        cuda_status(dl::sampler_submit(s->s, row, *settings, bits, false, st(stream)), "sampler_submit");
+    if (result) *result = s->s.result;
+    return r;
+  });
+}
+
+DL_API dl_status dl_sampler_submit_next(dl_sampler* s, const void* row, void* stream, const uint32_t** result) {
+  if (!s || !row) return fail(DL_INVALID_ARGUMENT, "sampler_submit_next: arguments");
+  if (!s->s.started) return fail(DL_INVALID_ARGUMENT, "device sampler not started");
+  const dl_status r =
+      cuda_status(dl::sampler_submit(s->s, row, s->s.settings, 0, true, st(stream)), "sampler_submit_next");
+  if (result) *result = s->s.result;
+  return r;
+}
+
+// ---------------------------------------------------------------------------
+// Engine
+// ---------------------------------------------------------------------------
+DL_API size_t dl_engine_tensor_count(const dl_model_config* c) { return c ? dl::Engine::tensor_count(*c) : 0; }
+
+DL_API dl_status dl_engine_tensor_shape(const dl_model_config* c, size_t index, size_t* rows, size_t* cols) {
+  if (!c || !rows || !cols || !dl::Engine::tensor_shape(*c, index, rows, cols))
+    return fail(DL_INVALID_ARGUMENT, "tensor_shape: index");
+  return DL_OK;
+}
+
+DL_API dl_status dl_engine_create(const dl_model_config* config, int device, size_t capacity, size_t max_rows,
+                                  dl_engine** out) {
+  if (!config || !out) return fail(DL_INVALID_ARGUMENT, "engine_create: arguments");
+  return guarded([&] {
+    *out = new dl_engine{new dl::Engine(*config, device, capacity, max_rows)};
+    return DL_OK;
+  });
+}
+
+DL_API void dl_engine_destroy(dl_engine* e) {
+  if (!e) return;
+  delete e->impl;
+  delete e;
+}
+
+#define DL_ENGINE_CALL(body)                                           \
+  if (!e || !e->impl) return fail(DL_INVALID_ARGUMENT, "null engine"); \
+  return guarded([&] {                                                 \
+    body;                                                              \
+    return DL_OK;                                                      \
+  })
+
+DL_API dl_status dl_engine_init_random(dl_engine* e, uint64_t seed, float sigma) {
+  DL_ENGINE_CALL(e->impl->init_random(seed, sigma));
+}
+DL_API dl_status dl_engine_set_tensor(dl_engine* e, size_t index, const void* host_bits, size_t bytes) {
+  DL_ENGINE_CALL(e->impl->set_tensor(index, host_bits, bytes));
+}
+DL_API dl_status dl_engine_get_tensor(dl_engine* e, size_t index, void* host_bits, size_t bytes) {
+  DL_ENGINE_CALL(e->impl->get_tensor(index, host_bits, bytes));
+}
+DL_API dl_status dl_engine_tensor_device(dl_engine* e, size_t index, void** device_ptr) {
+  if (!device_ptr) return fail(DL_INVALID_ARGUMENT, "tensor_device: null output");
+  DL_ENGINE_CALL(*device_ptr = e->impl->tensor_device(index));
+}
+DL_API dl_status dl_engine_reset(dl_engine* e) { DL_ENGINE_CALL(e->impl->reset()); }
+DL_API dl_status dl_engine_consume(dl_engine* e, const uint32_t* tokens, size_t n, int mode, uint16_t* logits_out) {
+  DL_ENGINE_CALL(e->impl->consume(tokens, n, mode, logits_out));
+}
+DL_API size_t dl_engine_position(dl_engine* e) {
+  if (!e || !e->impl) return 0;
+  try {
+    return e->impl->position();
+  } catch (...) {
+    return 0;
+  }
+}
+DL_API dl_status dl_engine_set_capture(dl_engine* e, int layer) { DL_ENGINE_CALL(e->impl->set_capture(layer)); }
+DL_API dl_status dl_engine_read_capture(dl_engine* e, size_t first, size_t count, uint16_t* host) {
+  DL_ENGINE_CALL(e->impl->read_capture(first, count, host));
+}
+DL_API dl_status dl_engine_set_intervention(dl_engine* e, int layer, size_t selected, float strength,
+                                            const float* host_direction) {
+  DL_ENGINE_CALL(e->impl->set_intervention(layer, selected, strength, host_direction));
+}
+DL_API dl_status dl_engine_read_kv(dl_engine* e, size_t layer, int values, size_t first, size_t count,
+                                   uint16_t* host) {
+  DL_ENGINE_CALL(e->impl->read_kv(layer, values, first, count, host));
+}
+DL_API dl_status dl_engine_generate(dl_engine* e, const uint32_t* prompt, size_t n_prompt, size_t max_new,
+                                    const dl_sampling* settings, uint64_t seed, const uint32_t* stop_ids,
+                                    size_t n_stop, int prefill_mode, uint32_t* tokens_out, size_t* n_out,
+                                    uint16_t* logits_out, dl_generation_stats* stats) {
+  if (!settings || !prompt || !tokens_out || !n_out) return fail(DL_INVALID_ARGUMENT, "generate: arguments");
+  DL_ENGINE_CALL(e->impl->generate(prompt, n_prompt, max_new, *settings, seed, stop_ids, n_stop, prefill_mode,
+                                   tokens_out, n_out, logits_out, stats));
+}
+
+}  // extern "C"

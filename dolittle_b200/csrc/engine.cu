@@ -1,0 +1,547 @@
+// Engine implementation (see engine.h).
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+#include "engine.h"
+#include "steering.h"
+
+namespace dl {
+
+namespace {
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct Shape {
+  size_t rows, cols;
+};
+
+Shape shape_of(const dl_model_config& c, size_t index) {
+  const size_t D = c.hidden, Q = size_t(c.query_heads) * c.head_width,
+               G = size_t(c.kv_heads) * c.head_width, F = c.mlp_width, V = c.vocabulary,
+               d = c.head_width;
+  if (index == 0) return {V, D};
+  if (index == 1) return {1, D};
+  if (index == 2) return {V, D};
+  switch ((index - 3) % 11) {
+    case 0: return {1, D};
+    case 1: return {Q, D};
+    case 2: return {G, D};
+    case 3: return {G, D};
+    case 4: return {1, d};
+    case 5: return {1, d};
+    case 6: return {D, Q};
+    case 7: return {1, D};
+    case 8: return {F, D};
+    case 9: return {F, D};
+    default: return {D, F};
+  }
+}
+}  // namespace
+
+bool Engine::tensor_shape(const dl_model_config& c, size_t index, size_t* rows, size_t* cols) {
+  if (index >= tensor_count(c)) return false;
+  const Shape s = shape_of(c, index);
+  *rows = s.rows;
+  *cols = s.cols;
+  return true;
+}
+
+void Engine::check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+Engine::Engine(const dl_model_config& cfg, int device, size_t capacity, size_t max_rows)
+    : cfg_(cfg), device_(device), capacity_(capacity), max_rows_(max_rows) {
+  const size_t D = cfg.hidden, Q = size_t(cfg.query_heads) * cfg.head_width,
+               G = size_t(cfg.kv_heads) * cfg.head_width, F = cfg.mlp_width, V = cfg.vocabulary,
+               d = cfg.head_width, L = cfg.layers;
+  if (!D || !Q || !G || !F || !V || !L || !capacity || !max_rows || max_rows > 64 ||
+      cfg.query_heads % cfg.kv_heads || d > 128 || d % 2 || D % 8 || Q % 8 || F % 8 ||
+      cfg.query_heads / cfg.kv_heads > 8)
+    throw std::invalid_argument("unsupported Qwen3 configuration");
+  check(cudaSetDevice(device), "cudaSetDevice");
+  int sms = 0;
+  check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "sm count");
+  sms_ = sms;
+  check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "stream");
+  for (auto& ev : ev_) check(cudaEventCreate(&ev), "event");
+
+  // ---- weights: one arena, 256-byte aligned tensors ----
+  size_t off = 0;
+  auto take = [&](size_t elems) {
+    const size_t o = off;
+    off = align_up(off + elems * 2, 256);
+    return o;
+  };
+  const size_t o_embed = take(V * D), o_final = take(D), o_head = take(V * D);
+  std::vector<size_t> lo(L * 8);
+  for (size_t l = 0; l < L; ++l) {
+    lo[l * 8 + 0] = take(D);
+    lo[l * 8 + 1] = take((Q + 2 * G) * D);
+    lo[l * 8 + 2] = take(d);
+    lo[l * 8 + 3] = take(d);
+    lo[l * 8 + 4] = take(D * Q);
+    lo[l * 8 + 5] = take(D);
+    lo[l * 8 + 6] = take(2 * F * D);
+    lo[l * 8 + 7] = take(D * F);
+  }
+  weight_bytes_ = off;
+  check(cudaMalloc(&weight_arena_, weight_bytes_), "weights");
+  auto* base = static_cast<unsigned char*>(weight_arena_);
+  embed_ = reinterpret_cast<bf16*>(base + o_embed);
+  final_norm_ = reinterpret_cast<bf16*>(base + o_final);
+  lm_head_ = reinterpret_cast<bf16*>(base + o_head);
+  layers_.resize(L);
+  for (size_t l = 0; l < L; ++l) {
+    Layer& y = layers_[l];
+    y.in_norm = reinterpret_cast<bf16*>(base + lo[l * 8 + 0]);
+    y.wqkv = reinterpret_cast<bf16*>(base + lo[l * 8 + 1]);
+    y.q_norm = reinterpret_cast<bf16*>(base + lo[l * 8 + 2]);
+    y.k_norm = reinterpret_cast<bf16*>(base + lo[l * 8 + 3]);
+    y.wo = reinterpret_cast<bf16*>(base + lo[l * 8 + 4]);
+    y.post_norm = reinterpret_cast<bf16*>(base + lo[l * 8 + 5]);
+    y.wgu = reinterpret_cast<bf16*>(base + lo[l * 8 + 6]);
+    y.wd = reinterpret_cast<bf16*>(base + lo[l * 8 + 7]);
+  }
+
+  // ---- KV cache: per block K[C][Hkv][d] then V[C][Hkv][d] ----
+  const size_t kv_block = align_up(capacity * G * 2, 256);
+  check(cudaMalloc(&kv_arena_, kv_block * 2 * L), "kv cache");
+  check(cudaMemsetAsync(kv_arena_, 0, kv_block * 2 * L, stream_), "kv clear");
+  for (size_t l = 0; l < L; ++l) {
+    kcache_.push_back(reinterpret_cast<bf16*>(static_cast<unsigned char*>(kv_arena_) + kv_block * (2 * l)));
+    vcache_.push_back(reinterpret_cast<bf16*>(static_cast<unsigned char*>(kv_arena_) + kv_block * (2 * l + 1)));
+  }
+
+  // ---- scratch ----
+  const size_t R = max_rows;
+  history_cap_ = capacity + 1;
+  size_t s = 0;
+  auto stake = [&](size_t bytes) {
+    const size_t o = s;
+    s = align_up(s + bytes, 256);
+    return o;
+  };
+  const size_t o_res = stake(R * D * 2), o_qraw = stake(R * Q * 2), o_kraw = stake(R * G * 2),
+               o_qrot = stake(R * Q * 2), o_att = stake(R * Q * 2), o_gu = stake(R * 2 * F * 2),
+               o_logits = stake(V * 2), o_scores = stake(R * cfg.query_heads * capacity * 4),
+               o_tok = stake(std::max<size_t>(R, 64) * 4), o_hist = stake(history_cap_ * 4),
+               o_part = stake(size_t(4 * sms_) * 16), o_state = stake(sizeof(DeviceState)),
+               o_inv = stake(d * 2), o_dir = stake(D * 4), o_edit = stake(64),
+               o_cap = stake(capacity * D * 2);
+  check(cudaMalloc(&scratch_, s), "scratch");
+  check(cudaMemsetAsync(scratch_, 0, s, stream_), "scratch clear");
+  auto* sb = static_cast<unsigned char*>(scratch_);
+  residual_ = reinterpret_cast<bf16*>(sb + o_res);
+  q_raw_ = reinterpret_cast<bf16*>(sb + o_qraw);
+  k_raw_ = reinterpret_cast<bf16*>(sb + o_kraw);
+  q_rot_ = reinterpret_cast<bf16*>(sb + o_qrot);
+  att_ = reinterpret_cast<bf16*>(sb + o_att);
+  gu_ = reinterpret_cast<bf16*>(sb + o_gu);
+  logits_ = reinterpret_cast<bf16*>(sb + o_logits);
+  scores_ = reinterpret_cast<float*>(sb + o_scores);
+  tokens_dev_ = reinterpret_cast<uint32_t*>(sb + o_tok);
+  history_ = reinterpret_cast<uint32_t*>(sb + o_hist);
+  partials_ = reinterpret_cast<uint4*>(sb + o_part);
+  state_ = reinterpret_cast<DeviceState*>(sb + o_state);
+  inv_freq_ = reinterpret_cast<float*>(sb + o_inv);
+  edit_direction_ = reinterpret_cast<float*>(sb + o_dir);
+  edit_state_ = reinterpret_cast<uint32_t*>(sb + o_edit);
+  capture_arena_ = reinterpret_cast<bf16*>(sb + o_cap);
+  check(launch_inv_freq(inv_freq_, int(d), cfg.theta, stream_), "inv_freq");
+  check(cudaStreamSynchronize(stream_), "init sync");
+}
+
+Engine::~Engine() {
+  if (decode_exec_) cudaGraphExecDestroy(decode_exec_);
+  for (auto& ev : ev_)
+    if (ev) cudaEventDestroy(ev);
+  cudaFree(scratch_);
+  cudaFree(kv_arena_);
+  cudaFree(weight_arena_);
+  if (stream_) cudaStreamDestroy(stream_);
+}
+
+bf16* Engine::tensor_ptr(size_t index, size_t* elems) {
+  const Shape sh = shape_of(cfg_, index);
+  *elems = sh.rows * sh.cols;
+  if (index == 0) return embed_;
+  if (index == 1) return final_norm_;
+  if (index == 2) return lm_head_;
+  const size_t l = (index - 3) / 11, role = (index - 3) % 11;
+  const size_t D = cfg_.hidden, Q = size_t(cfg_.query_heads) * cfg_.head_width,
+               G = size_t(cfg_.kv_heads) * cfg_.head_width, F = cfg_.mlp_width;
+  const Layer& y = layers_[l];
+  switch (role) {
+    case 0: return y.in_norm;
+    case 1: return y.wqkv;
+    case 2: return y.wqkv + Q * D;
+    case 3: return y.wqkv + (Q + G) * D;
+    case 4: return y.q_norm;
+    case 5: return y.k_norm;
+    case 6: return y.wo;
+    case 7: return y.post_norm;
+    case 8: return y.wgu;
+    case 9: return y.wgu + F * D;
+    default: return y.wd;
+  }
+}
+
+void Engine::init_random(uint64_t seed, float sigma) {
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  const double sd = std::sqrt(8.0 * (65536.0 * 65536.0 - 1.0) / 12.0);
+  const float scale = static_cast<float>(double(sigma) / sd);
+  for (size_t i = 0; i < tensor_count(cfg_); ++i) {
+    size_t n = 0;
+    bf16* p = tensor_ptr(i, &n);
+    const Shape sh = shape_of(cfg_, i);
+    if (sh.rows == 1)
+      check(launch_fill_const(p, n, 1.0f, stream_), "fill norm");
+    else
+      check(launch_fill_normal(p, n, seed, uint32_t(i), scale, stream_), "fill normal");
+  }
+  check(cudaStreamSynchronize(stream_), "init_random sync");
+}
+
+void Engine::set_tensor(size_t index, const void* host, size_t bytes) {
+  size_t n = 0;
+  if (index >= tensor_count(cfg_)) throw std::invalid_argument("tensor index out of range");
+  bf16* p = tensor_ptr(index, &n);
+  if (bytes != n * 2) throw std::invalid_argument("tensor byte size mismatch");
+  check(cudaMemcpyAsync(p, host, bytes, cudaMemcpyHostToDevice, stream_), "set_tensor");
+  check(cudaStreamSynchronize(stream_), "set_tensor sync");
+}
+
+void Engine::get_tensor(size_t index, void* host, size_t bytes) {
+  size_t n = 0;
+  if (index >= tensor_count(cfg_)) throw std::invalid_argument("tensor index out of range");
+  bf16* p = tensor_ptr(index, &n);
+  if (bytes != n * 2) throw std::invalid_argument("tensor byte size mismatch");
+  check(cudaMemcpyAsync(host, p, bytes, cudaMemcpyDeviceToHost, stream_), "get_tensor");
+  check(cudaStreamSynchronize(stream_), "get_tensor sync");
+}
+
+void Engine::reset() {
+  DeviceState z = {};
+  check(cudaMemcpyAsync(state_, &z, sizeof(z), cudaMemcpyHostToDevice, stream_), "reset");
+  const uint32_t zero[2] = {0, 0};
+  check(cudaMemcpyAsync(edit_state_, zero, sizeof(zero), cudaMemcpyHostToDevice, stream_), "reset edit");
+  check(cudaStreamSynchronize(stream_), "reset sync");
+}
+
+size_t Engine::position() {
+  DeviceState s;
+  check(cudaMemcpyAsync(&s, state_, sizeof(s), cudaMemcpyDeviceToHost, stream_), "position");
+  check(cudaStreamSynchronize(stream_), "position sync");
+  return size_t(s.position);
+}
+
+void Engine::check_fault() {
+  unsigned err = 0;
+  check(cudaMemcpyAsync(&err, &state_->err, 4, cudaMemcpyDeviceToHost, stream_), "fault read");
+  check(cudaStreamSynchronize(stream_), "fault sync");
+  if (err) throw std::runtime_error("device fault word " + std::to_string(err));
+}
+
+// One projection (possibly several segments sharing the input) over `rows`
+// input rows, split into row groups the streaming kernel holds in smem.
+void Engine::project(const bf16* x, int x_stride, int rows, int in_width, int prologue,
+                     const bf16* norm_w, int epilogue, GemvSegment* segs, int nseg, bool pdl) {
+  const int rt = gemv_rows_template(rows, in_width);
+  for (int g0 = 0; g0 < rows; g0 += rt) {
+    GemvArgs a = {};
+    a.x = x + size_t(g0) * x_stride;
+    a.x_stride = x_stride;
+    a.in_width = in_width;
+    a.nrows = std::min(rt, rows - g0);
+    a.prologue = prologue;
+    a.norm_w = norm_w;
+    a.eps = cfg_.epsilon;
+    a.epilogue = epilogue;
+    a.nseg = nseg;
+    for (int i = 0; i < nseg; ++i) {
+      a.seg[i] = segs[i];
+      a.seg[i].out = segs[i].out + size_t(g0) * segs[i].out_stride;
+    }
+    if (epilogue == kEpilogueResidual && capture_arena_ && capture_target_) {
+      a.capture = capture_arena_ + size_t(g0) * cfg_.hidden;
+      a.capture_row = &state_->position;
+      a.capture_stride = int(cfg_.hidden);
+    }
+    a.err = &state_->err;
+    check(launch_gemv(a, rt, sms_, stream_, pdl), "gemv");
+    ++launches_;
+  }
+}
+
+void Engine::run_layers(int rows, bool pdl) {
+  const int D = int(cfg_.hidden), Q = int(cfg_.query_heads * cfg_.head_width),
+            G = int(cfg_.kv_heads * cfg_.head_width), F = int(cfg_.mlp_width),
+            d = int(cfg_.head_width), H = int(cfg_.query_heads), Hk = int(cfg_.kv_heads);
+  const RowPositions pos{&state_->position, 0};
+  const float scale = attention_scale(d);
+  const int cap = int(capacity_);
+  const int score_ctas = rows == 1 ? std::clamp((cap + 63) / 64, 1, 16) : std::clamp((cap + 255) / 256, 1, 8);
+  for (size_t l = 0; l < layers_.size(); ++l) {
+    const Layer& y = layers_[l];
+    GemvSegment qkv[3] = {};
+    qkv[0] = {y.wqkv, q_raw_, nullptr, Q, projection_partials(D, Q), 0, 0, Q};
+    qkv[1] = {y.wqkv + size_t(Q) * D, k_raw_, nullptr, G, projection_partials(D, G), 0, 0, G};
+    qkv[2] = {y.wqkv + size_t(Q + G) * D, vcache_[l], &state_->position, G, projection_partials(D, G), 0, 0, G};
+    capture_target_ = false;
+    project(residual_, D, rows, D, kPrologueRmsNorm, y.in_norm, kEpilogueStore, qkv, 3, pdl);
+    check(launch_qk_norm_rope(q_raw_, k_raw_, y.q_norm, y.k_norm, inv_freq_, q_rot_, kcache_[l], pos, rows,
+                              H, Hk, d, cfg_.epsilon, stream_, pdl),
+          "qk_norm_rope");
+    check(launch_attention_scores(q_rot_, kcache_[l], scores_, pos, rows, H, Hk, d, cap, scale, score_ctas,
+                                  stream_, pdl),
+          "attention scores");
+    check(launch_attention_pv(scores_, vcache_[l], att_, pos, rows, H, Hk, d, cap, stream_, pdl),
+          "attention pv");
+    launches_ += 3;
+    GemvSegment o = {y.wo, residual_, nullptr, D, projection_partials(Q, D), 0, 0, D};
+    project(att_, Q, rows, Q, kProloguePlain, nullptr, kEpilogueResidual, &o, 1, pdl);
+    GemvSegment gu = {y.wgu, gu_, nullptr, 2 * F, projection_partials(D, F), 0, 0, 2 * F};
+    project(residual_, D, rows, D, kPrologueRmsNorm, y.post_norm, kEpilogueStore, &gu, 1, pdl);
+    const bool edit_here = edit_layer_ == int(l);
+    capture_target_ = capture_layer_ == int(l) && !edit_here;
+    GemvSegment dn = {y.wd, residual_, nullptr, D, projection_partials(F, D), 0, 0, D};
+    project(gu_, 2 * F, rows, F, kPrologueSwiGLU, nullptr, kEpilogueResidual, &dn, 1, pdl);
+    capture_target_ = false;
+    if (edit_here) {
+      check(launch_intervene(residual_, edit_direction_, &state_->position, edit_state_, D,
+                             (long long)edit_row_, rows, edit_strength_, stream_, pdl),
+            "intervene");
+      ++launches_;
+      if (capture_layer_ == int(l)) {
+        check(launch_copy_rows(residual_, capture_arena_, &state_->position, D, rows, stream_, pdl),
+              "capture copy");
+        ++launches_;
+      }
+    }
+  }
+}
+
+void Engine::lm_head_select(const bf16* last_row, bool advance, bool generating, bool pdl) {
+  const int D = int(cfg_.hidden), V = int(cfg_.vocabulary);
+  GemvArgs a = {};
+  a.x = last_row;
+  a.x_stride = D;
+  a.in_width = D;
+  a.nrows = 1;
+  a.prologue = kPrologueRmsNorm;
+  a.norm_w = final_norm_;
+  a.eps = cfg_.epsilon;
+  a.epilogue = kEpilogueArgmax;
+  a.nseg = 1;
+  a.seg[0] = {lm_head_, logits_, nullptr, V, projection_partials(D, V), 0, 0, V};
+  a.partials = partials_;
+  a.ticket = &state_->ticket;
+  a.select.result = state_->result;
+  if (generating) {
+    a.select.history = history_;
+    a.select.step = &state_->step;
+    a.select.embed = embed_;
+    a.select.residual = residual_;
+    a.select.width = D;
+    a.select.terminal = &state_->terminal;
+    a.select.stop_mask = stop_mask_;
+  }
+  if (advance) a.select.position = &state_->position;
+  a.err = &state_->err;
+  check(launch_gemv(a, 1, sms_, stream_, pdl), "lm_head");
+  ++launches_;
+}
+
+void Engine::consume_rows(const uint32_t* tokens, size_t n, bool pdl) {
+  for (size_t c0 = 0; c0 < n; c0 += max_rows_) {
+    const int rows = int(std::min(max_rows_, n - c0));
+    check(cudaMemcpyAsync(tokens_dev_, tokens + c0, rows * 4, cudaMemcpyHostToDevice, stream_), "tokens");
+    check(launch_embedding(tokens_dev_, embed_, residual_, rows, int(cfg_.hidden), stream_, false), "embed");
+    run_layers(rows, pdl);
+    check(launch_add_position(&state_->position, rows, stream_), "advance");
+    last_rows_ = rows;
+  }
+}
+
+void Engine::consume(const uint32_t* tokens, size_t n, int mode, uint16_t* logits_out) {
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  if (!n) throw std::invalid_argument("empty consume");
+  if (position() + n > capacity_) throw std::length_error("sequence exceeds KV capacity");
+  if (mode != DL_PREFILL_PARITY) throw std::invalid_argument("fast prefill not available");
+  consume_rows(tokens, n, true);
+  lm_head_select(residual_ + size_t(last_rows_ - 1) * cfg_.hidden, false, false, true);
+  if (logits_out)
+    check(cudaMemcpyAsync(logits_out, logits_, size_t(cfg_.vocabulary) * 2, cudaMemcpyDeviceToHost, stream_),
+          "logits");
+  check(cudaStreamSynchronize(stream_), "consume sync");
+  check_fault();
+}
+
+void Engine::set_capture(int layer) {
+  if (layer >= int(cfg_.layers)) throw std::invalid_argument("capture layer out of range");
+  capture_layer_ = layer;
+}
+
+void Engine::read_capture(size_t first, size_t count, uint16_t* host) {
+  if (first + count > capacity_) throw std::invalid_argument("capture range");
+  check(cudaMemcpyAsync(host, capture_arena_ + first * cfg_.hidden, count * cfg_.hidden * 2,
+                        cudaMemcpyDeviceToHost, stream_),
+        "read capture");
+  check(cudaStreamSynchronize(stream_), "read capture sync");
+}
+
+void Engine::set_intervention(int layer, size_t selected, float strength, const float* direction) {
+  if (layer >= int(cfg_.layers)) throw std::invalid_argument("intervention layer out of range");
+  edit_layer_ = layer;
+  edit_row_ = selected;
+  edit_strength_ = strength;
+  if (layer >= 0) {
+    check(cudaMemcpyAsync(edit_direction_, direction, cfg_.hidden * 4, cudaMemcpyHostToDevice, stream_),
+          "direction");
+    const uint32_t zero[2] = {0, 0};
+    check(cudaMemcpyAsync(edit_state_, zero, 8, cudaMemcpyHostToDevice, stream_), "edit state");
+    check(cudaStreamSynchronize(stream_), "intervention sync");
+  }
+}
+
+void Engine::read_kv(size_t layer, int values, size_t first, size_t count, uint16_t* host) {
+  if (layer >= layers_.size() || first + count > capacity_) throw std::invalid_argument("kv range");
+  const size_t G = size_t(cfg_.kv_heads) * cfg_.head_width;
+  const bf16* src = (values ? vcache_[layer] : kcache_[layer]) + first * G;
+  check(cudaMemcpyAsync(host, src, count * G * 2, cudaMemcpyDeviceToHost, stream_), "read kv");
+  check(cudaStreamSynchronize(stream_), "read kv sync");
+}
+
+void Engine::lm_head_logits(const bf16* last_row, bool pdl) {
+  const int D = int(cfg_.hidden), V = int(cfg_.vocabulary);
+  GemvArgs a = {};
+  a.x = last_row;
+  a.x_stride = D;
+  a.in_width = D;
+  a.nrows = 1;
+  a.prologue = kPrologueRmsNorm;
+  a.norm_w = final_norm_;
+  a.eps = cfg_.epsilon;
+  a.epilogue = kEpilogueStore;
+  a.nseg = 1;
+  a.seg[0] = {lm_head_, logits_, nullptr, V, projection_partials(D, V), 0, 0, V};
+  a.err = &state_->err;
+  check(launch_gemv(a, 1, sms_, stream_, pdl), "lm_head");
+  ++launches_;
+}
+
+// Selection after the logits of the last consumed row are in logits_.
+void Engine::select(const bf16* last_row, bool advance, bool pdl) {
+  if (mode_ == 0) {
+    lm_head_select(last_row, advance, true, pdl);
+    return;
+  }
+  lm_head_logits(last_row, pdl);
+  check(sampler_submit(sampler_, logits_, sampler_.settings, 0, true, stream_), "sampler");
+  check(sampler_feed(sampler_, history_, &state_->step, embed_, residual_, int(cfg_.hidden),
+                     advance ? &state_->position : nullptr, stream_),
+        "sampler feed");
+  launches_ += 4;
+}
+
+void Engine::decode_step(bool pdl) {
+  run_layers(1, pdl);
+  select(residual_, true, pdl);
+}
+
+void Engine::capture_decode_graph() {
+  if (decode_exec_ && graph_capture_layer_ == capture_layer_ && graph_edit_layer_ == edit_layer_ &&
+      graph_mode_ == mode_)
+    return;
+  if (decode_exec_) {
+    cudaGraphExecDestroy(decode_exec_);
+    decode_exec_ = nullptr;
+  }
+  cudaGraph_t graph = nullptr;
+  check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "begin capture");
+  launches_ = 0;
+  try {
+    decode_step(true);
+  } catch (...) {
+    cudaStreamEndCapture(stream_, &graph);
+    if (graph) cudaGraphDestroy(graph);
+    throw;
+  }
+  check(cudaStreamEndCapture(stream_, &graph), "end capture");
+  kernels_per_step_ = launches_;
+  const cudaError_t e = cudaGraphInstantiate(&decode_exec_, graph, 0);
+  cudaGraphDestroy(graph);
+  check(e, "graph instantiate");
+  graph_capture_layer_ = capture_layer_;
+  graph_edit_layer_ = edit_layer_;
+  graph_mode_ = mode_;
+}
+
+void Engine::generate(const uint32_t* prompt, size_t n_prompt, size_t max_new, const dl_sampling& s,
+                      uint64_t seed, const uint32_t* stop_ids, size_t n_stop, int prefill_mode,
+                      uint32_t* tokens_out, size_t* n_out, uint16_t* logits_out, dl_generation_stats* stats) {
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  if (!n_prompt || !max_new) throw std::invalid_argument("empty prompt or budget");
+  if (n_prompt + max_new > capacity_) throw std::length_error("sequence exceeds KV capacity");
+  validate_sampling(s, cfg_.vocabulary);
+  if (prefill_mode != DL_PREFILL_PARITY) throw std::invalid_argument("fast prefill not available");
+  for (size_t i = 0; i < n_stop; ++i)
+    if (stop_ids[i] >= cfg_.vocabulary) throw std::invalid_argument("stop ID outside vocabulary");
+  reset();
+  mode_ = s.mode;
+  if (!sampler_.arena) check(sampler_init(sampler_, cfg_.vocabulary, true), "sampler init");
+  check(sampler_start(sampler_, s, seed, stop_ids, n_stop, stream_), "sampler start");
+  stop_mask_ = sampler_.stop_mask;  // the greedy finisher latches on the same mask
+  capture_decode_graph();
+  const size_t V = cfg_.vocabulary;
+  check(cudaEventRecord(ev_[0], stream_), "event");
+  launches_ = 0;
+  consume_rows(prompt, n_prompt, true);
+  select(residual_ + size_t(last_rows_ - 1) * cfg_.hidden, false, true);
+  check(cudaEventRecord(ev_[1], stream_), "event");
+  if (logits_out) {
+    check(cudaMemcpyAsync(logits_out, logits_, V * 2, cudaMemcpyDeviceToHost, stream_), "logits");
+    for (size_t i = 1; i < max_new; ++i) {
+      check(cudaGraphLaunch(decode_exec_, stream_), "graph launch");
+      check(cudaMemcpyAsync(logits_out + i * V, logits_, V * 2, cudaMemcpyDeviceToHost, stream_), "logits");
+    }
+  } else {
+    for (size_t i = 1; i < max_new; ++i) check(cudaGraphLaunch(decode_exec_, stream_), "graph launch");
+  }
+  check(cudaEventRecord(ev_[2], stream_), "event");
+  check(cudaMemcpyAsync(tokens_out, history_, max_new * 4, cudaMemcpyDeviceToHost, stream_), "history");
+  DeviceState st;
+  check(cudaMemcpyAsync(&st, state_, sizeof(st), cudaMemcpyDeviceToHost, stream_), "state");
+  check(cudaStreamSynchronize(stream_), "generate sync");
+  float pre = 0, dec = 0;
+  check(cudaEventElapsedTime(&pre, ev_[0], ev_[1]), "elapsed");
+  check(cudaEventElapsedTime(&dec, ev_[1], ev_[2]), "elapsed");
+  // Stop at the first stop ID (inclusive) or failed selection, like the
+  // reference's device loop (src/kernels/cuda/decode.cu:161-194).
+  size_t produced = max_new;
+  {
+    std::vector<unsigned char> stop(cfg_.vocabulary, 0);
+    for (size_t i = 0; i < n_stop; ++i) stop[stop_ids[i]] = 1;
+    for (size_t i = 0; i < max_new; ++i)
+      if (stop[tokens_out[i]]) {
+        produced = i + 1;
+        break;
+      }
+  }
+  *n_out = produced;
+  if (stats) {
+    stats->prefill_ms = pre;
+    stats->decode_ms = dec;
+    stats->decode_steps = max_new - 1;
+    stats->kernels_per_decode_step = kernels_per_step_;
+    stats->kernels_total = launches_ + kernels_per_step_ * (max_new - 1);
+    stats->status = st.result[1];
+    stats->fault = st.err;
+  }
+  if (st.err) throw std::runtime_error("device fault word " + std::to_string(st.err));
+}
+
+}  // namespace dl

@@ -1,0 +1,121 @@
+// Engine: resident Qwen3 weights, contiguous KV cache, and the prefill/decode
+// loop.  Role of the reference's CachedForwardPlan (src/inference/executor.h:
+// 242-342) and DeviceSequence (src/inference/decoding/device.h:84-137) for the
+// CUDA backend: one ordered stream, device-resident position and token
+// feedback, and the per-token body captured once into a CUDA graph.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/dolittle_b200.h"
+#include "gemv.cuh"
+#include "launch.h"
+#include "sampler.h"
+
+namespace dl {
+
+struct Layer {
+  bf16 *in_norm, *wqkv, *q_norm, *k_norm, *wo, *post_norm, *wgu, *wd;
+};
+
+struct DeviceState {
+  long long position;  // absolute position of the next row to consume
+  int step;            // number of selections made
+  unsigned result[2];  // {token, status} of the last selection
+  unsigned terminal;   // stop ID or error latched
+  unsigned err;        // kernel error word
+  unsigned ticket;     // argmax completion counter
+  unsigned pad[9];
+};
+
+class Engine {
+ public:
+  Engine(const dl_model_config& cfg, int device, size_t capacity, size_t max_rows);
+  ~Engine();
+
+  static size_t tensor_count(const dl_model_config& c) { return 3 + 11 * size_t(c.layers); }
+  static bool tensor_shape(const dl_model_config& c, size_t index, size_t* rows, size_t* cols);
+
+  void init_random(uint64_t seed, float sigma);
+  void set_tensor(size_t index, const void* host, size_t bytes);
+  void get_tensor(size_t index, void* host, size_t bytes);
+  void* tensor_device(size_t index) {
+    size_t n = 0;
+    if (index >= tensor_count(cfg_)) throw std::invalid_argument("tensor index out of range");
+    return tensor_ptr(index, &n);
+  }
+  void reset();
+  void consume(const uint32_t* tokens, size_t n, int mode, uint16_t* logits_out);
+  size_t position();
+  void set_capture(int layer);
+  void read_capture(size_t first, size_t count, uint16_t* host);
+  void set_intervention(int layer, size_t selected, float strength, const float* direction);
+  void read_kv(size_t layer, int values, size_t first, size_t count, uint16_t* host);
+  void generate(const uint32_t* prompt, size_t n_prompt, size_t max_new, const dl_sampling& s,
+                uint64_t seed, const uint32_t* stop_ids, size_t n_stop, int prefill_mode,
+                uint32_t* tokens_out, size_t* n_out, uint16_t* logits_out,
+                dl_generation_stats* stats);
+
+ private:
+  bf16* tensor_ptr(size_t index, size_t* elems);
+  void consume_rows(const uint32_t* tokens, size_t n, bool pdl);
+  void run_layers(int rows, bool pdl);
+  void decode_step(bool pdl);
+  void lm_head_select(const bf16* last_row, bool advance_position, bool generating, bool pdl);
+  void lm_head_logits(const bf16* last_row, bool pdl);
+  void select(const bf16* last_row, bool advance_position, bool pdl);
+  void project(const bf16* x, int x_stride, int rows, int in_width, int prologue, const bf16* norm_w,
+               int epilogue, GemvSegment* segs, int nseg, bool pdl);
+  void capture_decode_graph();
+  void check(cudaError_t e, const char* what);
+  void check_fault();
+
+  dl_model_config cfg_;
+  int device_;
+  size_t capacity_, max_rows_;
+  int sms_;
+  cudaStream_t stream_ = nullptr;
+  // weights
+  void* weight_arena_ = nullptr;
+  size_t weight_bytes_ = 0;
+  bf16 *embed_ = nullptr, *final_norm_ = nullptr, *lm_head_ = nullptr;
+  std::vector<Layer> layers_;
+  float* inv_freq_ = nullptr;
+  // sequence
+  void* kv_arena_ = nullptr;
+  std::vector<bf16*> kcache_, vcache_;
+  // scratch
+  void* scratch_ = nullptr;
+  bf16 *residual_, *q_raw_, *k_raw_, *q_rot_, *att_, *gu_, *logits_;
+  float* scores_;
+  uint32_t* tokens_dev_;
+  uint32_t* history_;
+  size_t history_cap_;
+  uint4* partials_;
+  DeviceState* state_;
+  // capture / steering
+  int capture_layer_ = -1;
+  bf16* capture_arena_ = nullptr;
+  int edit_layer_ = -1;
+  size_t edit_row_ = 0;
+  float edit_strength_ = 0.f;
+  float* edit_direction_ = nullptr;
+  uint32_t* edit_state_ = nullptr;
+  // decode graph
+  cudaGraphExec_t decode_exec_ = nullptr;
+  int graph_capture_layer_ = -2, graph_edit_layer_ = -2;
+  size_t kernels_per_step_ = 0;
+  size_t launches_ = 0;
+  int last_rows_ = 1;
+  bool capture_target_ = false;
+  const unsigned char* stop_mask_ = nullptr;
+  int mode_ = 0, graph_mode_ = -1;
+  Sampler sampler_;
+  cudaEvent_t ev_[4] = {};
+};
+
+}  // namespace dl

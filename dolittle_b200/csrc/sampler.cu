@@ -1,0 +1,444 @@
+// Device token selection under the reference device law
+// (src/kernels/cuda/sampling.cu:106-376):
+//  * greedy: maximum value, lowest ID on ties; NaN/+inf latch status 1; no
+//    finite maximum gives status 2;
+//  * categorical: candidates in stable order (value descending, ID
+//    ascending; -0 == +0); keep = top_k or all; FP64 weights
+//    exp((v - best)/T) (0 for non-finite v); inclusive serial prefix inside
+//    fixed 256-entry tiles, serial exclusive scan of the tile totals; cutoff =
+//    first i with cum/total >= top_p; selection = first i <= cutoff with
+//    u < cum/retained; u = (word >> 11) * 2^-53;
+//  * the device-owned stream is MT19937-64 (std::mt19937_64), one word per
+//    categorical selection, latched after a stop ID or a failed selection.
+// The stable order is produced by an LSD radix sort over the 32-bit keys.  For
+// BF16 logits the low 16 key bits are a function of the sign, so sorting on
+// the high 16 bits alone gives the same order (two passes instead of four).
+#include <cstring>
+#include <stdexcept>
+#include <vector>
+
+#include "sampler.h"
+
+namespace dl {
+
+struct SamplerState {
+  uint64_t words[312];
+  unsigned index, terminal;
+  double draw;
+  unsigned previous[2];
+};
+
+namespace {
+
+constexpr unsigned kW = 256;
+constexpr unsigned kWarps = kW / 32;
+
+struct ScanState {
+  double total;
+  unsigned cutoff, selected, ticket, pad;
+};
+
+struct Layout {
+  uint2* keys_a;
+  uint2* keys_b;
+  double* prefix;
+  unsigned* counts;
+  double* tile_totals;
+  uint4* best;
+  ScanState* scan;
+  unsigned* result;
+  SamplerState* state;
+  unsigned char* stop_mask;
+};
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+Layout layout(void* arena, size_t n) {
+  const size_t blocks = (n + kW - 1) / kW;
+  auto* b = static_cast<unsigned char*>(arena);
+  size_t o = 0;
+  Layout L;
+  L.keys_a = reinterpret_cast<uint2*>(b + o); o = align_up(o + n * 8, 256);
+  L.keys_b = reinterpret_cast<uint2*>(b + o); o = align_up(o + n * 8, 256);
+  L.prefix = reinterpret_cast<double*>(b + o); o = align_up(o + n * 8, 256);
+  L.counts = reinterpret_cast<unsigned*>(b + o); o = align_up(o + blocks * kW * 4, 256);
+  L.tile_totals = reinterpret_cast<double*>(b + o); o = align_up(o + blocks * 8, 256);
+  L.best = reinterpret_cast<uint4*>(b + o); o = align_up(o + blocks * 16, 256);
+  L.scan = reinterpret_cast<ScanState*>(b + o); o = align_up(o + sizeof(ScanState), 256);
+  L.result = reinterpret_cast<unsigned*>(b + o); o = align_up(o + 8, 256);
+  L.state = reinterpret_cast<SamplerState*>(b + o); o = align_up(o + sizeof(SamplerState), 256);
+  L.stop_mask = b + o;
+  return L;
+}
+
+__device__ __forceinline__ float load_logit(const void* row, unsigned i, bool bf16_in) {
+  return bf16_in ? widen(static_cast<const bf16*>(row)[i]) : static_cast<const float*>(row)[i];
+}
+
+__device__ __forceinline__ unsigned descending_key(float v) {
+  if (v == 0.0f) v = 0.0f;
+  const unsigned bits = __float_as_uint(v);
+  const unsigned mask = (0u - (bits >> 31)) | 0x80000000u;
+  return ~(bits ^ mask);
+}
+
+// ---- MT19937-64 -----------------------------------------------------------
+__global__ void seed_kernel(SamplerState* s, uint64_t seed) {
+  s->words[0] = seed;
+  for (unsigned i = 1; i < 312; ++i) {
+    const uint64_t p = s->words[i - 1];
+    s->words[i] = 6364136223846793005ULL * (p ^ (p >> 62)) + i;
+  }
+  s->index = 312;
+  s->terminal = 0;
+  s->draw = 0;
+  s->previous[0] = s->previous[1] = 0;
+}
+
+__global__ void next_random_kernel(SamplerState* s, bool greedy) {
+  if (s->terminal || greedy) return;
+  if (s->index == 312) {
+    for (unsigned i = 0; i < 312; ++i) {
+      const uint64_t x = (s->words[i] & 0xffffffff80000000ULL) | (s->words[(i + 1) % 312] & 0x7fffffffULL);
+      s->words[i] = s->words[(i + 156) % 312] ^ (x >> 1) ^ ((x & 1) ? 0xb5026f5aa96619e9ULL : 0);
+    }
+    s->index = 0;
+  }
+  uint64_t x = s->words[s->index++];
+  x ^= (x >> 29) & 0x5555555555555555ULL;
+  x ^= (x << 17) & 0x71d67fffeda60000ULL;
+  x ^= (x << 37) & 0xfff7eee000000000ULL;
+  x ^= x >> 43;
+  s->draw = static_cast<double>(x >> 11) * 0x1.0p-53;
+}
+
+__global__ void commit_kernel(SamplerState* s, unsigned* result, const unsigned char* stops) {
+  if (s->terminal) {
+    result[0] = s->previous[0];
+    result[1] = s->previous[1];
+    return;
+  }
+  s->previous[0] = result[0];
+  s->previous[1] = result[1];
+  s->terminal = result[1] || stops[result[0]];
+}
+
+// ---- greedy ----------------------------------------------------------------
+__device__ __forceinline__ bool better(float v, unsigned id, float bv, unsigned bid) {
+  return v > bv || (v == bv && id < bid);
+}
+
+__global__ void greedy_kernel(const void* row, bool bf16_in, unsigned n, uint4* best, ScanState* scan,
+                              unsigned* result) {
+  __shared__ uint4 warp_best[kWarps];
+  __shared__ bool last;
+  const unsigned i = blockIdx.x * kW + threadIdx.x;
+  float v = -INFINITY;
+  unsigned id = 0xffffffffu, flags = 0;
+  if (i < n) {
+    v = load_logit(row, i, bf16_in);
+    if (isnan(v) || v == INFINITY) flags = 1;
+    id = i;
+    if (isnan(v)) v = -INFINITY;  // never selected; the status latch decides
+  }
+  for (int off = 16; off; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, off);
+    const unsigned oid = __shfl_xor_sync(0xffffffffu, id, off);
+    flags |= __shfl_xor_sync(0xffffffffu, flags, off);
+    if (better(ov, oid, v, id)) { v = ov; id = oid; }
+  }
+  if ((threadIdx.x & 31) == 0) warp_best[threadIdx.x >> 5] = make_uint4(__float_as_uint(v), id, flags, 0);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint4 b = warp_best[0];
+    for (unsigned w = 1; w < kWarps; ++w) {
+      const uint4 c = warp_best[w];
+      if (better(__uint_as_float(c.x), c.y, __uint_as_float(b.x), b.y)) { b.x = c.x; b.y = c.y; }
+      b.z |= c.z;
+    }
+    best[blockIdx.x] = b;
+    __threadfence();
+    last = atomicAdd(&scan->ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last || threadIdx.x != 0) return;
+  __threadfence();
+  float bv = -INFINITY;
+  unsigned bid = 0xffffffffu, fl = 0;
+  for (unsigned b = 0; b < gridDim.x; ++b) {
+    const uint4 c = __ldcg(&best[b]);
+    fl |= c.z;
+    if (better(__uint_as_float(c.x), c.y, bv, bid)) { bv = __uint_as_float(c.x); bid = c.y; }
+  }
+  scan->ticket = 0;
+  result[1] = fl ? 1u : (isfinite(bv) ? 0u : 2u);
+  result[0] = result[1] ? 0u : bid;
+}
+
+// ---- categorical -------------------------------------------------------------
+__global__ void keys_kernel(const void* row, bool bf16_in, unsigned n, uint2* keys, unsigned* result) {
+  const unsigned i = blockIdx.x * kW + threadIdx.x;
+  if (i >= n) return;
+  const float v = load_logit(row, i, bf16_in);
+  if (isnan(v) || v == INFINITY) atomicExch(&result[1], 1u);
+  keys[i] = make_uint2(descending_key(v), i);
+}
+
+// Per-block digit counts, stable ranks inside a block come from warp match.
+__device__ __forceinline__ void block_digit_ranks(unsigned digit, bool live, unsigned (*bins)[kW],
+                                                  unsigned& peers) {
+  const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (unsigned w = 0; w < kWarps; ++w) bins[w][threadIdx.x] = 0;
+  __syncthreads();
+  peers = __match_any_sync(0xffffffffu, live ? digit : 0x100u);
+  if (live && lane == unsigned(__ffs(int(peers)) - 1)) bins[warp][digit] = __popc(peers);
+  __syncthreads();
+}
+
+__global__ void histogram_kernel(const uint2* keys, unsigned n, unsigned shift, unsigned* counts) {
+  __shared__ unsigned bins[kWarps][kW];
+  const unsigned i = blockIdx.x * kW + threadIdx.x;
+  const bool live = i < n;
+  const unsigned digit = live ? (keys[i].x >> shift) & 0xffu : 0u;
+  unsigned peers;
+  block_digit_ranks(digit, live, bins, peers);
+  unsigned total = 0;
+  for (unsigned w = 0; w < kWarps; ++w) total += bins[w][threadIdx.x];
+  counts[blockIdx.x * kW + threadIdx.x] = total;
+}
+
+// Exclusive offsets in (digit, block) order.  One CTA, thread = digit.
+__global__ void digit_offsets_kernel(unsigned* counts, unsigned blocks) {
+  __shared__ unsigned totals[kW];
+  const unsigned d = threadIdx.x;
+  unsigned run = 0;
+  for (unsigned b = 0; b < blocks; ++b) {
+    const unsigned c = counts[b * kW + d];
+    counts[b * kW + d] = run;
+    run += c;
+  }
+  totals[d] = run;
+  __syncthreads();
+  // Exclusive scan of the 256 digit totals (integer: order-free).
+  unsigned v = run;
+  const unsigned lane = d & 31, warp = d >> 5;
+  for (unsigned off = 1; off < 32; off <<= 1) {
+    const unsigned o = __shfl_up_sync(0xffffffffu, v, off);
+    if (lane >= off) v += o;
+  }
+  __shared__ unsigned warp_sum[kWarps];
+  if (lane == 31) warp_sum[warp] = v;
+  __syncthreads();
+  unsigned base = 0;
+  for (unsigned w = 0; w < warp; ++w) base += warp_sum[w];
+  const unsigned exclusive = base + v - run;
+  for (unsigned b = 0; b < blocks; ++b) counts[b * kW + d] += exclusive;
+}
+
+__global__ void scatter_kernel(const uint2* in, uint2* out, unsigned n, unsigned shift, const unsigned* offsets) {
+  __shared__ unsigned bins[kWarps][kW];
+  const unsigned i = blockIdx.x * kW + threadIdx.x;
+  const bool live = i < n;
+  const uint2 k = live ? in[i] : make_uint2(0, 0);
+  const unsigned digit = (k.x >> shift) & 0xffu;
+  unsigned peers;
+  block_digit_ranks(digit, live, bins, peers);
+  if (!live) return;
+  const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned rank = __popc(peers & ((1u << lane) - 1u));
+  for (unsigned w = 0; w < warp; ++w) rank += bins[w][digit];
+  out[offsets[blockIdx.x * kW + digit] + rank] = k;
+}
+
+__global__ void weights_kernel(const void* row, bool bf16_in, const uint2* sorted, unsigned keep,
+                               double temperature, double* prefix, double* tile_totals) {
+  __shared__ double tile[kW];
+  const unsigned i = blockIdx.x * kW + threadIdx.x;
+  double w = 0.0;
+  if (i < keep) {
+    const double best = static_cast<double>(load_logit(row, sorted[0].y, bf16_in));
+    const double v = static_cast<double>(load_logit(row, sorted[i].y, bf16_in));
+    if (isfinite(v)) w = exp((v - best) / temperature);
+  }
+  tile[threadIdx.x] = w;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double sum = 0.0;
+    for (unsigned j = 0; j < kW; ++j) {
+      sum += tile[j];
+      tile[j] = sum;
+    }
+    tile_totals[blockIdx.x] = sum;
+  }
+  __syncthreads();
+  if (i < keep) prefix[i] = tile[threadIdx.x];
+}
+
+__global__ void scan_tiles_kernel(double* tile_totals, unsigned keep, ScanState* scan, unsigned* result) {
+  const unsigned tiles = (keep + kW - 1) / kW;
+  double total = 0.0;
+  for (unsigned b = 0; b < tiles; ++b) {
+    const double v = tile_totals[b];
+    tile_totals[b] = total;
+    total += v;
+  }
+  scan->total = total;
+  scan->cutoff = keep - 1;
+  scan->selected = keep - 1;
+  if (!(total > 0.0)) result[1] = 2;
+}
+
+__device__ unsigned block_min(unsigned v) {
+  __shared__ unsigned m[kWarps];
+  for (int off = 16; off; off >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, off));
+  if ((threadIdx.x & 31) == 0) m[threadIdx.x >> 5] = v;
+  __syncthreads();
+  unsigned r = m[0];
+  for (unsigned w = 1; w < kWarps; ++w) r = min(r, m[w]);
+  return r;
+}
+
+__global__ void cutoff_kernel(const double* prefix, const double* offsets, unsigned keep, double top_p,
+                              ScanState* scan) {
+  const unsigned i = blockIdx.x * kW + threadIdx.x;
+  unsigned c = 0xffffffffu;
+  if (i < keep && (offsets[blockIdx.x] + prefix[i]) / scan->total >= top_p) c = i;
+  const unsigned first = block_min(c);
+  if (threadIdx.x == 0 && first != 0xffffffffu) atomicMin(&scan->cutoff, first);
+}
+
+__global__ void select_kernel(const double* prefix, const double* offsets, unsigned keep, double draw,
+                              const SamplerState* state, ScanState* scan) {
+  const unsigned i = blockIdx.x * kW + threadIdx.x;
+  const unsigned last = scan->cutoff;
+  const double retained = offsets[last / kW] + prefix[last];
+  const double u = state ? state->draw : draw;
+  unsigned c = 0xffffffffu;
+  if (i <= last && i < keep && u < (offsets[blockIdx.x] + prefix[i]) / retained) c = i;
+  const unsigned first = block_min(c);
+  if (threadIdx.x == 0 && first != 0xffffffffu) atomicMin(&scan->selected, first);
+}
+
+__global__ void finish_kernel(const uint2* sorted, const ScanState* scan, unsigned* result) {
+  if (!result[1]) result[0] = sorted[min(scan->selected, scan->cutoff)].y;
+}
+
+__global__ void feed_kernel(const unsigned* result, unsigned* history, int* step, const bf16* embed,
+                            bf16* residual, int width, long long* position) {
+  const unsigned token = result[0];
+  if (threadIdx.x == 0) {
+    if (history) history[step ? *step : 0] = token;
+  }
+  if (embed) {
+    const bf16* src = embed + size_t(token) * width;
+    for (int f = threadIdx.x; f < width; f += blockDim.x) residual[f] = src[f];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (step) ++*step;
+    if (position) ++*position;
+  }
+}
+
+}  // namespace
+
+void validate_sampling(const dl_sampling& s, size_t vocabulary) {
+  const bool finite_t = s.temperature == s.temperature && s.temperature < 1e308 && s.temperature > -1e308;
+  const bool finite_p = s.top_p == s.top_p && s.top_p < 1e308 && s.top_p > -1e308;
+  if ((s.mode != 0 && s.mode != 1) || !finite_t || s.temperature <= 0 || !finite_p || s.top_p <= 0 ||
+      s.top_p > 1 || (s.mode == 0 && (s.temperature != 1 || s.top_k != 0 || s.top_p != 1)) ||
+      s.top_k > vocabulary)
+    throw std::invalid_argument("invalid sampling settings");
+}
+
+size_t sampler_required_bytes(size_t n) {
+  const size_t blocks = (n + kW - 1) / kW;
+  size_t o = 0;
+  o = align_up(o + n * 8, 256);
+  o = align_up(o + n * 8, 256);
+  o = align_up(o + n * 8, 256);
+  o = align_up(o + blocks * kW * 4, 256);
+  o = align_up(o + blocks * 8, 256);
+  o = align_up(o + blocks * 16, 256);
+  o = align_up(o + sizeof(ScanState), 256);
+  o = align_up(o + 8, 256);
+  o = align_up(o + sizeof(SamplerState), 256);
+  return o + n;
+}
+
+cudaError_t sampler_init(Sampler& s, size_t vocabulary, bool bf16_input) {
+  s.vocabulary = vocabulary;
+  s.bf16_input = bf16_input;
+  cudaError_t e = cudaMalloc(&s.arena, sampler_required_bytes(vocabulary));
+  if (e != cudaSuccess) return e;
+  e = cudaMemset(s.arena, 0, sampler_required_bytes(vocabulary));
+  const Layout L = layout(s.arena, vocabulary);
+  s.state = L.state;
+  s.result = L.result;
+  s.stop_mask = L.stop_mask;
+  return e;
+}
+
+void sampler_free(Sampler& s) {
+  if (s.arena) cudaFree(s.arena);
+  s.arena = nullptr;
+}
+
+cudaError_t sampler_start(Sampler& s, const dl_sampling& settings, uint64_t seed, const uint32_t* stop_ids,
+                          size_t n_stop, cudaStream_t stream) {
+  std::vector<unsigned char> mask(s.vocabulary, 0);
+  for (size_t i = 0; i < n_stop; ++i) mask[stop_ids[i]] = 1;
+  cudaError_t e = cudaMemcpyAsync(s.stop_mask, mask.data(), mask.size(), cudaMemcpyHostToDevice, stream);
+  if (e != cudaSuccess) return e;
+  e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return e;
+  seed_kernel<<<1, 1, 0, stream>>>(s.state, seed);
+  s.settings = settings;
+  s.started = true;
+  return cudaGetLastError();
+}
+
+cudaError_t sampler_submit(Sampler& s, const void* row, const dl_sampling& st, uint64_t bits, bool owned,
+                           cudaStream_t stream) {
+  const Layout L = layout(s.arena, s.vocabulary);
+  const unsigned n = unsigned(s.vocabulary), blocks = (n + kW - 1) / kW;
+  cudaError_t e = cudaMemsetAsync(L.result, 0, 8, stream);
+  if (e != cudaSuccess) return e;
+  const bool greedy = st.mode == 0;
+  if (owned) next_random_kernel<<<1, 1, 0, stream>>>(L.state, greedy);
+  if (greedy) {
+    greedy_kernel<<<blocks, kW, 0, stream>>>(row, s.bf16_input, n, L.best, L.scan, L.result);
+  } else {
+    keys_kernel<<<blocks, kW, 0, stream>>>(row, s.bf16_input, n, L.keys_a, L.result);
+    uint2* in = L.keys_a;
+    uint2* out = L.keys_b;
+    for (unsigned shift = s.bf16_input ? 16 : 0; shift < 32; shift += 8) {
+      histogram_kernel<<<blocks, kW, 0, stream>>>(in, n, shift, L.counts);
+      digit_offsets_kernel<<<1, kW, 0, stream>>>(L.counts, blocks);
+      scatter_kernel<<<blocks, kW, 0, stream>>>(in, out, n, shift, L.counts);
+      uint2* t = in;
+      in = out;
+      out = t;
+    }
+    const unsigned keep = st.top_k ? unsigned(st.top_k) : n;
+    const unsigned kept_blocks = (keep + kW - 1) / kW;
+    weights_kernel<<<kept_blocks, kW, 0, stream>>>(row, s.bf16_input, in, keep, st.temperature, L.prefix,
+                                                   L.tile_totals);
+    scan_tiles_kernel<<<1, 1, 0, stream>>>(L.tile_totals, keep, L.scan, L.result);
+    cutoff_kernel<<<kept_blocks, kW, 0, stream>>>(L.prefix, L.tile_totals, keep, st.top_p, L.scan);
+    const double draw = static_cast<double>(bits >> 11) * 0x1.0p-53;
+    select_kernel<<<kept_blocks, kW, 0, stream>>>(L.prefix, L.tile_totals, keep, draw, owned ? L.state : nullptr,
+                                                  L.scan);
+    finish_kernel<<<1, 1, 0, stream>>>(in, L.scan, L.result);
+  }
+  if (owned) commit_kernel<<<1, 1, 0, stream>>>(L.state, L.result, L.stop_mask);
+  return cudaGetLastError();
+}
+
+cudaError_t sampler_feed(Sampler& s, unsigned* history, int* step, const bf16* embed, bf16* residual, int width,
+                         long long* position, cudaStream_t stream) {
+  feed_kernel<<<1, 256, 0, stream>>>(s.result, history, step, embed, residual, width, position);
+  return cudaGetLastError();
+}
+
+}  // namespace dl

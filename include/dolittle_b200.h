@@ -1,0 +1,234 @@
+/*
+ * dolittle_b200.h -- C ABI of the B200 (sm_100a) Qwen3 token loop.
+ *
+ * Plain pointers and sizes only.  Device pointers are CUDA device addresses
+ * on the current device; `stream` is a cudaStream_t passed as void* (NULL =
+ * legacy default stream).  Every launch entry point only enqueues work: no
+ * allocation, transfer or host wait (the contract of the reference's
+ * src/kernels/cuda/launch.h:1-60), and is graph-capturable.  Errors are
+ * returned as dl_status; dl_last_error() gives a message for the calling
+ * thread.  BF16 tensors are raw 16-bit storage (uint16_t bits).
+ *
+ * Reference interfaces replaced (paths inside plainsight-systems/dolittle):
+ *   dl_projection ........ launch_projection       src/kernels/cuda/launch.h:79-83
+ *   dl_rms_norm .......... launch_rms_norm         src/kernels/cuda/launch.h:84-86
+ *   dl_rotary ............ launch_rotary           src/kernels/cuda/launch.h:87-92
+ *   dl_attention_scale ... launch_attention_scale  src/kernels/cuda/launch.h:93-94
+ *   dl_attention ......... launch_attention        src/kernels/cuda/launch.h:95-101
+ *   dl_embedding ......... launch_embedding        src/kernels/cuda/launch.h:102-104
+ *   dl_add ............... launch_add              src/kernels/cuda/launch.h:105-106
+ *   dl_silu_multiply ..... launch_silu_multiply    src/kernels/cuda/launch.h:107-109
+ *   dl_sampler_* ......... DeviceCategorical       src/inference/sampling/device.h:54-85
+ *   dl_intervene ......... DeviceIntervention      src/inference/steering/device.h:30-68
+ *                          (kernel src/kernels/cuda/steering.cu:106-159)
+ *   dl_normalize_injection DeviceInjection         src/inference/injection/device.h:26-47
+ *                          (kernel src/kernels/cuda/injection.cu:48-102)
+ *   dl_engine_* .......... CachedForwardPlan       src/inference/executor.h:242-342
+ *                          (prepare_device_generation/start_sequence/
+ *                           collect_sequence/consume_view) and generate()
+ *                          src/inference/generation.h:129-138
+ * Fused entry points (new Operation variants the Qwen3 recipe may emit):
+ *   dl_qkv_projection, dl_qk_norm_rope_append, dl_projection_residual.
+ */
+#ifndef DOLITTLE_B200_H
+#define DOLITTLE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define DL_API __attribute__((visibility("default")))
+#else
+#define DL_API
+#endif
+
+typedef enum {
+  DL_OK = 0,
+  DL_INVALID_ARGUMENT = 1,  /* reference: std::invalid_argument */
+  DL_UNSUPPORTED = 2,       /* unsupported dtype/shape (reference: invalid_argument) */
+  DL_CUDA_ERROR = 3,        /* launch or runtime error (reference: runtime_error) */
+  DL_OUT_OF_MEMORY = 4,     /* reference: length_error on budget */
+  DL_DEVICE_FAULT = 5       /* a kernel recorded a bounded-wait timeout */
+} dl_status;
+
+typedef enum { DL_BF16 = 0, DL_F32 = 1 } dl_dtype;
+
+DL_API const char* dl_last_error(void);
+DL_API const char* dl_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* Operation launches (reference launch.h mirrors).  The product computes in */
+/* BF16 storage with FP32 arithmetic; DL_F32 is rejected with DL_UNSUPPORTED.*/
+/* Positions: device_position (size_t on device) overrides first_position.  */
+/* ------------------------------------------------------------------------ */
+
+/* Y[rows][O] = X[rows][I] * W[O][I]^T under the reference projection law.
+ * output_position (device, optional): output rows start at row
+ * *output_position of Y (KV-cache append). I must be a multiple of 8. */
+DL_API dl_status dl_projection(dl_dtype type, const void* input, const void* weight, void* output,
+                               size_t rows, size_t input_width, size_t output_width, void* stream,
+                               const size_t* output_position);
+DL_API dl_status dl_rms_norm(dl_dtype type, const void* input, const void* weight, void* output,
+                             size_t rows, size_t width, float epsilon, void* stream);
+DL_API dl_status dl_rotary(dl_dtype type, const void* input, void* output, size_t positions,
+                           size_t heads, size_t width, size_t first_position, double theta,
+                           void* stream, const size_t* device_position, int positioned_output);
+DL_API dl_status dl_attention_scale(float* output, size_t width, void* stream);
+/* Causal GQA attention; query row i attends keys [0, first+i].  workspace:
+ * dl_attention_workspace_bytes() bytes of device memory (scores), declared
+ * at preparation time like the reference's PreparedOperation::workspace(). */
+DL_API size_t dl_attention_workspace_bytes(size_t positions, size_t query_heads, size_t capacity);
+DL_API dl_status dl_attention(dl_dtype type, const void* query, const void* key, const void* value,
+                              void* output, size_t positions, size_t query_heads, size_t kv_heads,
+                              size_t width, void* stream, size_t first_position,
+                              const size_t* device_position, size_t capacity, const float* scale,
+                              void* workspace);
+DL_API dl_status dl_embedding(dl_dtype type, const uint32_t* tokens, const void* weight,
+                              void* output, size_t rows, size_t width, void* stream);
+DL_API dl_status dl_add(dl_dtype type, const void* left, const void* right, void* output,
+                        size_t count, void* stream);
+DL_API dl_status dl_silu_multiply(dl_dtype type, const void* gate, const void* up, void* output,
+                                  size_t count, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Fused decode operations (same arithmetic as the unfused recipe).          */
+/* ------------------------------------------------------------------------ */
+
+/* normalized = RMSNorm(residual, norm_weight); q/k/v = projections of it.
+ * wqkv = [Wq; Wk; Wv] contiguous ([q_rows + 2*kv_rows][I]).  v rows are
+ * written at row *v_position of v_out (KV append) when v_position != NULL. */
+DL_API dl_status dl_qkv_projection(const void* residual, const void* norm_weight, float epsilon,
+                                   const void* wqkv, size_t rows, size_t input_width,
+                                   size_t q_rows, size_t kv_rows, void* q_out, void* k_out,
+                                   void* v_out, const int64_t* v_position, void* stream);
+/* QK-norm + RoPE for rows at positions *position + i; queries to q_out,
+ * keys into k_cache row (*position + i).  inv_freq from dl_rope_inverse_frequency. */
+DL_API dl_status dl_rope_inverse_frequency(float* output, size_t width, double theta,
+                                           void* stream);
+DL_API dl_status dl_qk_norm_rope_append(const void* q_raw, const void* k_raw,
+                                        const void* q_norm_weight, const void* k_norm_weight,
+                                        const float* inv_freq, void* q_out, void* k_cache,
+                                        const int64_t* position, size_t rows, size_t query_heads,
+                                        size_t kv_heads, size_t width, float epsilon,
+                                        void* stream);
+/* residual = round(residual + round(X W^T)) in place. */
+DL_API dl_status dl_projection_residual(const void* input, const void* weight, void* residual,
+                                        size_t rows, size_t input_width, size_t output_width,
+                                        void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Device sampler (DeviceCategorical).  Greedy or categorical with          */
+/* temperature / top-k / top-p under the reference device law; the draw is */
+/* explicit bits or the device-owned MT19937-64 stream.                     */
+/* ------------------------------------------------------------------------ */
+typedef struct dl_sampler dl_sampler;
+typedef struct {
+  int32_t mode;        /* 0 greedy, 1 categorical */
+  double temperature;
+  size_t top_k;        /* 0 disables */
+  double top_p;
+} dl_sampling;
+
+DL_API size_t dl_sampler_required_bytes(size_t vocabulary);
+DL_API dl_status dl_sampler_create(size_t vocabulary, dl_dtype type, dl_sampler** out);
+DL_API void dl_sampler_destroy(dl_sampler* s);
+/* Seed the device MT19937-64 stream and the stop-ID mask. */
+DL_API dl_status dl_sampler_start(dl_sampler* s, const dl_sampling* settings, uint64_t seed,
+                                  const uint32_t* stop_ids, size_t n_stop, void* stream);
+/* One selection of a device logits row; result = device {token, status}. */
+DL_API dl_status dl_sampler_submit(dl_sampler* s, const void* row, const dl_sampling* settings,
+                                   uint64_t bits, void* stream, const uint32_t** result);
+DL_API dl_status dl_sampler_submit_next(dl_sampler* s, const void* row, void* stream,
+                                        const uint32_t** result);
+
+/* ------------------------------------------------------------------------ */
+/* Steering and injection                                                    */
+/* ------------------------------------------------------------------------ */
+/* At absolute row `selected` (if *position <= selected < *position+rows):
+ * beta = strength*||h||, h' = round(h + beta*direction); state = {invalid,
+ * count} in device memory. */
+DL_API dl_status dl_intervene(void* residual, const float* direction, const int64_t* position,
+                              uint32_t* state, size_t width, size_t selected, size_t rows,
+                              float strength, void* stream);
+/* out = BF16((h/||h||)*scale); norm and status written to device memory. */
+DL_API dl_status dl_normalize_injection(const void* source, void* output, float* norm,
+                                        uint32_t* status, size_t width, float scale,
+                                        void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Engine: resident Qwen3 weights + KV cache + prefill/decode loop.          */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+  uint32_t hidden, query_heads, kv_heads, head_width, mlp_width, vocabulary, layers;
+  float epsilon;
+  double theta;
+} dl_model_config;
+
+typedef struct dl_engine dl_engine;
+
+typedef struct {
+  double prefill_ms;     /* device time of the prompt pass + first selection */
+  double decode_ms;      /* device time of all decode steps */
+  uint64_t decode_steps; /* single-token forward passes */
+  uint64_t kernels_per_decode_step;
+  uint64_t kernels_total; /* kernels this library launched for the call */
+  uint32_t status;       /* last selection status (0 ok) */
+  uint32_t fault;        /* kernel error word (bounded waits) */
+} dl_generation_stats;
+
+enum { DL_PREFILL_PARITY = 0, DL_PREFILL_FAST = 1 };
+
+/* Tensors are addressed by index: 0 embedding [V][D], 1 final norm [D],
+ * 2 lm_head [V][D], then 3 + 11*block + role with roles input_norm, q, k,
+ * v, q_norm, k_norm, o, post_norm, gate, up, down (Qwen3 recipe order,
+ * src/models/qwen3/model.cpp:343-409). */
+DL_API size_t dl_engine_tensor_count(const dl_model_config* config);
+DL_API dl_status dl_engine_tensor_shape(const dl_model_config* config, size_t index, size_t* rows,
+                                        size_t* cols);
+DL_API dl_status dl_engine_create(const dl_model_config* config, int device, size_t capacity,
+                                  size_t max_rows, dl_engine** out);
+DL_API void dl_engine_destroy(dl_engine* e);
+/* Seeded synthetic weights: N(0, sigma) approximation (Philox4x32-10,
+ * Irwin-Hall of 8 halves) per tensor, norms = 1. */
+DL_API dl_status dl_engine_init_random(dl_engine* e, uint64_t seed, float sigma);
+DL_API dl_status dl_engine_set_tensor(dl_engine* e, size_t index, const void* host_bits,
+                                      size_t bytes);
+DL_API dl_status dl_engine_get_tensor(dl_engine* e, size_t index, void* host_bits, size_t bytes);
+/* Device address of a resident tensor (for binding it into other kernels,
+ * like the reference executor binds parameter regions). */
+DL_API dl_status dl_engine_tensor_device(dl_engine* e, size_t index, void** device_ptr);
+/* Fresh sequence: position 0, empty KV cache contents unchanged. */
+DL_API dl_status dl_engine_reset(dl_engine* e);
+/* Consume prompt/continuation tokens (host IDs) at the current position;
+ * logits_out (host, optional) receives the BF16 logits of the last row.
+ * mode: DL_PREFILL_PARITY (reference reduction order) or DL_PREFILL_FAST. */
+DL_API dl_status dl_engine_consume(dl_engine* e, const uint32_t* tokens, size_t n, int mode,
+                                   uint16_t* logits_out);
+DL_API size_t dl_engine_position(dl_engine* e);
+/* Capture block `layer`'s output rows for every consumed position into an
+ * arena [capacity][D] (layer < 0 disables). */
+DL_API dl_status dl_engine_set_capture(dl_engine* e, int layer);
+DL_API dl_status dl_engine_read_capture(dl_engine* e, size_t first, size_t count, uint16_t* host);
+/* One-shot steering edit at block `layer`, absolute row `selected`. */
+DL_API dl_status dl_engine_set_intervention(dl_engine* e, int layer, size_t selected,
+                                            float strength, const float* host_direction);
+DL_API dl_status dl_engine_read_kv(dl_engine* e, size_t layer, int values, size_t first,
+                                   size_t count, uint16_t* host);
+/* Live generation: prompt pass, first selection, then decode steps replayed
+ * from one captured CUDA graph per step until max_new tokens or a stop ID.
+ * tokens_out receives the generated IDs (host); logits_out (optional, host,
+ * [max_new][V]) the BF16 logits each selection read. */
+DL_API dl_status dl_engine_generate(dl_engine* e, const uint32_t* prompt, size_t n_prompt,
+                                    size_t max_new, const dl_sampling* settings, uint64_t seed,
+                                    const uint32_t* stop_ids, size_t n_stop, int prefill_mode,
+                                    uint32_t* tokens_out, size_t* n_out, uint16_t* logits_out,
+                                    dl_generation_stats* stats);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DOLITTLE_B200_H */
