@@ -216,7 +216,8 @@ def dominant_kernel_roofline(engine, cfg, hbm, kind):
     stream = torch.cuda.Stream()
     x = torch.randn(D, device="cuda").to(torch.bfloat16)
     y = torch.empty(2 * F, device="cuda", dtype=torch.bfloat16)
-    ptrs = [engine.tensor_device(3 + 11 * l + 8) for l in range(cfg.layers)]
+    # Block l's resident gate|up matrix: [2F][D], gate and up rows interleaved.
+    ptrs = [engine.tensor_device(3 + 11 * l + 8)[0] for l in range(cfg.layers)]
     L = dl.lib()
     with torch.cuda.stream(stream):
         for p in ptrs[:4]:
@@ -332,6 +333,34 @@ def run_ours(args):
     return 0
 
 
+def run_profile_case(args):
+    """Small standalone cases for ncu captures (a few hundred MB on device).
+
+    gemv: the decode GEMV on one gate|up-shaped matrix (24576 x 4096, 201 MB,
+    larger than L2), launched 4 times.  decode: a 36-block engine with a
+    16-token prompt and 3 decode passes (one prefill chunk, then graphs)."""
+    import torch
+    import dolittle_b200 as dl
+    torch.cuda.set_device(0)
+    if args.profile == "gemv":
+        D, O = 4096, 24576
+        w = (torch.randn(O, D, device="cuda") * 0.02).to(torch.bfloat16)
+        x = torch.randn(D, device="cuda").to(torch.bfloat16)
+        y = torch.empty(O, device="cuda", dtype=torch.bfloat16)
+        for _ in range(4):
+            assert dl.lib().dl_projection(dl.DL_BF16, x.data_ptr(), w.data_ptr(), y.data_ptr(), 1, D, O, None,
+                                          None) == 0
+        torch.cuda.synchronize()
+        print("profile gemv ok")
+    else:
+        cfg = dl.QWEN3_8B
+        e = dl.Engine(cfg, capacity=64, max_rows=16)
+        e.init_random(SEED, 0.02)
+        g = e.generate(prompt_ids(cfg.vocabulary)[:16], 4)
+        print("profile decode ok", g.tokens, g.kernels_per_decode_step)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -339,7 +368,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", choices=["gemv", "decode"], default=None,
+                    help="run a small case for an ncu capture instead of the benchmark")
     args = ap.parse_args()
+    if args.profile:
+        return run_profile_case(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

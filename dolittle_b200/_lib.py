@@ -77,7 +77,7 @@ SIGNATURES = {
     "dl_engine_init_random": (C.c_int, [vp, C.c_uint64, C.c_float]),
     "dl_engine_set_tensor": (C.c_int, [vp, sz, vp, sz]),
     "dl_engine_get_tensor": (C.c_int, [vp, sz, vp, sz]),
-    "dl_engine_tensor_device": (C.c_int, [vp, sz, C.POINTER(vp)]),
+    "dl_engine_tensor_device": (C.c_int, [vp, sz, C.POINTER(vp), C.POINTER(sz)]),
     "dl_engine_reset": (C.c_int, [vp]),
     "dl_engine_consume": (C.c_int, [vp, u32p, sz, C.c_int, u16p]),
     "dl_engine_position": (sz, [vp]),

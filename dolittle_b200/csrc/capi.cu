@@ -97,7 +97,7 @@ DL_API dl_status dl_rms_norm(dl_dtype type, const void* input, const void* weigh
                              size_t rows, size_t width, float epsilon, void* stream) {
   if (type != DL_BF16) return fail(DL_UNSUPPORTED, "rms_norm: only BF16 storage is supported");
   if (!input || !weight || !output || !rows || !width) return fail(DL_INVALID_ARGUMENT, "rms_norm: arguments");
-  if (width > 8192) return fail(DL_UNSUPPORTED, "rms_norm: width above 8192");
+  if (width > 32768) return fail(DL_UNSUPPORTED, "rms_norm: width above 32768");
   return cuda_status(dl::launch_rms_norm(static_cast<const bf16*>(input), static_cast<const bf16*>(weight),
                                          static_cast<bf16*>(output), rows, int(width), epsilon, st(stream)),
                      "rms_norm");
@@ -203,10 +203,11 @@ DL_API dl_status dl_qkv_projection(const void* residual, const void* norm_weight
   a.eps = epsilon;
   a.epilogue = dl::kEpilogueStore;
   a.nseg = 3;
-  a.seg[0] = {w, static_cast<bf16*>(q_out), nullptr, Qr, dl::projection_partials(I, Qr), 0, 0, Qr};
-  a.seg[1] = {w + size_t(Qr) * I, static_cast<bf16*>(k_out), nullptr, Kr, dl::projection_partials(I, Kr), 0, 0, Kr};
-  a.seg[2] = {w + size_t(Qr + Kr) * I, static_cast<bf16*>(v_out), reinterpret_cast<const long long*>(v_position),
-              Kr, dl::projection_partials(I, Kr), 0, 0, Kr};
+  a.seg[0] = dl::make_segment(w, static_cast<bf16*>(q_out), nullptr, Qr, dl::projection_partials(I, Qr), Qr);
+  a.seg[1] = dl::make_segment(w + size_t(Qr) * I, static_cast<bf16*>(k_out), nullptr, Kr,
+                              dl::projection_partials(I, Kr), Kr);
+  a.seg[2] = dl::make_segment(w + size_t(Qr + Kr) * I, static_cast<bf16*>(v_out),
+                              reinterpret_cast<const long long*>(v_position), Kr, dl::projection_partials(I, Kr), Kr);
   return cuda_status(dl::launch_gemv(a, dl::gemv_rows_template(int(rows), I), sms, st(stream), false),
                      "qkv_projection");
 }
@@ -253,8 +254,9 @@ DL_API dl_status dl_projection_residual(const void* input, const void* weight, v
     a.prologue = dl::kProloguePlain;
     a.epilogue = dl::kEpilogueResidual;
     a.nseg = 1;
-    a.seg[0] = {static_cast<const bf16*>(weight), static_cast<bf16*>(residual) + g0 * output_width, nullptr,
-                int(output_width), dl::projection_partials(input_width, output_width), 0, 0, int(output_width)};
+    a.seg[0] = dl::make_segment(static_cast<const bf16*>(weight), static_cast<bf16*>(residual) + g0 * output_width,
+                                nullptr, int(output_width), dl::projection_partials(input_width, output_width),
+                                int(output_width));
     const dl_status s = cuda_status(dl::launch_gemv(a, rt, sms, st(stream), false), "projection_residual");
     if (s != DL_OK) return s;
   }
@@ -383,9 +385,9 @@ DL_API dl_status dl_engine_set_tensor(dl_engine* e, size_t index, const void* ho
 DL_API dl_status dl_engine_get_tensor(dl_engine* e, size_t index, void* host_bits, size_t bytes) {
   DL_ENGINE_CALL(e->impl->get_tensor(index, host_bits, bytes));
 }
-DL_API dl_status dl_engine_tensor_device(dl_engine* e, size_t index, void** device_ptr) {
+DL_API dl_status dl_engine_tensor_device(dl_engine* e, size_t index, void** device_ptr, size_t* row_stride) {
   if (!device_ptr) return fail(DL_INVALID_ARGUMENT, "tensor_device: null output");
-  DL_ENGINE_CALL(*device_ptr = e->impl->tensor_device(index));
+  DL_ENGINE_CALL(*device_ptr = e->impl->tensor_device(index, row_stride));
 }
 DL_API dl_status dl_engine_reset(dl_engine* e) { DL_ENGINE_CALL(e->impl->reset()); }
 DL_API dl_status dl_engine_consume(dl_engine* e, const uint32_t* tokens, size_t n, int mode, uint16_t* logits_out) {

@@ -1,6 +1,7 @@
 // Engine implementation (see engine.h).
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <stdexcept>
 #include <string>
@@ -164,29 +165,36 @@ Engine::~Engine() {
   if (stream_) cudaStreamDestroy(stream_);
 }
 
-bf16* Engine::tensor_ptr(size_t index, size_t* elems) {
+// Resident layout of each logical tensor.  Gate and up rows are interleaved
+// in one [2F][D] matrix (row 2o = gate o, row 2o+1 = up o) so one CTA holds
+// both halves of every SwiGLU pair; every other tensor is contiguous.
+TensorView Engine::view(size_t index) {
+  if (index >= tensor_count(cfg_)) throw std::invalid_argument("tensor index out of range");
   const Shape sh = shape_of(cfg_, index);
-  *elems = sh.rows * sh.cols;
-  if (index == 0) return embed_;
-  if (index == 1) return final_norm_;
-  if (index == 2) return lm_head_;
-  const size_t l = (index - 3) / 11, role = (index - 3) % 11;
-  const size_t D = cfg_.hidden, Q = size_t(cfg_.query_heads) * cfg_.head_width,
-               G = size_t(cfg_.kv_heads) * cfg_.head_width, F = cfg_.mlp_width;
-  const Layer& y = layers_[l];
-  switch (role) {
-    case 0: return y.in_norm;
-    case 1: return y.wqkv;
-    case 2: return y.wqkv + Q * D;
-    case 3: return y.wqkv + (Q + G) * D;
-    case 4: return y.q_norm;
-    case 5: return y.k_norm;
-    case 6: return y.wo;
-    case 7: return y.post_norm;
-    case 8: return y.wgu;
-    case 9: return y.wgu + F * D;
-    default: return y.wd;
+  TensorView v{nullptr, sh.rows, sh.cols, sh.cols};
+  if (index == 0) v.ptr = embed_;
+  else if (index == 1) v.ptr = final_norm_;
+  else if (index == 2) v.ptr = lm_head_;
+  else {
+    const size_t l = (index - 3) / 11, role = (index - 3) % 11;
+    const size_t D = cfg_.hidden, Q = size_t(cfg_.query_heads) * cfg_.head_width,
+                 G = size_t(cfg_.kv_heads) * cfg_.head_width;
+    const Layer& y = layers_[l];
+    switch (role) {
+      case 0: v.ptr = y.in_norm; break;
+      case 1: v.ptr = y.wqkv; break;
+      case 2: v.ptr = y.wqkv + Q * D; break;
+      case 3: v.ptr = y.wqkv + (Q + G) * D; break;
+      case 4: v.ptr = y.q_norm; break;
+      case 5: v.ptr = y.k_norm; break;
+      case 6: v.ptr = y.wo; break;
+      case 7: v.ptr = y.post_norm; break;
+      case 8: v.ptr = y.wgu; v.row_stride = 2 * D; break;
+      case 9: v.ptr = y.wgu + D; v.row_stride = 2 * D; break;
+      default: v.ptr = y.wd; break;
+    }
   }
+  return v;
 }
 
 void Engine::init_random(uint64_t seed, float sigma) {
@@ -194,32 +202,31 @@ void Engine::init_random(uint64_t seed, float sigma) {
   const double sd = std::sqrt(8.0 * (65536.0 * 65536.0 - 1.0) / 12.0);
   const float scale = static_cast<float>(double(sigma) / sd);
   for (size_t i = 0; i < tensor_count(cfg_); ++i) {
-    size_t n = 0;
-    bf16* p = tensor_ptr(i, &n);
-    const Shape sh = shape_of(cfg_, i);
-    if (sh.rows == 1)
-      check(launch_fill_const(p, n, 1.0f, stream_), "fill norm");
+    const TensorView v = view(i);
+    if (v.rows == 1)
+      check(launch_fill_const(v.ptr, v.cols, 1.0f, stream_), "fill norm");
     else
-      check(launch_fill_normal(p, n, seed, uint32_t(i), scale, stream_), "fill normal");
+      check(launch_fill_normal(v.ptr, v.rows, v.cols, v.row_stride, seed, uint32_t(i), scale, stream_),
+            "fill normal");
   }
   check(cudaStreamSynchronize(stream_), "init_random sync");
 }
 
 void Engine::set_tensor(size_t index, const void* host, size_t bytes) {
-  size_t n = 0;
-  if (index >= tensor_count(cfg_)) throw std::invalid_argument("tensor index out of range");
-  bf16* p = tensor_ptr(index, &n);
-  if (bytes != n * 2) throw std::invalid_argument("tensor byte size mismatch");
-  check(cudaMemcpyAsync(p, host, bytes, cudaMemcpyHostToDevice, stream_), "set_tensor");
+  const TensorView v = view(index);
+  if (bytes != v.rows * v.cols * 2) throw std::invalid_argument("tensor byte size mismatch");
+  check(cudaMemcpy2DAsync(v.ptr, v.row_stride * 2, host, v.cols * 2, v.cols * 2, v.rows, cudaMemcpyHostToDevice,
+                          stream_),
+        "set_tensor");
   check(cudaStreamSynchronize(stream_), "set_tensor sync");
 }
 
 void Engine::get_tensor(size_t index, void* host, size_t bytes) {
-  size_t n = 0;
-  if (index >= tensor_count(cfg_)) throw std::invalid_argument("tensor index out of range");
-  bf16* p = tensor_ptr(index, &n);
-  if (bytes != n * 2) throw std::invalid_argument("tensor byte size mismatch");
-  check(cudaMemcpyAsync(host, p, bytes, cudaMemcpyDeviceToHost, stream_), "get_tensor");
+  const TensorView v = view(index);
+  if (bytes != v.rows * v.cols * 2) throw std::invalid_argument("tensor byte size mismatch");
+  check(cudaMemcpy2DAsync(host, v.cols * 2, v.ptr, v.row_stride * 2, v.cols * 2, v.rows, cudaMemcpyDeviceToHost,
+                          stream_),
+        "get_tensor");
   check(cudaStreamSynchronize(stream_), "get_tensor sync");
 }
 
@@ -286,10 +293,10 @@ void Engine::run_layers(int rows, bool pdl) {
   const int score_ctas = rows == 1 ? std::clamp((cap + 63) / 64, 1, 16) : std::clamp((cap + 255) / 256, 1, 8);
   for (size_t l = 0; l < layers_.size(); ++l) {
     const Layer& y = layers_[l];
-    GemvSegment qkv[3] = {};
-    qkv[0] = {y.wqkv, q_raw_, nullptr, Q, projection_partials(D, Q), 0, 0, Q};
-    qkv[1] = {y.wqkv + size_t(Q) * D, k_raw_, nullptr, G, projection_partials(D, G), 0, 0, G};
-    qkv[2] = {y.wqkv + size_t(Q + G) * D, vcache_[l], &state_->position, G, projection_partials(D, G), 0, 0, G};
+    GemvSegment qkv[3];
+    qkv[0] = make_segment(y.wqkv, q_raw_, nullptr, Q, projection_partials(D, Q), Q);
+    qkv[1] = make_segment(y.wqkv + size_t(Q) * D, k_raw_, nullptr, G, projection_partials(D, G), G);
+    qkv[2] = make_segment(y.wqkv + size_t(Q + G) * D, vcache_[l], &state_->position, G, projection_partials(D, G), G);
     capture_target_ = false;
     project(residual_, D, rows, D, kPrologueRmsNorm, y.in_norm, kEpilogueStore, qkv, 3, pdl);
     check(launch_qk_norm_rope(q_raw_, k_raw_, y.q_norm, y.k_norm, inv_freq_, q_rot_, kcache_[l], pos, rows,
@@ -301,14 +308,15 @@ void Engine::run_layers(int rows, bool pdl) {
     check(launch_attention_pv(scores_, vcache_[l], att_, pos, rows, H, Hk, d, cap, stream_, pdl),
           "attention pv");
     launches_ += 3;
-    GemvSegment o = {y.wo, residual_, nullptr, D, projection_partials(Q, D), 0, 0, D};
+    GemvSegment o = make_segment(y.wo, residual_, nullptr, D, projection_partials(Q, D), D);
     project(att_, Q, rows, Q, kProloguePlain, nullptr, kEpilogueResidual, &o, 1, pdl);
-    GemvSegment gu = {y.wgu, gu_, nullptr, 2 * F, projection_partials(D, F), 0, 0, 2 * F};
-    project(residual_, D, rows, D, kPrologueRmsNorm, y.post_norm, kEpilogueStore, &gu, 1, pdl);
+    // Interleaved gate|up rows; the epilogue writes the SwiGLU activation.
+    GemvSegment gu = make_segment(y.wgu, gu_, nullptr, 2 * F, projection_partials(D, F), F);
+    project(residual_, D, rows, D, kPrologueRmsNorm, y.post_norm, kEpilogueSwiGLU, &gu, 1, pdl);
     const bool edit_here = edit_layer_ == int(l);
     capture_target_ = capture_layer_ == int(l) && !edit_here;
-    GemvSegment dn = {y.wd, residual_, nullptr, D, projection_partials(F, D), 0, 0, D};
-    project(gu_, 2 * F, rows, F, kPrologueSwiGLU, nullptr, kEpilogueResidual, &dn, 1, pdl);
+    GemvSegment dn = make_segment(y.wd, residual_, nullptr, D, projection_partials(F, D), D);
+    project(gu_, F, rows, F, kProloguePlain, nullptr, kEpilogueResidual, &dn, 1, pdl);
     capture_target_ = false;
     if (edit_here) {
       check(launch_intervene(residual_, edit_direction_, &state_->position, edit_state_, D,
@@ -336,7 +344,7 @@ void Engine::lm_head_select(const bf16* last_row, bool advance, bool generating,
   a.eps = cfg_.epsilon;
   a.epilogue = kEpilogueArgmax;
   a.nseg = 1;
-  a.seg[0] = {lm_head_, logits_, nullptr, V, projection_partials(D, V), 0, 0, V};
+  a.seg[0] = make_segment(lm_head_, logits_, nullptr, V, projection_partials(D, V), V);
   a.partials = partials_;
   a.ticket = &state_->ticket;
   a.select.result = state_->result;
@@ -427,7 +435,7 @@ void Engine::lm_head_logits(const bf16* last_row, bool pdl) {
   a.eps = cfg_.epsilon;
   a.epilogue = kEpilogueStore;
   a.nseg = 1;
-  a.seg[0] = {lm_head_, logits_, nullptr, V, projection_partials(D, V), 0, 0, V};
+  a.seg[0] = make_segment(lm_head_, logits_, nullptr, V, projection_partials(D, V), V);
   a.err = &state_->err;
   check(launch_gemv(a, 1, sms_, stream_, pdl), "lm_head");
   ++launches_;
@@ -502,14 +510,26 @@ void Engine::generate(const uint32_t* prompt, size_t n_prompt, size_t max_new, c
   consume_rows(prompt, n_prompt, true);
   select(residual_ + size_t(last_rows_ - 1) * cfg_.hidden, false, true);
   check(cudaEventRecord(ev_[1], stream_), "event");
+  // DOLITTLE_DECODE_GRAPH=0 launches the same per-token kernels eagerly
+  // instead of replaying the captured graph (for per-kernel profilers).
+  static const bool use_graph = [] {
+    const char* v = std::getenv("DOLITTLE_DECODE_GRAPH");
+    return !(v && v[0] == '0');
+  }();
+  auto step = [&] {
+    if (use_graph)
+      check(cudaGraphLaunch(decode_exec_, stream_), "graph launch");
+    else
+      decode_step(true);
+  };
   if (logits_out) {
     check(cudaMemcpyAsync(logits_out, logits_, V * 2, cudaMemcpyDeviceToHost, stream_), "logits");
     for (size_t i = 1; i < max_new; ++i) {
-      check(cudaGraphLaunch(decode_exec_, stream_), "graph launch");
+      step();
       check(cudaMemcpyAsync(logits_out + i * V, logits_, V * 2, cudaMemcpyDeviceToHost, stream_), "logits");
     }
   } else {
-    for (size_t i = 1; i < max_new; ++i) check(cudaGraphLaunch(decode_exec_, stream_), "graph launch");
+    for (size_t i = 1; i < max_new; ++i) step();
   }
   check(cudaEventRecord(ev_[2], stream_), "event");
   check(cudaMemcpyAsync(tokens_out, history_, max_new * 4, cudaMemcpyDeviceToHost, stream_), "history");

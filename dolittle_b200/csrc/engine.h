@@ -22,6 +22,11 @@ struct Layer {
   bf16 *in_norm, *wqkv, *q_norm, *k_norm, *wo, *post_norm, *wgu, *wd;
 };
 
+struct TensorView {
+  bf16* ptr;
+  size_t rows, cols, row_stride;  // elements
+};
+
 struct DeviceState {
   long long position;  // absolute position of the next row to consume
   int step;            // number of selections made
@@ -43,10 +48,12 @@ class Engine {
   void init_random(uint64_t seed, float sigma);
   void set_tensor(size_t index, const void* host, size_t bytes);
   void get_tensor(size_t index, void* host, size_t bytes);
-  void* tensor_device(size_t index) {
-    size_t n = 0;
-    if (index >= tensor_count(cfg_)) throw std::invalid_argument("tensor index out of range");
-    return tensor_ptr(index, &n);
+  // Device address of a resident tensor; gate/up live interleaved (strided)
+  // and are reported through their row stride.
+  void* tensor_device(size_t index, size_t* row_stride) {
+    const TensorView v = view(index);
+    if (row_stride) *row_stride = v.row_stride;
+    return v.ptr;
   }
   void reset();
   void consume(const uint32_t* tokens, size_t n, int mode, uint16_t* logits_out);
@@ -61,7 +68,7 @@ class Engine {
                 dl_generation_stats* stats);
 
  private:
-  bf16* tensor_ptr(size_t index, size_t* elems);
+  TensorView view(size_t index);
   void consume_rows(const uint32_t* tokens, size_t n, bool pdl);
   void run_layers(int rows, bool pdl);
   void decode_step(bool pdl);

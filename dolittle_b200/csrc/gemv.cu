@@ -1,6 +1,10 @@
 // Streaming GEMV kernel (see gemv.cuh for the law and the B200 mapping).
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
+#include <mutex>
 
 #include "gemv.cuh"
 #include "launch.h"
@@ -8,8 +12,10 @@
 namespace dl {
 namespace {
 
-// Lane layout inside a warp: a quarter-warp (8 lanes) holds 8 different rows
-// with the same slot, so padded shared rows give conflict-free LDS.128.
+// Lane layout inside a warp: a quarter-warp (8 lanes) holds 8 consecutive
+// rows with the same slot, so the 8 swizzle phases (or the 16-byte row
+// padding) give conflict-free LDS.128.  Rows 2k and 2k+1 sit in lanes l and
+// l^1 (used by the SwiGLU epilogue).
 template <int P>
 struct Layout {
   static constexpr int kSlots = P / 8;                 // threads per row
@@ -26,16 +32,10 @@ template <int P>
 __device__ __forceinline__ float reduce_partials(float (&acc)[8]) {
   if constexpr (P == 32) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float other = __shfl_xor_sync(0xffffffffu, acc[i], 16);
-      acc[i] = __fadd_rn(acc[i], other);   // p[j] + p[j+16] (slots 0,1)
-    }
+    for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], __shfl_xor_sync(0xffffffffu, acc[i], 16));
   }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float other = __shfl_xor_sync(0xffffffffu, acc[i], 8);
-    acc[i] = __fadd_rn(acc[i], other);     // p[j] + p[j+8] (slot 0)
-  }
+  for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], __shfl_xor_sync(0xffffffffu, acc[i], 8));
 #pragma unroll
   for (int i = 0; i < 4; ++i) acc[i] = __fadd_rn(acc[i], acc[i + 4]);
 #pragma unroll
@@ -43,23 +43,40 @@ __device__ __forceinline__ float reduce_partials(float (&acc)[8]) {
   return __fadd_rn(acc[0], acc[1]);
 }
 
-// RMSNorm inverse of one global BF16 row by one warp (reference law).
-__device__ float rms_inverse_global(const bf16* x, int width, float eps) {
-  const unsigned lane = threadIdx.x & 31u;
-  float sum;
+// acc[0] += x.lo * w.lo, acc[1] += x.hi * w.hi: one rounding each (the
+// product of two BF16 values is exact in FP32).
+__device__ __forceinline__ void fma_pair(float& a0, float& a1, uint32_t x2, uint32_t w2) {
+  asm("{\n\t.reg .b16 xl, xh, wl, wh;\n\t"
+      "mov.b32 {xl, xh}, %2;\n\t"
+      "mov.b32 {wl, wh}, %3;\n\t"
+      "fma.rn.f32.bf16 %0, xl, wl, %0;\n\t"
+      "fma.rn.f32.bf16 %1, xh, wh, %1;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "r"(x2), "r"(w2));
+}
+
+__device__ __forceinline__ void fma8(float (&acc)[8], const uint4& x, const uint4& w) {
+  fma_pair(acc[0], acc[1], x.x, w.x);
+  fma_pair(acc[2], acc[3], x.y, w.y);
+  fma_pair(acc[4], acc[5], x.z, w.z);
+  fma_pair(acc[6], acc[7], x.w, w.w);
+}
+
+// RMSNorm inverse of one BF16 row held in shared memory, by one warp, with
+// the reference law (normalization.cu:82-186, by width).
+__device__ float rms_inverse_smem(const bf16* x, int width, float eps) {
+  const int lane = threadIdx.x & 31;
+  float part[4] = {0.f, 0.f, 0.f, 0.f};
   if (width <= 128) {
-    float part[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (unsigned c = 0; c < 4; ++c) {
-      const unsigned col = lane + 32u * c;
-      if (col < static_cast<unsigned>(width)) {
+    for (int c = 0; c < 4; ++c) {
+      const int col = lane + 32 * c;
+      if (col < width) {
         const float v = widen(x[col]);
         part[c] = __fmul_rn(v, v);
       }
     }
-    sum = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), part[2]), part[3]);
   } else {
-    float part[4] = {0.f, 0.f, 0.f, 0.f};
     for (int base = 4 * lane; base < width; base += 128) {
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -69,16 +86,15 @@ __device__ float rms_inverse_global(const bf16* x, int width, float eps) {
         }
       }
     }
-    sum = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), part[2]), part[3]);
   }
+  float sum = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), part[2]), part[3]);
   sum = shuffle_down_tree32(sum);
   const float total = __shfl_sync(0xffffffffu, sum, 0);
   const float mean = __fmul_rn(total, 1.0f / static_cast<float>(width));
   return rsqrtf(__fadd_rn(mean, eps));
 }
 
-// SwiGLU law (reference elementwise.cu:62-87 with Silu): gate and up are
-// BF16 values; the activation is rounded to storage before the product.
+// SwiGLU law (reference elementwise.cu:62-87 with Silu) on BF16 gate/up.
 __device__ __forceinline__ float swiglu(float a, float b) {
   const float e = expf(a >= 0.0f ? -a : a);
   const float s = a >= 0.0f ? 1.0f / (1.0f + e) : e / (1.0f + e);
@@ -89,28 +105,76 @@ __device__ __forceinline__ bool better(float v, unsigned id, float bv, unsigned 
   return v > bv || (v == bv && id < bid);
 }
 
-template <int ROWS>
-struct XStore {
-  // ROWS == 1: FP32 row; ROWS > 1: BF16 rows.
-  static constexpr bool kF32 = ROWS == 1;
-  __device__ static size_t bytes(int width) {
-    return kF32 ? size_t(width) * 4 : size_t(width) * 2 * ROWS;
-  }
-};
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
 
-template <int ROWS, int P>
+__host__ __device__ __forceinline__ size_t x_bytes(int rows_template, int width) {
+  return (size_t(width) * 2 * rows_template + 127) / 128 * 128;
+}
+
+// One full tensor-map stage: KC features of this thread's row.
+template <int ROWS, int P, int KC>
+__device__ __forceinline__ void stage_map(const unsigned char* stage, int box_bytes, int row, int slot,
+                                          const bf16* xs, int I, int k0, float (&acc)[ROWS][8]) {
+  const unsigned char* rbase = stage + row * 128;
+  const int swz = row & 7;
+#pragma unroll
+  for (int m = 0; m < KC / P; ++m) {
+    const int b = (P * m) >> 6;                              // box (compile-time)
+    const int c = (((P * m) & 63) >> 3) + slot;              // chunk within the 128-byte row
+    const uint4 w = lds128(rbase + b * box_bytes + ((c ^ swz) << 4));
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+      const uint4 xv = lds128(xs + size_t(r) * I + k0 + P * m + 8 * slot);
+      fma8(acc[r], xv, w);
+    }
+  }
+}
+
+// Generic stage (ragged tail or padded-row layout): guarded per 8 features.
+template <int ROWS, int P, bool MAP>
+__device__ __forceinline__ void stage_generic(const unsigned char* stage, int box_bytes, int row_stride,
+                                              int row, int slot, const bf16* xs, int I, int k0, int kc,
+                                              int nfeat, float (&acc)[ROWS][8]) {
+  for (int m = 0; m < kc / P; ++m) {
+    const int f = P * m + 8 * slot;
+    if (f >= nfeat) continue;
+    const unsigned char* wp;
+    if constexpr (MAP) {
+      const int c = (f & 63) >> 3;
+      wp = stage + (f >> 6) * box_bytes + row * 128 + ((c ^ (row & 7)) << 4);
+    } else {
+      wp = stage + row * row_stride + 2 * f;
+    }
+    const uint4 w = lds128(wp);
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+      const uint4 xv = lds128(xs + size_t(r) * I + k0 + f);
+      fma8(acc[r], xv, w);
+    }
+  }
+}
+
+template <int ROWS, int P, bool MAP, int KC>
 __device__ void consume(const GemvArgs& a, const GemvSegment& sg, int r0, int r1, int ntiles,
-                        int tile_rows, unsigned char* ring, int stage_bytes, int row_stride,
-                        uint64_t* full, uint64_t* empty, const void* xs, uint4* cta_best,
+                        unsigned char* ring, uint64_t* full, uint64_t* empty, const bf16* xs, uint4* cta_best,
                         bool& failed) {
   using L = Layout<P>;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int slot = L::slot(lane);
   const int my_row = L::row(warp, lane);
   const int I = a.in_width;
-  const int kc = a.kc;
+  const int kc = MAP ? KC : a.kc;
   const int nk = (I + kc - 1) / kc;
   const int padded = (I + 15) / 16 * 16;
+  const int tile_rows = sg.tile_rows;
+  const int box_bytes = ((tile_rows + 7) / 8) * 8 * 128;
   float best_v = -INFINITY;
   unsigned best_id = 0xffffffffu, flags = 0;
   int g = 0;
@@ -132,38 +196,11 @@ __device__ void consume(const GemvArgs& a, const GemvSegment& sg, int r0, int r1
       if (active && !failed) {
         const int k0 = ks * kc;
         const int nfeat = min(kc, I - k0);
-        const unsigned char* wrow = ring + st * stage_bytes + my_row * row_stride;
-#pragma unroll 4
-        for (int m = 0; m < kc / P; ++m) {
-          const int f = P * m + 8 * slot;          // feature offset inside stage
-          if (f < nfeat) {
-            const uint4 w = lds128(wrow + 2 * f);
-            const float w0 = bf_lo(w.x), w1 = bf_hi(w.x), w2 = bf_lo(w.y), w3 = bf_hi(w.y);
-            const float w4 = bf_lo(w.z), w5 = bf_hi(w.z), w6 = bf_lo(w.w), w7 = bf_hi(w.w);
-#pragma unroll
-            for (int r = 0; r < ROWS; ++r) {
-              float x0, x1, x2, x3, x4, x5, x6, x7;
-              if constexpr (ROWS == 1) {
-                const float* xf = static_cast<const float*>(xs) + k0 + f;
-                const float4 xa = lds128f(xf), xb = lds128f(xf + 4);
-                x0 = xa.x; x1 = xa.y; x2 = xa.z; x3 = xa.w;
-                x4 = xb.x; x5 = xb.y; x6 = xb.z; x7 = xb.w;
-              } else {
-                const uint4 xv = lds128(static_cast<const bf16*>(xs) + size_t(r) * I + k0 + f);
-                x0 = bf_lo(xv.x); x1 = bf_hi(xv.x); x2 = bf_lo(xv.y); x3 = bf_hi(xv.y);
-                x4 = bf_lo(xv.z); x5 = bf_hi(xv.z); x6 = bf_lo(xv.w); x7 = bf_hi(xv.w);
-              }
-              acc[r][0] = __fmaf_rn(x0, w0, acc[r][0]);
-              acc[r][1] = __fmaf_rn(x1, w1, acc[r][1]);
-              acc[r][2] = __fmaf_rn(x2, w2, acc[r][2]);
-              acc[r][3] = __fmaf_rn(x3, w3, acc[r][3]);
-              acc[r][4] = __fmaf_rn(x4, w4, acc[r][4]);
-              acc[r][5] = __fmaf_rn(x5, w5, acc[r][5]);
-              acc[r][6] = __fmaf_rn(x6, w6, acc[r][6]);
-              acc[r][7] = __fmaf_rn(x7, w7, acc[r][7]);
-            }
-          }
-        }
+        const unsigned char* stage = ring + st * a.stage_bytes;
+        if (MAP && nfeat == KC)
+          stage_map<ROWS, P, KC>(stage, box_bytes, my_row, slot, xs, I, k0, acc);
+        else
+          stage_generic<ROWS, P, MAP>(stage, box_bytes, a.row_stride, my_row, slot, xs, I, k0, kc, nfeat, acc);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
@@ -183,31 +220,37 @@ __device__ void consume(const GemvArgs& a, const GemvSegment& sg, int r0, int r1
 #pragma unroll
     for (int r = 0; r < ROWS; ++r) {
       const float y = reduce_partials<P>(acc[r]);
+      const int row = tr0 + my_row;
+      if (a.epilogue == kEpilogueSwiGLU) {
+        // Even row = gate o, odd row = up o; both rounded to storage first.
+        const float partner = __shfl_xor_sync(0xffffffffu, y, 1);
+        if (!active || slot != 0 || failed || r >= a.nrows || (row & 1)) continue;
+        const float act = swiglu(round_bf16(y), round_bf16(partner));
+        sg.out[size_t(r) * sg.out_stride + (row >> 1)] = narrow(act);
+        continue;
+      }
       if (!active || slot != 0 || failed || r >= a.nrows) continue;
-      const int o = tr0 + my_row;
       const bf16 yb = narrow(y);
       bf16* out = sg.out + (sg.out_row ? size_t(*sg.out_row) * sg.out_stride : 0);
-      const size_t idx = size_t(r) * sg.out_stride + o;
+      const size_t idx = size_t(r) * sg.out_stride + row;
       if (a.epilogue == kEpilogueResidual) {
         const bf16 nv = narrow(__fadd_rn(widen(out[idx]), widen(yb)));
         out[idx] = nv;
-        if (a.capture)
-          a.capture[(size_t(*a.capture_row) + r) * a.capture_stride + o] = nv;
+        if (a.capture) a.capture[(size_t(*a.capture_row) + r) * a.capture_stride + row] = nv;
       } else {
         out[idx] = yb;
         if (a.epilogue == kEpilogueArgmax) {
           const float v = widen(yb);
           if (isnan(v) || v == INFINITY) flags |= 1u;
-          if (better(v, static_cast<unsigned>(o), best_v, best_id)) {
+          if (better(v, static_cast<unsigned>(row), best_v, best_id)) {
             best_v = v;
-            best_id = static_cast<unsigned>(o);
+            best_id = static_cast<unsigned>(row);
           }
         }
       }
     }
   }
   if (a.epilogue == kEpilogueArgmax) {
-    // Warp then CTA reduction of (value, lowest id); flags OR.
 #pragma unroll
     for (int off = 16; off; off >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, best_v, off);
@@ -223,34 +266,57 @@ __device__ void consume(const GemvArgs& a, const GemvSegment& sg, int r0, int r1
 }
 
 template <int ROWS>
+__device__ void consume_dispatch(const GemvArgs& a, const GemvSegment& sg, int r0, int r1, int ntiles,
+                                 unsigned char* ring, uint64_t* full, uint64_t* empty, const bf16* xs,
+                                 uint4* cta_best, bool& failed) {
+  const int P = sg.partials;
+  if (a.use_map) {
+    if (a.kc == 256) {
+      if (P == 16)
+        consume<ROWS, 16, true, 256>(a, sg, r0, r1, ntiles, ring, full, empty, xs, cta_best, failed);
+      else
+        consume<ROWS, 32, true, 256>(a, sg, r0, r1, ntiles, ring, full, empty, xs, cta_best, failed);
+    } else {
+      if (P == 16)
+        consume<ROWS, 16, true, 128>(a, sg, r0, r1, ntiles, ring, full, empty, xs, cta_best, failed);
+      else
+        consume<ROWS, 32, true, 128>(a, sg, r0, r1, ntiles, ring, full, empty, xs, cta_best, failed);
+    }
+  } else {
+    if (P == 16)
+      consume<ROWS, 16, false, 0>(a, sg, r0, r1, ntiles, ring, full, empty, xs, cta_best, failed);
+    else
+      consume<ROWS, 32, false, 0>(a, sg, r0, r1, ntiles, ring, full, empty, xs, cta_best, failed);
+  }
+}
+
+template <int ROWS>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_constant__ GemvArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ uint4 cta_best[kGemvConsumers / 32];
+  __shared__ float row_inv[8];
   __shared__ bool last_cta;
+  __shared__ unsigned chosen;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + a.stages;
-  unsigned char* xs = smem + 256;
-  const size_t xbytes = (XStore<ROWS>::bytes(a.in_width) + 127) / 128 * 128;
-  unsigned char* ring = xs + xbytes;
+  bf16* xs = reinterpret_cast<bf16*>(smem + 256);
+  const size_t xb = x_bytes(ROWS, a.in_width);
+  unsigned char* xend = smem + 256 + xb;
+  // The swizzled boxes need 1024-byte alignment of every stage.
+  const uint32_t ring_s = (smem_addr(xend) + 1023u) & ~1023u;
+  unsigned char* ring = xend + (ring_s - smem_addr(xend));
 
-  // Segment and row range of this CTA.
   int si = 0;
   for (int i = 1; i < a.nseg; ++i)
     if (static_cast<int>(blockIdx.x) >= a.seg[i].cta_begin) si = i;
   const GemvSegment& sg = a.seg[si];
-  const int P = sg.partials;
   const int local = blockIdx.x - sg.cta_begin;
-  const int per = (sg.rows + sg.cta_count - 1) / sg.cta_count;
-  const int r0 = min(sg.rows, local * per), r1 = min(sg.rows, r0 + per);
-  const int max_rows = kGemvConsumers / (P / 8);
-  const int ntiles = r1 > r0 ? (r1 - r0 + max_rows - 1) / max_rows : 0;
-  const int tile_rows = ntiles ? (r1 - r0 + ntiles - 1) / ntiles : 0;
+  const int r0 = min(sg.rows, local * sg.rows_per_cta), r1 = min(sg.rows, r0 + sg.rows_per_cta);
+  const int tile_rows = sg.tile_rows;
+  const int ntiles = r1 > r0 ? (r1 - r0 + tile_rows - 1) / tile_rows : 0;
   const int I = a.in_width;
   const int kc = a.kc;
   const int nk = (I + kc - 1) / kc;
-  const int row_stride = 2 * kc + 16;
-  const int stage_bytes = a.max_tile_rows * row_stride;
-  const int total = ntiles * nk;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < a.stages; ++s) {
@@ -267,75 +333,63 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     // ---------------- producer warp: stream this CTA's weight slab ----------
     const int lane = threadIdx.x & 31;
     const uint64_t policy = evict_first_policy();
-    bool failed = false;
+    const int box_bytes = ((tile_rows + 7) / 8) * 8 * 128;
     int g = 0;
-    for (int t = 0; t < ntiles && !failed; ++t) {
+    for (int t = 0; t < ntiles; ++t) {
       const int tr0 = r0 + t * tile_rows;
       const int trows = min(tile_rows, r1 - tr0);
       for (int ks = 0; ks < nk; ++ks, ++g) {
         const int st = g % a.stages;
         if (g >= a.stages && !mbar_wait(&empty[st], ((g / a.stages) - 1) & 1)) {
-          failed = true;
           record_error(a.err, kErrWaitEmpty);
-          break;
+          return;
         }
         const int k0 = ks * kc;
-        const unsigned bytes = 2u * min(kc, I - k0);
-        if (lane == 0) mbar_arrive_expect_tx(&full[st], bytes * trows);
-        __syncwarp();
-        unsigned char* dst = ring + st * stage_bytes;
-        for (int r = lane; r < trows; r += 32)
-          bulk_g2s(dst + r * row_stride, sg.w + size_t(tr0 + r) * I + k0, bytes, &full[st], policy);
+        const int nfeat = min(kc, I - k0);
+        unsigned char* dst = ring + st * a.stage_bytes;
+        if (a.use_map) {
+          const int nbox = (nfeat + kGemvBox - 1) / kGemvBox;
+          if (lane == 0) mbar_arrive_expect_tx(&full[st], unsigned(nbox) * tile_rows * 128u);
+          __syncwarp();
+          if (lane < nbox) tma_load_2d(dst + lane * box_bytes, &sg.map, k0 + lane * kGemvBox, tr0, &full[st], policy);
+        } else {
+          const unsigned bytes = 2u * nfeat;
+          if (lane == 0) mbar_arrive_expect_tx(&full[st], bytes * trows);
+          __syncwarp();
+          for (int r = lane; r < trows; r += 32)
+            bulk_g2s(dst + r * a.row_stride, sg.w + size_t(tr0 + r) * I + k0, bytes, &full[st], policy);
+        }
       }
     }
-    (void)total;
     return;
   }
 
-  // ---------------- consumers: build x, then stream-multiply -----------------
+  // ---------------- consumers: build x (BF16 rows in smem), then multiply ----
   wait_prior();
   const int nrows = a.nrows;
-  if (a.prologue == kPrologueRmsNorm) {
-    for (int r = warp; r < nrows; r += kGemvConsumers / 32) {
-      const bf16* xr = a.x + size_t(r) * a.x_stride;
-      const float inv = rms_inverse_global(xr, I, a.eps);
-      for (int f = threadIdx.x & 31; f < I; f += 32) {
-        const float v = round_bf16(__fmul_rn(round_bf16(__fmul_rn(widen(xr[f]), inv)), widen(a.norm_w[f])));
-        if constexpr (ROWS == 1)
-          reinterpret_cast<float*>(xs)[f] = v;
-        else
-          reinterpret_cast<bf16*>(xs)[size_t(r) * I + f] = narrow(v);
-      }
+  {
+    // Cooperative 16-byte copies of the input rows.
+    const int v8 = I / 8;
+    for (int idx = threadIdx.x; idx < nrows * v8; idx += kGemvConsumers) {
+      const int r = idx / v8, q = idx % v8;
+      reinterpret_cast<uint4*>(xs + size_t(r) * I)[q] = reinterpret_cast<const uint4*>(a.x + size_t(r) * a.x_stride)[q];
     }
-  } else {
-    for (int idx = threadIdx.x; idx < nrows * I; idx += kGemvConsumers) {
-      const int r = idx / I, f = idx % I;
-      const bf16* xr = a.x + size_t(r) * a.x_stride;
-      float v;
-      if (a.prologue == kPrologueSwiGLU)
-        v = swiglu(widen(xr[f]), widen(xr[I + f]));
-      else
-        v = widen(xr[f]);
-      if constexpr (ROWS == 1)
-        reinterpret_cast<float*>(xs)[f] = v;
-      else
-        reinterpret_cast<bf16*>(xs)[size_t(r) * I + f] = narrow(v);
-    }
-  }
-  if constexpr (ROWS > 1) {
-    // Zero the unused rows so the loop can run all ROWS.
-    for (int idx = nrows * I + threadIdx.x; idx < ROWS * I; idx += kGemvConsumers)
-      reinterpret_cast<bf16*>(xs)[idx] = narrow(0.0f);
+    for (int idx = nrows * I + threadIdx.x; idx < ROWS * I; idx += kGemvConsumers) xs[idx] = narrow(0.0f);
   }
   named_sync(1, kGemvConsumers);
+  if (a.prologue == kPrologueRmsNorm) {
+    if (warp < nrows) row_inv[warp] = rms_inverse_smem(xs + size_t(warp) * I, I, a.eps);
+    named_sync(1, kGemvConsumers);
+    for (int idx = threadIdx.x; idx < nrows * I; idx += kGemvConsumers) {
+      const int r = idx / I, f = idx % I;
+      const float v = __fmul_rn(round_bf16(__fmul_rn(widen(xs[idx]), row_inv[r])), widen(a.norm_w[f]));
+      xs[idx] = narrow(v);
+    }
+    named_sync(1, kGemvConsumers);
+  }
 
   bool failed = false;
-  if (P == 16)
-    consume<ROWS, 16>(a, sg, r0, r1, ntiles, tile_rows, ring, stage_bytes, row_stride, full, empty,
-                      xs, cta_best, failed);
-  else
-    consume<ROWS, 32>(a, sg, r0, r1, ntiles, tile_rows, ring, stage_bytes, row_stride, full, empty,
-                      xs, cta_best, failed);
+  consume_dispatch<ROWS>(a, sg, r0, r1, ntiles, ring, full, empty, xs, cta_best, failed);
 
   if (a.epilogue != kEpilogueArgmax) return;
   named_sync(1, kGemvConsumers);
@@ -371,7 +425,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
   }
   if (lane == 0) cta_best[warp] = make_uint4(__float_as_uint(bv), bid, fl, 0);
   named_sync(1, kGemvConsumers);
-  __shared__ unsigned chosen;
   if (threadIdx.x == 0) {
     uint4 b = cta_best[0];
     for (int w = 1; w < kGemvConsumers / 32; ++w) {
@@ -402,42 +455,103 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
   }
 }
 
-}  // namespace
-
-size_t gemv_smem_bytes(int rows, int in_width, int kc, int stages, int max_tile_rows) {
-  const size_t x = rows == 1 ? size_t(in_width) * 4 : size_t(in_width) * 2 * rows;
-  return 256 + (x + 127) / 128 * 128 + size_t(stages) * max_tile_rows * (2 * kc + 16);
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
 }
 
-// Plan + launch.  Segments get CTAs in proportion to their bytes.
+bool encode_weight_map(CUtensorMap* map, const void* w, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {uint32_t(kGemvBox), box_rows};
+  cuuint32_t es[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(w), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Tuning overrides (features per stage, ring depth) read once from
+// DOLITTLE_GEMV_KC / DOLITTLE_GEMV_STAGES.
+struct GemvTuning {
+  int kc = 0, stages = 16;
+  GemvTuning() {
+    if (const char* v = std::getenv("DOLITTLE_GEMV_KC")) kc = std::atoi(v) >= 256 ? 256 : 128;
+    if (const char* v = std::getenv("DOLITTLE_GEMV_STAGES")) stages = std::max(2, std::min(16, std::atoi(v)));
+  }
+};
+const GemvTuning& tuning() {
+  static GemvTuning t;
+  return t;
+}
+
+}  // namespace
+
+size_t gemv_smem_bytes(int rows, int in_width, int stage_bytes, int stages) {
+  return 256 + x_bytes(rows, in_width) + 1024 + size_t(stages) * stage_bytes;
+}
+
+// Plan + launch.  Segments get CTAs in proportion to their bytes; each
+// segment's rows are split evenly over its CTAs (even counts for the SwiGLU
+// pairing) and into tiles of at most 256/(P/8) rows (the consumer threads).
 cudaError_t launch_gemv(GemvArgs a, int rows_template, int grid, cudaStream_t stream, bool pdl) {
   const int I = a.in_width;
+  if (I % 8) return cudaErrorInvalidValue;
+  const GemvTuning& tune = tuning();
+  const bool pairs = a.epilogue == kEpilogueSwiGLU;
   long long total_bytes = 0;
   for (int i = 0; i < a.nseg; ++i) total_bytes += (long long)a.seg[i].rows * I;
   int assigned = 0;
-  int max_tile_rows = 1;
+  a.use_map = I >= kGemvBox ? 1 : 0;
+  int max_box_rows = 0;
   for (int i = 0; i < a.nseg; ++i) {
-    int c = a.nseg == 1 ? grid
-                        : std::max(1, (int)std::llround((double)grid * a.seg[i].rows * I / total_bytes));
+    GemvSegment& s = a.seg[i];
+    if (pairs && s.rows % 2) return cudaErrorInvalidValue;
+    int c = a.nseg == 1 ? grid : std::max(1, (int)std::llround((double)grid * s.rows * I / total_bytes));
     if (i == a.nseg - 1) c = std::max(1, grid - assigned);
-    c = std::min(c, a.seg[i].rows);
-    a.seg[i].cta_begin = assigned;
-    a.seg[i].cta_count = c;
+    c = std::min(c, s.rows);
+    int per = (s.rows + c - 1) / c;
+    if (pairs) per += per & 1;
+    c = (s.rows + per - 1) / per;
+    s.cta_begin = assigned;
+    s.cta_count = c;
+    s.rows_per_cta = per;
     assigned += c;
-    const int per = (a.seg[i].rows + c - 1) / c;
-    const int maxr = kGemvConsumers / (a.seg[i].partials / 8);
+    const int maxr = kGemvConsumers / (s.partials / 8);
     const int nt = (per + maxr - 1) / maxr;
-    max_tile_rows = std::max(max_tile_rows, (per + nt - 1) / nt);
+    s.tile_rows = (per + nt - 1) / nt;
+    if (pairs) s.tile_rows += s.tile_rows & 1;
+    max_box_rows = std::max(max_box_rows, ((s.tile_rows + 7) / 8) * 8);
   }
-  a.max_tile_rows = max_tile_rows;
-  const size_t xbytes = rows_template == 1 ? size_t(I) * 4 : size_t(I) * 2 * rows_template;
-  a.kc = max_tile_rows <= 32 ? 256 : 128;
-  if (a.kc > ((I + 31) / 32) * 32) a.kc = ((I + 31) / 32) * 32;
-  const size_t stage = size_t(max_tile_rows) * (2 * a.kc + 16);
-  const size_t avail = kGemvSmemBudget - 256 - (xbytes + 127) / 128 * 128;
-  a.stages = (int)std::min<size_t>(16, avail / stage);
+  if (a.use_map) {
+    a.kc = tune.kc ? tune.kc : (4 * max_box_rows * 128 <= 40 * 1024 ? 256 : 128);
+    for (int i = 0; i < a.nseg; ++i)
+      if (!encode_weight_map(&a.seg[i].map, a.seg[i].w, uint64_t(a.seg[i].rows), uint64_t(I),
+                             uint32_t(a.seg[i].tile_rows)))
+        return cudaErrorInvalidValue;
+    a.stage_bytes = (a.kc / kGemvBox) * max_box_rows * 128;
+  } else {
+    a.kc = ((I + 31) / 32) * 32;
+    a.row_stride = 2 * a.kc + 16;
+    int maxt = 0;
+    for (int i = 0; i < a.nseg; ++i) maxt = std::max(maxt, a.seg[i].tile_rows);
+    a.stage_bytes = maxt * a.row_stride;
+  }
+  const size_t fixed = gemv_smem_bytes(rows_template, I, 0, 0);
+  if (kGemvSmemBudget <= fixed) return cudaErrorInvalidValue;
+  a.stages = (int)std::min<size_t>(tune.stages, (kGemvSmemBudget - fixed) / a.stage_bytes);
   if (a.stages < 2) return cudaErrorInvalidValue;
-  const size_t smem = gemv_smem_bytes(rows_template, I, a.kc, a.stages, max_tile_rows);
+  const size_t smem = gemv_smem_bytes(rows_template, I, a.stage_bytes, a.stages);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(assigned);
   cfg.blockDim = dim3(kGemvThreads);
@@ -465,9 +579,9 @@ cudaError_t launch_gemv(GemvArgs a, int rows_template, int grid, cudaStream_t st
 }
 
 int gemv_rows_template(int rows, int in_width) {
-  // x for all rows must fit next to the ring: BF16 rows when rows > 1.
+  // x for all rows (BF16) must fit next to the ring.
   for (int r : {1, 2, 4, 8})
-    if (rows <= r && (r == 1 || size_t(in_width) * 2 * r <= 64 * 1024)) return r;
+    if (rows <= r && size_t(in_width) * 2 * r <= 64 * 1024) return r;
   if (size_t(in_width) * 2 * 8 <= 64 * 1024) return 8;
   if (size_t(in_width) * 2 * 4 <= 64 * 1024) return 4;
   if (size_t(in_width) * 2 * 2 <= 64 * 1024) return 2;

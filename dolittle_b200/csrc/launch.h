@@ -15,7 +15,7 @@ namespace dl {
 struct GemvArgs;
 
 // gemv.cu
-size_t gemv_smem_bytes(int rows, int in_width, int kc, int stages, int max_tile_rows);
+size_t gemv_smem_bytes(int rows, int in_width, int stage_bytes, int stages);
 cudaError_t launch_gemv(GemvArgs a, int rows_template, int grid, cudaStream_t stream, bool pdl);
 int gemv_rows_template(int rows, int in_width);
 inline int projection_partials(size_t in_width, size_t out_width) {
@@ -50,8 +50,8 @@ cudaError_t launch_rotary(const bf16* x, bf16* out, size_t positions, int heads,
                           RowPositions pos, double theta, bool positioned_output,
                           cudaStream_t stream);
 cudaError_t launch_inv_freq(float* out, int width, double theta, cudaStream_t stream);
-cudaError_t launch_fill_normal(bf16* out, size_t n, uint64_t seed, uint32_t stream_id,
-                               float scale, cudaStream_t stream);
+cudaError_t launch_fill_normal(bf16* out, size_t rows, size_t cols, size_t row_stride, uint64_t seed,
+                               uint32_t stream_id, float scale, cudaStream_t stream);
 cudaError_t launch_fill_const(bf16* out, size_t n, float value, cudaStream_t stream);
 cudaError_t launch_uniform_ids(uint32_t* out, size_t n, uint64_t seed, uint32_t stream_id,
                                uint32_t bound, cudaStream_t stream);

@@ -352,14 +352,17 @@ __device__ __forceinline__ void philox4x32_10(uint32_t (&c)[4], uint32_t k0, uin
   }
 }
 
-__global__ void fill_normal_kernel(bf16* out, size_t n, uint64_t seed, uint32_t stream_id, float scale) {
+// Element i of a logical [rows][cols] tensor lands at row (i/cols) of a
+// resident layout with `row_stride` elements per row.
+__global__ void fill_normal_kernel(bf16* out, size_t n, size_t cols, size_t row_stride, uint64_t seed,
+                                   uint32_t stream_id, float scale) {
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
     uint32_t c[4] = {uint32_t(i), uint32_t(uint64_t(i) >> 32), stream_id, 0u};
     philox4x32_10(c, uint32_t(seed), uint32_t(seed >> 32));
     int s = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) s += int(c[j] & 0xffffu) + int(c[j] >> 16);
-    out[i] = narrow(__fmul_rn(static_cast<float>(s - 262140), scale));
+    out[(i / cols) * row_stride + i % cols] = narrow(__fmul_rn(static_cast<float>(s - 262140), scale));
   }
 }
 
@@ -443,8 +446,8 @@ cudaError_t launch_silu_multiply(const bf16* g, const bf16* u, bf16* out, size_t
 
 cudaError_t launch_rms_norm(const bf16* x, const bf16* w, bf16* out, size_t rows, int width, float eps,
                             cudaStream_t stream) {
-  if (width > 8192) return cudaErrorInvalidValue;
-  const int warps = width > 2048 ? 2 : 4;
+  if (width > 32768) return cudaErrorInvalidValue;
+  const int warps = width > 8192 ? 1 : (width > 2048 ? 2 : 4);
   const size_t smem = size_t(warps) * width * sizeof(float);
   cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   rms_norm_kernel<<<unsigned((rows + warps - 1) / warps), 32 * warps, smem, stream>>>(x, w, out, rows, width,
@@ -465,9 +468,10 @@ cudaError_t launch_inv_freq(float* out, int width, double theta, cudaStream_t st
   return cudaGetLastError();
 }
 
-cudaError_t launch_fill_normal(bf16* out, size_t n, uint64_t seed, uint32_t stream_id, float scale,
-                               cudaStream_t stream) {
-  fill_normal_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(out, n, seed, stream_id, scale);
+cudaError_t launch_fill_normal(bf16* out, size_t rows, size_t cols, size_t row_stride, uint64_t seed,
+                               uint32_t stream_id, float scale, cudaStream_t stream) {
+  const size_t n = rows * cols;
+  fill_normal_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(out, n, cols, row_stride, seed, stream_id, scale);
   return cudaGetLastError();
 }
 

@@ -116,10 +116,11 @@ class Engine:
         check(lib().dl_engine_get_tensor(self._h, index, out.ctypes.data, out.nbytes))
         return out
 
-    def tensor_device(self, index: int) -> int:
-        p = C.c_void_p()
-        check(lib().dl_engine_tensor_device(self._h, index, C.byref(p)))
-        return int(p.value)
+    def tensor_device(self, index: int) -> tuple:
+        """(device address, row stride in elements) of a resident tensor."""
+        p, s = C.c_void_p(), C.c_size_t()
+        check(lib().dl_engine_tensor_device(self._h, index, C.byref(p), C.byref(s)))
+        return int(p.value), int(s.value)
 
     def load_tensors(self, tensors: list) -> None:
         for i, t in enumerate(tensors):

@@ -199,8 +199,11 @@ DL_API dl_status dl_engine_set_tensor(dl_engine* e, size_t index, const void* ho
                                       size_t bytes);
 DL_API dl_status dl_engine_get_tensor(dl_engine* e, size_t index, void* host_bits, size_t bytes);
 /* Device address of a resident tensor (for binding it into other kernels,
- * like the reference executor binds parameter regions). */
-DL_API dl_status dl_engine_tensor_device(dl_engine* e, size_t index, void** device_ptr);
+ * like the reference executor binds parameter regions) and its row stride
+ * in elements: gate and up rows are stored interleaved in one [2F][D]
+ * matrix, so their stride is 2*D; every other tensor is contiguous. */
+DL_API dl_status dl_engine_tensor_device(dl_engine* e, size_t index, void** device_ptr,
+                                         size_t* row_stride);
 /* Fresh sequence: position 0, empty KV cache contents unchanged. */
 DL_API dl_status dl_engine_reset(dl_engine* e);
 /* Consume prompt/continuation tokens (host IDs) at the current position;

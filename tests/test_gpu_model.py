@@ -33,8 +33,19 @@ def _tiny_engine(capacity=64, max_rows=8):
 
 
 def _ref_for(engine, cfg, capacity, max_rows):
-    ptrs = [engine.tensor_device(i) for i in range(cfg.tensor_count())]
-    return gu.RefModel(cfg, ptrs, capacity, max_rows)
+    """Reference kernels over the engine's own device weights; tensors the
+    engine stores strided (interleaved gate/up rows) get contiguous copies."""
+    ptrs, keep = [], []
+    for i in range(cfg.tensor_count()):
+        p, stride = engine.tensor_device(i)
+        if stride != cfg.tensor_shape(i)[1]:
+            t = gu.to_dev(engine.get_tensor(i))
+            keep.append(t)
+            p = gu.ptr(t)
+        ptrs.append(p)
+    ref = gu.RefModel(cfg, ptrs, capacity, max_rows)
+    ref.keep = keep
+    return ref
 
 
 @needs_ref
