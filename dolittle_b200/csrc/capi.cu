@@ -46,6 +46,10 @@ cudaStream_t st(void* s) { return static_cast<cudaStream_t>(s); }
 using dl::bf16;
 }  // namespace
 
+namespace dl {
+void set_last_error(const std::string& message) { g_error = message; }
+}  // namespace dl
+
 struct dl_engine {
   dl::Engine* impl;
 };

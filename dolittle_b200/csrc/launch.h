@@ -7,6 +7,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <string>
 
 #include "common.cuh"
 
@@ -56,6 +57,9 @@ cudaError_t launch_fill_const(bf16* out, size_t n, float value, cudaStream_t str
 cudaError_t launch_uniform_ids(uint32_t* out, size_t n, uint64_t seed, uint32_t stream_id,
                                uint32_t bound, cudaStream_t stream);
 cudaError_t launch_add_position(long long* value, long long delta, cudaStream_t stream);
+
+// capi.cu: message returned by dl_last_error() on the calling thread.
+void set_last_error(const std::string& message);
 
 inline float attention_scale(int width) {
   return static_cast<float>(1.0 / __builtin_sqrt(static_cast<double>(width)));

@@ -87,6 +87,25 @@ DL_API dl_status dl_attention(dl_dtype type, const void* query, const void* key,
                               size_t width, void* stream, size_t first_position,
                               const size_t* device_position, size_t capacity, const float* scale,
                               void* workspace);
+/* dl_attention for callers that cannot allocate device memory: a host that
+ * owns every device allocation through its own arena and forbids allocation
+ * once generation runs, or a plugin whose process allocator does not let it
+ * call cudaMalloc.  No counterpart in the reference.  Same arguments and
+ * results as dl_attention, but the scores live in a fixed array inside the
+ * library's device memory (DL_ATTENTION_FIXED_SCRATCH_SCORES FP32 values,
+ * 4 MiB, held on every GPU that loads the library until the process exits),
+ * so nothing is allocated.  positions * query_heads * key capacity above
+ * that limit is rejected with DL_INVALID_ARGUMENT.  All calls on a device
+ * share the array and it keeps the last call's contents; calls that overlap
+ * on the GPU race on it, so serialize them.  The first call on each device
+ * looks up the array's address (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture. */
+#define DL_ATTENTION_FIXED_SCRATCH_SCORES ((size_t)1 << 20)
+DL_API dl_status dl_attention_fixed_scratch(dl_dtype type, const void* query, const void* key,
+                                            const void* value, void* output, size_t positions,
+                                            size_t query_heads, size_t kv_heads, size_t width,
+                                            void* stream, size_t first_position,
+                                            const size_t* device_position, size_t capacity);
 DL_API dl_status dl_embedding(dl_dtype type, const uint32_t* tokens, const void* weight,
                               void* output, size_t rows, size_t width, void* stream);
 DL_API dl_status dl_add(dl_dtype type, const void* left, const void* right, void* output,
