@@ -63,6 +63,7 @@ SIGNATURES = {
     "dl_rope_inverse_frequency": (C.c_int, [vp, sz, C.c_double, vp]),
     "dl_qk_norm_rope_append": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, vp, sz, sz, sz, sz, C.c_float, vp]),
     "dl_projection_residual": (C.c_int, [vp, vp, vp, sz, sz, sz, vp]),
+    "dl_gemm_bf16": (C.c_int, [vp, sz, vp, vp, sz, sz, sz, sz, C.c_int, vp]),
     "dl_sampler_required_bytes": (sz, [sz]),
     "dl_sampler_create": (C.c_int, [sz, C.c_int, C.POINTER(vp)]),
     "dl_sampler_destroy": (None, [vp]),

@@ -11,6 +11,7 @@
 
 #include "../../include/dolittle_b200.h"
 #include "engine.h"
+#include "gemm_tcgen05.h"
 #include "gemv.cuh"
 #include "launch.h"
 #include "sampler.h"
@@ -238,6 +239,29 @@ DL_API dl_status dl_qk_norm_rope_append(const void* q_raw, const void* k_raw, co
                                              int(rows), int(query_heads), int(kv_heads), int(width), epsilon,
                                              st(stream), false),
                      "qk_norm_rope_append");
+}
+
+DL_API dl_status dl_gemm_bf16(const void* x, size_t ldx, const void* w, void* y, size_t ldy, size_t M, size_t N,
+                              size_t K, int epilogue, void* stream) {
+  if (!x || !w || !y || !M) return fail(DL_INVALID_ARGUMENT, "gemm: null pointer or empty shape");
+  if (epilogue != dl::kGemmStore && epilogue != dl::kGemmResidual && epilogue != dl::kGemmSwiGLU)
+    return fail(DL_INVALID_ARGUMENT, "gemm: epilogue must be 0, 1 or 3");
+  if (!dl::gemm_tcgen05_supported(int(M), int(N), int(K)) || ldx % 8 || ldy % 8 || ldx < K ||
+      (reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y)) % 16)
+    return fail(DL_UNSUPPORTED, "gemm: K % 64, N % 128, 8-element row strides and 16-byte alignment required");
+  dl::GemmProblem p = {};
+  p.x = static_cast<const bf16*>(x);
+  p.ldx = int(ldx);
+  p.w = static_cast<const bf16*>(w);
+  p.M = int(M);
+  p.N = int(N);
+  p.K = int(K);
+  p.epilogue = epilogue;
+  p.nseg = 1;
+  p.seg_out[0] = static_cast<bf16*>(y);
+  p.seg_ld[0] = int(ldy);
+  p.wide_tiles = true;
+  return cuda_status(dl::launch_gemm_tcgen05(p, st(stream), false), "gemm");
 }
 
 DL_API dl_status dl_projection_residual(const void* input, const void* weight, void* residual, size_t rows,

@@ -6,7 +6,9 @@
 #include <stdexcept>
 #include <string>
 
+#include "attention_decode.h"
 #include "engine.h"
+#include "gemm_tcgen05.h"
 #include "steering.h"
 
 namespace dl {
@@ -58,7 +60,7 @@ Engine::Engine(const dl_model_config& cfg, int device, size_t capacity, size_t m
   const size_t D = cfg.hidden, Q = size_t(cfg.query_heads) * cfg.head_width,
                G = size_t(cfg.kv_heads) * cfg.head_width, F = cfg.mlp_width, V = cfg.vocabulary,
                d = cfg.head_width, L = cfg.layers;
-  if (!D || !Q || !G || !F || !V || !L || !capacity || !max_rows || max_rows > 64 ||
+  if (!D || !Q || !G || !F || !V || !L || !capacity || !max_rows || max_rows > 8192 ||
       cfg.query_heads % cfg.kv_heads || d > 128 || d % 2 || D % 8 || Q % 8 || F % 8 ||
       cfg.query_heads / cfg.kv_heads > 8)
     throw std::invalid_argument("unsupported Qwen3 configuration");
@@ -131,7 +133,7 @@ Engine::Engine(const dl_model_config& cfg, int device, size_t capacity, size_t m
                o_tok = stake(std::max<size_t>(R, 64) * 4), o_hist = stake(history_cap_ * 4),
                o_part = stake(size_t(4 * sms_) * 16), o_state = stake(sizeof(DeviceState)),
                o_inv = stake(d * 2), o_dir = stake(D * 4), o_edit = stake(64),
-               o_cap = stake(capacity * D * 2);
+               o_cap = stake(capacity * D * 2), o_xn = stake(R * D * 2);
   check(cudaMalloc(&scratch_, s), "scratch");
   check(cudaMemsetAsync(scratch_, 0, s, stream_), "scratch clear");
   auto* sb = static_cast<unsigned char*>(scratch_);
@@ -151,6 +153,7 @@ Engine::Engine(const dl_model_config& cfg, int device, size_t capacity, size_t m
   edit_direction_ = reinterpret_cast<float*>(sb + o_dir);
   edit_state_ = reinterpret_cast<uint32_t*>(sb + o_edit);
   capture_arena_ = reinterpret_cast<bf16*>(sb + o_cap);
+  xn_ = reinterpret_cast<bf16*>(sb + o_xn);
   check(launch_inv_freq(inv_freq_, int(d), cfg.theta, stream_), "inv_freq");
   check(cudaStreamSynchronize(stream_), "init sync");
 }
@@ -299,15 +302,23 @@ void Engine::run_layers(int rows, bool pdl) {
     qkv[2] = make_segment(y.wqkv + size_t(Q + G) * D, vcache_[l], &state_->position, G, projection_partials(D, G), G);
     capture_target_ = false;
     project(residual_, D, rows, D, kPrologueRmsNorm, y.in_norm, kEpilogueStore, qkv, 3, pdl);
-    check(launch_qk_norm_rope(q_raw_, k_raw_, y.q_norm, y.k_norm, inv_freq_, q_rot_, kcache_[l], pos, rows,
-                              H, Hk, d, cfg_.epsilon, stream_, pdl),
-          "qk_norm_rope");
-    check(launch_attention_scores(q_rot_, kcache_[l], scores_, pos, rows, H, Hk, d, cap, scale, score_ctas,
-                                  stream_, pdl),
-          "attention scores");
-    check(launch_attention_pv(scores_, vcache_[l], att_, pos, rows, H, Hk, d, cap, stream_, pdl),
-          "attention pv");
-    launches_ += 3;
+    if (rows == 1 && attention_decode_supported(H, Hk, d, cap)) {
+      // One query row: QK-norm/RoPE/K-append fused into the score kernel.
+      check(launch_attention_decode(q_raw_, k_raw_, y.q_norm, y.k_norm, inv_freq_, kcache_[l], vcache_[l], scores_,
+                                    att_, &state_->position, H, Hk, d, cap, cfg_.epsilon, score_ctas, stream_, pdl),
+            "attention decode");
+      launches_ += 2;
+    } else {
+      check(launch_qk_norm_rope(q_raw_, k_raw_, y.q_norm, y.k_norm, inv_freq_, q_rot_, kcache_[l], pos, rows,
+                                H, Hk, d, cfg_.epsilon, stream_, pdl),
+            "qk_norm_rope");
+      check(launch_attention_scores(q_rot_, kcache_[l], scores_, pos, rows, H, Hk, d, cap, scale, score_ctas,
+                                    stream_, pdl),
+            "attention scores");
+      check(launch_attention_pv(scores_, vcache_[l], att_, pos, rows, H, Hk, d, cap, stream_, pdl),
+            "attention pv");
+      launches_ += 3;
+    }
     GemvSegment o = make_segment(y.wo, residual_, nullptr, D, projection_partials(Q, D), D);
     project(att_, Q, rows, Q, kProloguePlain, nullptr, kEpilogueResidual, &o, 1, pdl);
     // Interleaved gate|up rows; the epilogue writes the SwiGLU activation.
@@ -363,13 +374,108 @@ void Engine::lm_head_select(const bf16* last_row, bool advance, bool generating,
   ++launches_;
 }
 
-void Engine::consume_rows(const uint32_t* tokens, size_t n, bool pdl) {
+bool Engine::fast_prefill_supported() const {
+  const int D = int(cfg_.hidden), Q = int(cfg_.query_heads * cfg_.head_width),
+            G = int(cfg_.kv_heads * cfg_.head_width), F = int(cfg_.mlp_width);
+  return gemm_tcgen05_supported(1, Q + 2 * G, D) && gemm_tcgen05_supported(1, D, Q) &&
+         gemm_tcgen05_supported(1, 2 * F, D) && gemm_tcgen05_supported(1, D, F) && Q % 256 == 0 &&
+         (Q + G) % 256 == 0;
+}
+
+// Prompt rows on the tensor cores: RMSNorm, then tcgen05 GEMMs for QKV (V
+// rows appended to the cache by the epilogue), o (+residual), gate|up
+// (+SwiGLU) and down (+residual); QK-norm/RoPE and causal attention use the
+// same kernels as the parity path.  `first` is the absolute position of row 0.
+void Engine::run_layers_fast(int rows, long long first) {
+  const int D = int(cfg_.hidden), Q = int(cfg_.query_heads * cfg_.head_width),
+            G = int(cfg_.kv_heads * cfg_.head_width), F = int(cfg_.mlp_width), d = int(cfg_.head_width),
+            H = int(cfg_.query_heads), Hk = int(cfg_.kv_heads);
+  const RowPositions pos{&state_->position, 0};
+  const int cap = int(capacity_);
+  const int score_ctas = std::clamp((cap + 255) / 256, 1, 8);
+  auto gemm = [&](const bf16* x, int ldx, const bf16* w, int N, int K, int epi, int nseg, const int* n0s,
+                  bf16* const* outs, const int* lds) {
+    GemmProblem p = {};
+    p.x = x;
+    p.ldx = ldx;
+    p.w = w;
+    p.M = rows;
+    p.N = N;
+    p.K = K;
+    p.epilogue = epi;
+    p.nseg = nseg;
+    for (int i = 0; i < nseg; ++i) {
+      p.seg_n0[i] = n0s[i];
+      p.seg_out[i] = outs[i];
+      p.seg_ld[i] = lds[i];
+    }
+    p.wide_tiles = true;
+    p.err = &state_->err;
+    check(launch_gemm_tcgen05(p, stream_, false), "gemm");
+    ++launches_;
+  };
+  for (size_t l = 0; l < layers_.size(); ++l) {
+    const Layer& y = layers_[l];
+    check(launch_rms_norm(residual_, y.in_norm, xn_, size_t(rows), D, cfg_.epsilon, stream_), "rms_norm");
+    {
+      const int n0s[3] = {0, Q, Q + G};
+      bf16* outs[3] = {q_raw_, k_raw_, vcache_[l] + size_t(first) * G};
+      const int lds[3] = {Q, G, G};
+      gemm(xn_, D, y.wqkv, Q + 2 * G, D, kGemmStore, 3, n0s, outs, lds);
+    }
+    check(launch_qk_norm_rope(q_raw_, k_raw_, y.q_norm, y.k_norm, inv_freq_, q_rot_, kcache_[l], pos, rows, H, Hk,
+                              d, cfg_.epsilon, stream_, false),
+          "qk_norm_rope");
+    check(launch_attention_scores(q_rot_, kcache_[l], scores_, pos, rows, H, Hk, d, cap, attention_scale(d),
+                                  score_ctas, stream_, false),
+          "attention scores");
+    check(launch_attention_pv(scores_, vcache_[l], att_, pos, rows, H, Hk, d, cap, stream_, false), "attention pv");
+    launches_ += 4;
+    {
+      const int n0s[1] = {0};
+      bf16* outs[1] = {residual_};
+      const int lds[1] = {D};
+      gemm(att_, Q, y.wo, D, Q, kGemmResidual, 1, n0s, outs, lds);
+    }
+    check(launch_rms_norm(residual_, y.post_norm, xn_, size_t(rows), D, cfg_.epsilon, stream_), "rms_norm");
+    ++launches_;
+    {
+      const int n0s[1] = {0};
+      bf16* outs[1] = {gu_};
+      const int lds[1] = {F};
+      gemm(xn_, D, y.wgu, 2 * F, D, kGemmSwiGLU, 1, n0s, outs, lds);
+    }
+    {
+      const int n0s[1] = {0};
+      bf16* outs[1] = {residual_};
+      const int lds[1] = {D};
+      gemm(gu_, F, y.wd, D, F, kGemmResidual, 1, n0s, outs, lds);
+    }
+    if (edit_layer_ == int(l)) {
+      check(launch_intervene(residual_, edit_direction_, &state_->position, edit_state_, D, (long long)edit_row_,
+                             rows, edit_strength_, stream_, false),
+            "intervene");
+      ++launches_;
+    }
+    if (capture_layer_ == int(l)) {
+      check(launch_copy_rows(residual_, capture_arena_, &state_->position, D, rows, stream_, false), "capture copy");
+      ++launches_;
+    }
+  }
+}
+
+void Engine::consume_rows(const uint32_t* tokens, size_t n, bool pdl, int mode, long long first) {
+  const bool fast = mode == DL_PREFILL_FAST && fast_prefill_supported();
   for (size_t c0 = 0; c0 < n; c0 += max_rows_) {
     const int rows = int(std::min(max_rows_, n - c0));
     check(cudaMemcpyAsync(tokens_dev_, tokens + c0, rows * 4, cudaMemcpyHostToDevice, stream_), "tokens");
     check(launch_embedding(tokens_dev_, embed_, residual_, rows, int(cfg_.hidden), stream_, false), "embed");
-    run_layers(rows, pdl);
+    if (fast)
+      run_layers_fast(rows, first);
+    else
+      run_layers(rows, pdl);
     check(launch_add_position(&state_->position, rows, stream_), "advance");
+    first += rows;
     last_rows_ = rows;
   }
 }
@@ -377,9 +483,10 @@ void Engine::consume_rows(const uint32_t* tokens, size_t n, bool pdl) {
 void Engine::consume(const uint32_t* tokens, size_t n, int mode, uint16_t* logits_out) {
   check(cudaSetDevice(device_), "cudaSetDevice");
   if (!n) throw std::invalid_argument("empty consume");
-  if (position() + n > capacity_) throw std::length_error("sequence exceeds KV capacity");
-  if (mode != DL_PREFILL_PARITY) throw std::invalid_argument("fast prefill not available");
-  consume_rows(tokens, n, true);
+  const size_t first = position();
+  if (first + n > capacity_) throw std::length_error("sequence exceeds KV capacity");
+  if (mode != DL_PREFILL_PARITY && mode != DL_PREFILL_FAST) throw std::invalid_argument("unknown prefill mode");
+  consume_rows(tokens, n, true, mode, (long long)first);
   lm_head_select(residual_ + size_t(last_rows_ - 1) * cfg_.hidden, false, false, true);
   if (logits_out)
     check(cudaMemcpyAsync(logits_out, logits_, size_t(cfg_.vocabulary) * 2, cudaMemcpyDeviceToHost, stream_),
@@ -495,7 +602,8 @@ void Engine::generate(const uint32_t* prompt, size_t n_prompt, size_t max_new, c
   if (!n_prompt || !max_new) throw std::invalid_argument("empty prompt or budget");
   if (n_prompt + max_new > capacity_) throw std::length_error("sequence exceeds KV capacity");
   validate_sampling(s, cfg_.vocabulary);
-  if (prefill_mode != DL_PREFILL_PARITY) throw std::invalid_argument("fast prefill not available");
+  if (prefill_mode != DL_PREFILL_PARITY && prefill_mode != DL_PREFILL_FAST)
+    throw std::invalid_argument("unknown prefill mode");
   for (size_t i = 0; i < n_stop; ++i)
     if (stop_ids[i] >= cfg_.vocabulary) throw std::invalid_argument("stop ID outside vocabulary");
   reset();
@@ -507,7 +615,7 @@ void Engine::generate(const uint32_t* prompt, size_t n_prompt, size_t max_new, c
   const size_t V = cfg_.vocabulary;
   check(cudaEventRecord(ev_[0], stream_), "event");
   launches_ = 0;
-  consume_rows(prompt, n_prompt, true);
+  consume_rows(prompt, n_prompt, true, prefill_mode, 0);
   select(residual_ + size_t(last_rows_ - 1) * cfg_.hidden, false, true);
   check(cudaEventRecord(ev_[1], stream_), "event");
   // DOLITTLE_DECODE_GRAPH=0 launches the same per-token kernels eagerly

@@ -69,8 +69,10 @@ class Engine {
 
  private:
   TensorView view(size_t index);
-  void consume_rows(const uint32_t* tokens, size_t n, bool pdl);
+  void consume_rows(const uint32_t* tokens, size_t n, bool pdl, int mode, long long first);
   void run_layers(int rows, bool pdl);
+  void run_layers_fast(int rows, long long first);
+  bool fast_prefill_supported() const;
   void decode_step(bool pdl);
   void lm_head_select(const bf16* last_row, bool advance_position, bool generating, bool pdl);
   void lm_head_logits(const bf16* last_row, bool pdl);
@@ -97,7 +99,7 @@ class Engine {
   std::vector<bf16*> kcache_, vcache_;
   // scratch
   void* scratch_ = nullptr;
-  bf16 *residual_, *q_raw_, *k_raw_, *q_rot_, *att_, *gu_, *logits_;
+  bf16 *residual_, *q_raw_, *k_raw_, *q_rot_, *att_, *gu_, *logits_, *xn_;
   float* scores_;
   uint32_t* tokens_dev_;
   uint32_t* history_;

@@ -1,0 +1,31 @@
+// tcgen05/TMEM GEMM for prefill projections (see gemm_tcgen05.cu).
+#pragma once
+
+#include "launch.h"
+
+namespace dl {
+
+enum GemmEpilogue : int {
+  kGemmStore = 0,     // out = bf16(acc)
+  kGemmResidual = 1,  // out = round(out + round(acc)) in place
+  kGemmSwiGLU = 3,    // columns (2o, 2o+1) = (gate o, up o): out[o] = SwiGLU law
+};
+
+struct GemmProblem {
+  const bf16* x;      // [M][K], row stride ldx
+  int ldx;
+  const bf16* w;      // [N][K] contiguous
+  int M, N, K;
+  int epilogue;
+  int nseg;           // outputs by column range: columns [seg_n0[i], seg_n0[i+1])
+  int seg_n0[3];
+  bf16* seg_out[3];   // output of segment i (column 0 of the segment)
+  int seg_ld[3];      // output row stride (elements)
+  bool wide_tiles;    // allow 128 x 256 tiles
+  unsigned* err;
+};
+
+bool gemm_tcgen05_supported(int M, int N, int K);
+cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool pdl);
+
+}  // namespace dl

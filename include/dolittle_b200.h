@@ -134,6 +134,15 @@ DL_API dl_status dl_qk_norm_rope_append(const void* q_raw, const void* k_raw,
                                         const int64_t* position, size_t rows, size_t query_heads,
                                         size_t kv_heads, size_t width, float epsilon,
                                         void* stream);
+/* Prefill / batched projection on the tcgen05 tensor cores (TMEM FP32
+ * accumulation; not the reference's summation order):
+ *   epilogue 0: Y = bf16(X W^T)            (Y row stride ldy)
+ *   epilogue 1: Y = round(Y + round(X W^T)) in place (residual add)
+ *   epilogue 3: W rows interleaved (gate o, up o): Y[:, o] = SwiGLU law.
+ * X [M][K] with row stride ldx, W [N][K] contiguous; K % 64 == 0,
+ * N % 128 == 0, 16-byte aligned rows. */
+DL_API dl_status dl_gemm_bf16(const void* x, size_t ldx, const void* w, void* y, size_t ldy, size_t M,
+                              size_t N, size_t K, int epilogue, void* stream);
 /* residual = round(residual + round(X W^T)) in place. */
 DL_API dl_status dl_projection_residual(const void* input, const void* weight, void* residual,
                                         size_t rows, size_t input_width, size_t output_width,

@@ -1,0 +1,78 @@
+"""tcgen05/TMEM GEMM (fast prefill projections) against a PyTorch FP32
+reference of the same op: Y = X W^T accumulated in FP32, rounded to BF16.
+
+The tensor-core summation order differs from the reference's strided FP32
+chains, so the check is the reference's BF16 projection tolerance
+(atol 1e-3, rtol 1.6e-2; tests/gpu/operator_reference.cpp) plus a
+relative-L2 bound, and nearly all elements must round identically.
+"""
+import numpy as np
+import pytest
+
+import dolittle_b200 as dl
+from tests import numerics as nm
+
+pytestmark = pytest.mark.gpu
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def _case(M, N, K, seed, scale_w=0.02):
+    torch = _torch()
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) * scale_w).to(torch.bfloat16)
+    return x, w
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 4096, 4096), (77, 1024, 4096), (128, 256, 12288),
+                                   (512, 6144, 4096), (300, 128, 64), (1, 256, 128)])
+def test_gemm_store_matches_fp32_reference(M, N, K):
+    torch = _torch()
+    x, w = _case(M, N, K, seed=M + N + K)
+    y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    assert dl.lib().dl_gemm_bf16(x.data_ptr(), K, w.data_ptr(), y.data_ptr(), N, M, N, K, 0, None) == 0, \
+        dl.lib().dl_last_error()
+    torch.cuda.synchronize()
+    ref = (x.float() @ w.float().T)
+    got = y.float()
+    r = nm.compare_elementwise(ref.cpu().numpy(), got.cpu().numpy(), 1e-3, 1.6e-2)
+    assert r["passed"], r
+    same = (ref.to(torch.bfloat16) == y).float().mean().item()
+    assert same > 0.97, same
+    rel = ((got - ref).norm() / ref.norm()).item()
+    assert rel < 4e-3, rel
+
+
+def test_gemm_residual_and_swiglu_epilogues():
+    torch = _torch()
+    M, D, F = 96, 512, 256
+    x, w = _case(M, D, D, seed=5)
+    res = torch.randn(M, D, device="cuda").to(torch.bfloat16)
+    out = res.clone()
+    assert dl.lib().dl_gemm_bf16(x.data_ptr(), D, w.data_ptr(), out.data_ptr(), D, M, D, D, 1, None) == 0
+    torch.cuda.synchronize()
+    proj = (x.float() @ w.float().T).to(torch.bfloat16).float()
+    ref = (res.float() + proj).to(torch.bfloat16).float()
+    r = nm.compare_elementwise(ref.cpu().numpy(), out.float().cpu().numpy(), 1e-2, 1.6e-2)
+    assert r["passed"], r
+    # SwiGLU on interleaved (gate, up) rows.
+    xg, wgu = _case(M, 2 * F, D, seed=6)
+    act = torch.empty(M, F, device="cuda", dtype=torch.bfloat16)
+    assert dl.lib().dl_gemm_bf16(xg.data_ptr(), D, wgu.data_ptr(), act.data_ptr(), F, M, 2 * F, D, 3, None) == 0
+    torch.cuda.synchronize()
+    yy = (xg.float() @ wgu.float().T).to(torch.bfloat16).float()
+    g, u = yy[:, 0::2], yy[:, 1::2]
+    ref2 = ((g * torch.sigmoid(g)).to(torch.bfloat16).float() * u).to(torch.bfloat16).float()
+    r2 = nm.compare_elementwise(ref2.cpu().numpy(), act.float().cpu().numpy(), 1e-2, 3e-2)
+    assert r2["passed"], r2
+
+
+def test_gemm_rejects_unsupported_shapes():
+    torch = _torch()
+    x = torch.zeros(8, 100, device="cuda", dtype=torch.bfloat16)
+    assert dl.lib().dl_gemm_bf16(x.data_ptr(), 100, x.data_ptr(), x.data_ptr(), 128, 8, 128, 100, 0,
+                                 None) == dl._lib.DL_UNSUPPORTED

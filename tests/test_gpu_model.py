@@ -149,6 +149,32 @@ def test_8b_shape_generation_graph_matches_reference_greedy():
     assert tokens == out.tokens
 
 
+def test_fast_prefill_within_tolerance_of_parity_prefill():
+    """The tcgen05 prompt pass (tensor-core accumulation order) against the
+    parity prompt pass: the 36-block fixture tolerance (max-abs <= 0.0625 x
+    peak, relative L2 <= 0.03, forward_reference.py:153-162) on the logits
+    and on the KV cache, cosine > 0.999."""
+    cap = 200
+    cfg, e = _model_8b_shape(2, cap, max_rows=160)
+    prompt = oracle.uniform_ids(150, 1, 104, cfg.vocabulary)
+    parity = nm.bf16_bits_to_f32(e.consume_view(prompt, dl.DL_PREFILL_PARITY))
+    kv_parity = [e.read_kv(l, v, 0, 150) for l in range(2) for v in (False, True)]
+    e.reset()
+    fast = nm.bf16_bits_to_f32(e.consume_view(prompt, dl.DL_PREFILL_FAST))
+    peak = float(np.max(np.abs(parity)))
+    r = nm.compare_values(parity, fast, max(1e-4, 0.0625 * peak), 0.03)
+    assert r["passed"], r
+    assert nm.cosine(parity, fast) > 0.999
+    for a, (l, v) in zip(kv_parity, [(l, v) for l in range(2) for v in (False, True)]):
+        b = nm.bf16_bits_to_f32(e.read_kv(l, v, 0, 150))
+        a = nm.bf16_bits_to_f32(a)
+        assert nm.cosine(a, b) > 0.999
+        assert nm.compare_values(a, b, max(1e-4, 0.0625 * float(np.max(np.abs(a)))), 0.03)["passed"]
+    # Decode continues from the fast cache through the graph.
+    out = e.generate(prompt, 4, prefill=dl.DL_PREFILL_FAST)
+    assert out.status == 0 and len(out.tokens) == 4
+
+
 @needs_ref
 def test_chunked_prefill_is_bit_invariant():
     cap = 64
