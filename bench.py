@@ -361,6 +361,12 @@ def run_profile_case(args):
                                           None) == 0
         torch.cuda.synchronize()
         print("profile gemv ok")
+    elif args.profile == "prefill":
+        cfg = dl.QWEN3_8B
+        e = dl.Engine(cfg, capacity=PROMPT + 8, max_rows=PROMPT)
+        e.init_random(SEED, 0.02)
+        e.consume_view(prompt_ids(cfg.vocabulary), dl.DL_PREFILL_FAST)
+        print("profile prefill ok")
     else:
         cfg = dl.QWEN3_8B
         e = dl.Engine(cfg, capacity=64, max_rows=16)
@@ -379,7 +385,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill", choices=["fast", "parity"], default="fast",
                     help="prompt pass on the tcgen05 GEMMs (fast) or in the reference order (parity)")
-    ap.add_argument("--profile", choices=["gemv", "decode"], default=None,
+    ap.add_argument("--profile", choices=["gemv", "decode", "prefill"], default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
     args = ap.parse_args()
     if args.profile:
