@@ -16,6 +16,7 @@ HEADER = os.path.join(os.path.dirname(HERE), "include", "dolittle_b200.h")
 DL_OK, DL_INVALID_ARGUMENT, DL_UNSUPPORTED, DL_CUDA_ERROR, DL_OUT_OF_MEMORY, DL_DEVICE_FAULT = range(6)
 DL_BF16, DL_F32 = 0, 1
 DL_PREFILL_PARITY, DL_PREFILL_FAST = 0, 1
+DL_DECODE_PERSISTENT, DL_DECODE_KERNELS = 0, 1
 
 
 class DolittleError(RuntimeError):
@@ -86,6 +87,7 @@ SIGNATURES = {
     "dl_engine_set_capture": (C.c_int, [vp, C.c_int]),
     "dl_engine_read_capture": (C.c_int, [vp, sz, sz, u16p]),
     "dl_engine_set_intervention": (C.c_int, [vp, C.c_int, sz, C.c_float, C.POINTER(C.c_float)]),
+    "dl_engine_set_decode_path": (C.c_int, [vp, C.c_int]),
     "dl_engine_read_kv": (C.c_int, [vp, sz, C.c_int, sz, sz, u16p]),
     "dl_engine_generate": (C.c_int, [vp, u32p, sz, sz, C.POINTER(Sampling), C.c_uint64, u32p, sz, C.c_int,
                                      u32p, C.POINTER(sz), u16p, C.POINTER(GenerationStats)]),

@@ -437,6 +437,9 @@ DL_API dl_status dl_engine_set_intervention(dl_engine* e, int layer, size_t sele
                                             const float* host_direction) {
   DL_ENGINE_CALL(e->impl->set_intervention(layer, selected, strength, host_direction));
 }
+DL_API dl_status dl_engine_set_decode_path(dl_engine* e, int path) {
+  DL_ENGINE_CALL(e->impl->set_decode_path(path));
+}
 DL_API dl_status dl_engine_read_kv(dl_engine* e, size_t layer, int values, size_t first, size_t count,
                                    uint16_t* host) {
   DL_ENGINE_CALL(e->impl->read_kv(layer, values, first, count, host));

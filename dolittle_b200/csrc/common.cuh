@@ -33,6 +33,7 @@ enum : unsigned {
   kErrWaitFull = 1,    // consumer gave up waiting for a weight stage
   kErrWaitEmpty = 2,   // producer gave up waiting for a free stage
   kErrBounds = 3,      // a device-side position/index check failed
+  kErrGridSync = 4,    // a persistent kernel's grid barrier gave up waiting
 };
 
 __device__ __forceinline__ void record_error(unsigned* err, unsigned code) {
@@ -74,6 +75,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Non-blocking test of a phase (try_wait may suspend the thread for a while).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(smem_addr(bar)), "r"(parity)

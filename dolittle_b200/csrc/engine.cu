@@ -129,7 +129,7 @@ Engine::Engine(const dl_model_config& cfg, int device, size_t capacity, size_t m
   };
   const size_t o_res = stake(R * D * 2), o_qraw = stake(R * Q * 2), o_kraw = stake(R * G * 2),
                o_qrot = stake(R * Q * 2), o_att = stake(R * Q * 2), o_gu = stake(R * 2 * F * 2),
-               o_logits = stake(V * 2), o_scores = stake(R * cfg.query_heads * capacity * 4),
+               o_logits = stake(V * 2), o_scores = stake(R * cfg.query_heads * align_up(capacity, 4) * 4),
                o_tok = stake(std::max<size_t>(R, 64) * 4), o_hist = stake(history_cap_ * 4),
                o_part = stake(size_t(4 * sms_) * 16), o_state = stake(sizeof(DeviceState)),
                o_inv = stake(d * 2), o_dir = stake(D * 4), o_edit = stake(64),
@@ -160,6 +160,8 @@ Engine::Engine(const dl_model_config& cfg, int device, size_t capacity, size_t m
 
 Engine::~Engine() {
   if (decode_exec_) cudaGraphExecDestroy(decode_exec_);
+  cudaFree(persist_layers_);
+  cudaFree(persist_maps_);
   for (auto& ev : ev_)
     if (ev) cudaEventDestroy(ev);
   cudaFree(scratch_);
@@ -510,6 +512,11 @@ void Engine::read_capture(size_t first, size_t count, uint16_t* host) {
 
 void Engine::set_intervention(int layer, size_t selected, float strength, const float* direction) {
   if (layer >= int(cfg_.layers)) throw std::invalid_argument("intervention layer out of range");
+  // The captured step graph holds the row and strength as launch arguments.
+  if (decode_exec_) {
+    cudaGraphExecDestroy(decode_exec_);
+    decode_exec_ = nullptr;
+  }
   edit_layer_ = layer;
   edit_row_ = selected;
   edit_strength_ = strength;
@@ -559,18 +566,145 @@ void Engine::select(const bf16* last_row, bool advance, bool pdl) {
   check(sampler_feed(sampler_, history_, &state_->step, embed_, residual_, int(cfg_.hidden),
                      advance ? &state_->position : nullptr, stream_),
         "sampler feed");
-  launches_ += 4;
+  launches_ += sampler_launch_count(sampler_, sampler_.settings, true) + 1;
+}
+
+void Engine::set_decode_path(int path) {
+  if (path != DL_DECODE_PERSISTENT && path != DL_DECODE_KERNELS) throw std::invalid_argument("unknown decode path");
+  decode_path_ = path;
+}
+
+// Plans the persistent decode step once: per block the qkv, o, gate|up and
+// down projection phases and the vocabulary head, with their tensor maps, in
+// device memory.  Unsupported shapes or devices keep the per-operation path.
+bool Engine::persistent_decode_ready() {
+  if (persist_state_ >= 0) return persist_state_ == 1;
+  persist_state_ = 0;
+  const int D = int(cfg_.hidden), Q = int(cfg_.query_heads * cfg_.head_width),
+            G = int(cfg_.kv_heads * cfg_.head_width), F = int(cfg_.mlp_width), V = int(cfg_.vocabulary),
+            d = int(cfg_.head_width), group = int(cfg_.query_heads / cfg_.kv_heads);
+  const int grid = sms_;
+  if (group > 7 || d > 128 || d % 8 || 2 * group * 8 > kGemvConsumers || !decode_persistent_fits(grid)) return false;
+  const size_t L = layers_.size();
+  std::vector<PLayer> host(L);
+  std::vector<CUtensorMap> maps(L * 6 + 1);
+  for (size_t l = 0; l < L; ++l) {
+    const Layer& y = layers_[l];
+    PLayer& p = host[l];
+    const PSegSpec qkv[3] = {
+        {y.wqkv, q_raw_, nullptr, Q, projection_partials(D, Q), Q},
+        {y.wqkv + size_t(Q) * D, k_raw_, nullptr, G, projection_partials(D, G), G},
+        {y.wqkv + size_t(Q + G) * D, vcache_[l], &state_->position, G, projection_partials(D, G), G}};
+    const PSegSpec o = {y.wo, residual_, nullptr, D, projection_partials(Q, D), D};
+    const PSegSpec gu = {y.wgu, gu_, nullptr, 2 * F, projection_partials(D, F), F};
+    const PSegSpec dn = {y.wd, residual_, nullptr, D, projection_partials(F, D), D};
+    if (!plan_persist_gemv(p.qkv, qkv, 3, residual_, y.in_norm, D, kEpilogueStore, grid, &maps[l * 6]) ||
+        !plan_persist_gemv(p.o, &o, 1, att_, nullptr, Q, kEpilogueResidual, grid, &maps[l * 6 + 3]) ||
+        !plan_persist_gemv(p.gu, &gu, 1, residual_, y.post_norm, D, kEpilogueSwiGLU, grid, &maps[l * 6 + 4]) ||
+        !plan_persist_gemv(p.down, &dn, 1, gu_, nullptr, F, kEpilogueResidual, grid, &maps[l * 6 + 5]))
+      return false;
+    p.q_norm = y.q_norm;
+    p.k_norm = y.k_norm;
+    p.k_cache = kcache_[l];
+    p.v_cache = vcache_[l];
+  }
+  const PSegSpec head = {lm_head_, logits_, nullptr, V, projection_partials(D, V), V};
+  if (!plan_persist_gemv(persist_head_, &head, 1, residual_, final_norm_, D, kEpilogueArgmax, grid, &maps[L * 6]))
+    return false;
+  check(cudaMalloc(&persist_maps_, maps.size() * sizeof(CUtensorMap)), "persistent maps");
+  check(cudaMalloc(&persist_layers_, L * sizeof(PLayer)), "persistent plan");
+  for (size_t l = 0; l < L; ++l) {
+    PGemv* ph[4] = {&host[l].qkv, &host[l].o, &host[l].gu, &host[l].down};
+    const int base[4] = {0, 3, 4, 5};
+    for (int k = 0; k < 4; ++k)
+      for (int i = 0; i < ph[k]->nseg; ++i) ph[k]->seg[i].map = persist_maps_ + l * 6 + base[k] + i;
+  }
+  persist_head_.seg[0].map = persist_maps_ + L * 6;
+  check(cudaMemcpy(persist_maps_, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice),
+        "persistent maps copy");
+  check(cudaMemcpy(persist_layers_, host.data(), L * sizeof(PLayer), cudaMemcpyHostToDevice), "persistent plan copy");
+  persist_state_ = 1;
+  return true;
+}
+
+void Engine::launch_persistent_step(bool greedy) {
+  PersistArgs a = {};
+  a.layers = persist_layers_;
+  a.nlayers = int(layers_.size());
+  a.head = persist_head_;
+  a.head.epilogue = greedy ? kEpilogueArgmax : kEpilogueStore;
+  a.q_raw = q_raw_;
+  a.k_raw = k_raw_;
+  a.scores = scores_;
+  a.att = att_;
+  a.residual = residual_;
+  a.inv_freq = inv_freq_;
+  a.position = &state_->position;
+  a.hidden = int(cfg_.hidden);
+  a.query_heads = int(cfg_.query_heads);
+  a.kv_heads = int(cfg_.kv_heads);
+  a.width = int(cfg_.head_width);
+  a.capacity = int(capacity_);
+  a.scale = attention_scale(int(cfg_.head_width));
+  a.eps = cfg_.epsilon;
+  a.score_stride = int(align_up(capacity_, 4));
+  a.score_slices = std::max(1, sms_ / int(cfg_.kv_heads));
+  a.pv_features = 8;
+  // DOLITTLE_PERSIST_PREFETCH overrides the L2 prefetch distance (stages).
+  static const int prefetch = [] {
+    const char* v = std::getenv("DOLITTLE_PERSIST_PREFETCH");
+    return v ? std::max(0, std::min(256, std::atoi(v))) : kPersistPrefetchStages;
+  }();
+  a.prefetch_stages = prefetch;
+  a.capture = capture_layer_ >= 0 ? capture_arena_ : nullptr;
+  a.capture_layer = capture_layer_;
+  a.edit_layer = edit_layer_;
+  a.edit_row = (long long)edit_row_;
+  a.edit_strength = edit_strength_;
+  a.edit_direction = edit_direction_;
+  a.edit_state = edit_state_;
+  a.partials = partials_;
+  a.ticket = &state_->ticket;
+  if (greedy) {
+    a.select.result = state_->result;
+    a.select.history = history_;
+    a.select.step = &state_->step;
+    a.select.embed = embed_;
+    a.select.residual = residual_;
+    a.select.width = int(cfg_.hidden);
+    a.select.terminal = &state_->terminal;
+    a.select.stop_mask = stop_mask_;
+    a.select.position = &state_->position;
+  }
+  a.barrier = &state_->barrier;
+  a.exit_ticket = &state_->exit_ticket;
+  a.err = &state_->err;
+  check(launch_decode_persistent(a, sms_, stream_), "persistent decode");
+  ++launches_;
 }
 
 void Engine::decode_step(bool pdl) {
+  if (decode_path_ == DL_DECODE_PERSISTENT && persistent_decode_ready()) {
+    launch_persistent_step(mode_ == 0);
+    if (mode_ != 0) {
+      check(sampler_submit(sampler_, logits_, sampler_.settings, 0, true, stream_), "sampler");
+      check(sampler_feed(sampler_, history_, &state_->step, embed_, residual_, int(cfg_.hidden), &state_->position,
+                         stream_),
+            "sampler feed");
+      launches_ += sampler_launch_count(sampler_, sampler_.settings, true) + 1;
+    }
+    return;
+  }
   run_layers(1, pdl);
   select(residual_, true, pdl);
 }
 
 void Engine::capture_decode_graph() {
   if (decode_exec_ && graph_capture_layer_ == capture_layer_ && graph_edit_layer_ == edit_layer_ &&
-      graph_mode_ == mode_)
+      graph_mode_ == mode_ && graph_path_ == decode_path_)
     return;
+  // Plan outside the capture (it allocates and copies).
+  if (decode_path_ == DL_DECODE_PERSISTENT) persistent_decode_ready();
   if (decode_exec_) {
     cudaGraphExecDestroy(decode_exec_);
     decode_exec_ = nullptr;
@@ -593,6 +727,7 @@ void Engine::capture_decode_graph() {
   graph_capture_layer_ = capture_layer_;
   graph_edit_layer_ = edit_layer_;
   graph_mode_ = mode_;
+  graph_path_ = decode_path_;
 }
 
 void Engine::generate(const uint32_t* prompt, size_t n_prompt, size_t max_new, const dl_sampling& s,

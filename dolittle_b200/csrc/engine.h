@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "../../include/dolittle_b200.h"
+#include "decode_persistent.h"
 #include "gemv.cuh"
 #include "launch.h"
 #include "sampler.h"
@@ -34,7 +35,9 @@ struct DeviceState {
   unsigned terminal;   // stop ID or error latched
   unsigned err;        // kernel error word
   unsigned ticket;     // argmax completion counter
-  unsigned pad[9];
+  unsigned barrier;    // persistent decode: grid barrier arrivals
+  unsigned exit_ticket;
+  unsigned pad[7];
 };
 
 class Engine {
@@ -80,6 +83,8 @@ class Engine {
   void project(const bf16* x, int x_stride, int rows, int in_width, int prologue, const bf16* norm_w,
                int epilogue, GemvSegment* segs, int nseg, bool pdl);
   void capture_decode_graph();
+  bool persistent_decode_ready();
+  void launch_persistent_step(bool greedy);
   void check(cudaError_t e, const char* what);
   void check_fault();
 
@@ -125,6 +130,15 @@ class Engine {
   int mode_ = 0, graph_mode_ = -1;
   Sampler sampler_;
   cudaEvent_t ev_[4] = {};
+  // persistent decode step (one cooperative launch per token)
+  int decode_path_ = DL_DECODE_PERSISTENT, graph_path_ = -1;
+  int persist_state_ = -1;  // -1 not planned, 0 unsupported, 1 ready
+  PLayer* persist_layers_ = nullptr;
+  CUtensorMap* persist_maps_ = nullptr;
+  PGemv persist_head_ = {};
+
+ public:
+  void set_decode_path(int path);
 };
 
 }  // namespace dl

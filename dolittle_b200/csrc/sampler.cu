@@ -435,6 +435,12 @@ cudaError_t sampler_submit(Sampler& s, const void* row, const dl_sampling& st, u
   return cudaGetLastError();
 }
 
+int sampler_launch_count(const Sampler& s, const dl_sampling& st, bool owned) {
+  const int radix_passes = s.bf16_input ? 2 : 4;
+  const int body = st.mode == 0 ? 1 : 1 + 3 * radix_passes + 5;
+  return body + (owned ? 2 : 0);
+}
+
 cudaError_t sampler_feed(Sampler& s, unsigned* history, int* step, const bf16* embed, bf16* residual, int width,
                          long long* position, cudaStream_t stream) {
   feed_kernel<<<1, 256, 0, stream>>>(s.result, history, step, embed, residual, width, position);

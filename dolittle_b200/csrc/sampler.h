@@ -37,6 +37,8 @@ cudaError_t sampler_start(Sampler& s, const dl_sampling& settings, uint64_t seed
 // owned = device-owned MT stream (submit_next); otherwise `bits` is the draw.
 cudaError_t sampler_submit(Sampler& s, const void* row, const dl_sampling& settings, uint64_t bits, bool owned,
                            cudaStream_t stream);
+// Kernels one sampler_submit enqueues (for launch accounting).
+int sampler_launch_count(const Sampler& s, const dl_sampling& settings, bool owned);
 // After a selection: history[*step] = token, ++*step, residual = embed[token],
 // ++*position (each optional).
 cudaError_t sampler_feed(Sampler& s, unsigned* history, int* step, const bf16* embed, bf16* residual,

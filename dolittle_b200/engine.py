@@ -156,6 +156,11 @@ class Engine:
         check(lib().dl_engine_set_intervention(self._h, layer, selected, strength,
                                                d.ctypes.data_as(C.POINTER(C.c_float))))
 
+    def set_decode_path(self, path: int) -> None:
+        """DL_DECODE_PERSISTENT (one cooperative kernel per token) or
+        DL_DECODE_KERNELS (per-operation kernels); the results are identical."""
+        check(lib().dl_engine_set_decode_path(self._h, path))
+
     def read_kv(self, layer: int, values: bool, first: int, count: int) -> np.ndarray:
         g = self.config.kv_heads * self.config.head_width
         out = np.empty((count, g), np.uint16)

@@ -209,6 +209,11 @@ typedef struct {
 } dl_generation_stats;
 
 enum { DL_PREFILL_PARITY = 0, DL_PREFILL_FAST = 1 };
+/* Decode step implementation (identical results): one persistent
+ * cooperative kernel per token (default; falls back to the per-operation
+ * kernels when the model shape or device does not fit it), or the
+ * per-operation kernels captured in the step graph. */
+enum { DL_DECODE_PERSISTENT = 0, DL_DECODE_KERNELS = 1 };
 
 /* Tensors are addressed by index: 0 embedding [V][D], 1 final norm [D],
  * 2 lm_head [V][D], then 3 + 11*block + role with roles input_norm, q, k,
@@ -247,6 +252,7 @@ DL_API dl_status dl_engine_read_capture(dl_engine* e, size_t first, size_t count
 /* One-shot steering edit at block `layer`, absolute row `selected`. */
 DL_API dl_status dl_engine_set_intervention(dl_engine* e, int layer, size_t selected,
                                             float strength, const float* host_direction);
+DL_API dl_status dl_engine_set_decode_path(dl_engine* e, int path);
 DL_API dl_status dl_engine_read_kv(dl_engine* e, size_t layer, int values, size_t first,
                                    size_t count, uint16_t* host);
 /* Live generation: prompt pass, first selection, then decode steps replayed
