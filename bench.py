@@ -239,6 +239,19 @@ def dominant_kernel_roofline(engine, cfg, hbm, kind):
             "bytes_per_launch": algo, "ms_per_launch": ms, "peak_kind": kind}
 
 
+def persistent_traffic(bytes_per_launch):
+    """DRAM read+write bytes per persistent decode launch, from the committed
+    ncu capture (profiles/decode_persistent_traffic.json): the measured
+    traffic / algorithmic bytes ratio of a smaller case, scaled to this
+    launch's algorithmic bytes (traffic grows with the weights streamed)."""
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", "decode_persistent_traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        rec = json.load(f)
+    return bytes_per_launch * rec["traffic_bytes"] / rec["algorithmic_bytes"]
+
+
 def run_ours(args):
     world, rank, local = dist_setup()
     import torch
@@ -293,10 +306,17 @@ def run_ours(args):
     roof = None
     cpu = None
     if rank == 0:
-        roof = dominant_kernel_roofline(engine, cfg, hbm, kind)
-        roof["decode_step_gbs"] = bytes_step * per_rank / 1e9
-        roof["decode_step_frac"] = roof["decode_step_gbs"] / hbm
-        roof["decode_step_frac_of_8tbs"] = roof["decode_step_gbs"] / 8000.0
+        # Dominant kernel: the persistent decode step, one launch per token,
+        # timed by the engine's CUDA events on its own stream over the decode loop.
+        ms_launch = 1000 * decode_s / (args.steps * steps_decoded)
+        achieved = bytes_step / (ms_launch * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                "traffic": persistent_traffic(bytes_step),
+                "kernel": "decode_persistent_kernel (one cooperative launch per decode token)"
+                          if gens[0].kernels_per_decode_step == 1 else "per-operation decode kernels",
+                "bytes_per_launch": bytes_step, "ms_per_launch": ms_launch, "peak_kind": kind,
+                "frac_of_8tbs": achieved / 8000.0}
+        roof["gemv_gate_up"] = dominant_kernel_roofline(engine, cfg, hbm, kind)
         if world == 1 and not args.no_cpu_baseline:
             def from_engine(ocfg):
                 return [engine.get_tensor(i) for i in range(cfg.tensor_count())]
@@ -361,6 +381,14 @@ def run_profile_case(args):
                                           None) == 0
         torch.cuda.synchronize()
         print("profile gemv ok")
+    elif args.profile == "persist":
+        # Four full-width blocks, full vocabulary: one persistent launch per
+        # decode step over ~4 GB of resident weights.
+        cfg = dl.Qwen3Config(layers=4)
+        e = dl.Engine(cfg, capacity=64, max_rows=16)
+        e.init_random(SEED, 0.02)
+        g = e.generate(prompt_ids(cfg.vocabulary)[:16], 3)
+        print("profile persist ok", g.tokens, g.kernels_per_decode_step)
     elif args.profile == "prefill":
         cfg = dl.QWEN3_8B
         e = dl.Engine(cfg, capacity=PROMPT + 8, max_rows=PROMPT)
@@ -385,7 +413,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill", choices=["fast", "parity"], default="fast",
                     help="prompt pass on the tcgen05 GEMMs (fast) or in the reference order (parity)")
-    ap.add_argument("--profile", choices=["gemv", "decode", "prefill"], default=None,
+    ap.add_argument("--profile", choices=["gemv", "decode", "prefill", "persist"], default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
     args = ap.parse_args()
     if args.profile:
