@@ -15,7 +15,8 @@ constexpr int kConsumerWarps = kGemvConsumers / 32;
 constexpr long long kSpinLimit = 1ll << 32;  // ~2 s of SM cycles
 constexpr int kMaxInput8 = kPersistMaxInput / 8 / kGemvConsumers;  // 16-byte input loads per thread
 constexpr int kMaxNorm8 = kPersistMaxNormInput / 8 / kGemvConsumers;
-constexpr int kScoreScratch = (8 * 128 + 128 + 8 * 128) * 4;  // qs, ks, norm_vals of a score unit
+// Score unit scratch: qs, ks, norm_vals (FP32) and the raw q / k rows (BF16).
+constexpr int kScoreScratch = (8 * 128 + 128 + 8 * 128) * 4 + 8 * 128 * 2;
 
 // RMSNorm apply (two rounding points, normalization.cu:82-186) on 8 packed
 // BF16 features.
@@ -48,9 +49,13 @@ struct PHeader {
   unsigned sync_ok;
   unsigned pf_req;         // consumer-requested L2 prefetch bursts
   alignas(16) unsigned char desc[2][256];  // phase descriptors, fetched one phase ahead
+  alignas(16) const bf16* attn[2][4];      // per block: q_norm, k_norm, k_cache, v_cache
+  float rope[64][2];                       // RoPE cos, sin (storage-rounded) at this step's position
 };
 static_assert(sizeof(PHeader) <= kPersistHeaderBytes, "persistent header too large");
 static_assert(sizeof(PGemv) <= 256 && sizeof(PGemv) % 16 == 0, "phase descriptor size");
+static_assert(offsetof(PLayer, q_norm) % 16 == 0 && offsetof(PLayer, v_cache) == offsetof(PLayer, q_norm) + 24,
+              "attention operands are copied as 32 contiguous bytes");
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
@@ -433,39 +438,54 @@ __device__ void gemv_phase(const PersistArgs& a, const PGemv& ph, unsigned char*
 // Scores of one (GQA group g, key slice) unit: QK-norm + RoPE of the group's
 // query heads (warps 0..group-1) and the new key (warp 7), the new key into
 // the K cache by the slice that holds it, then the scaled scores.
-__device__ void score_unit(const PersistArgs& a, const PLayer& L, int g, int slice, int S, unsigned char* uni) {
+__device__ void score_unit(const PersistArgs& a, const bf16* const* ap, int g, int slice, int S, unsigned char* uni,
+                           const PHeader* h) {
   float(*qs)[128] = reinterpret_cast<float(*)[128]>(uni);
   float* ks = reinterpret_cast<float*>(uni + 8 * 128 * 4);
   float(*norm_vals)[128] = reinterpret_cast<float(*)[128]>(uni + 8 * 128 * 4 + 128 * 4);
+  bf16* raw = reinterpret_cast<bf16*>(uni + (8 * 128 + 128 + 8 * 128) * 4);  // [8][128]: q heads, key in row 7
+  const bf16* q_norm = ap[0];
+  const bf16* k_norm = ap[1];
+  bf16* k_cache = const_cast<bf16*>(ap[2]);
   const int width = a.width, kv_heads = a.kv_heads, group = a.query_heads / kv_heads;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int count = S + 1;
   const int per = (count + a.score_slices - 1) / a.score_slices;
   const int j0 = slice * per, j1 = min(count, j0 + per);
   const bool owns_new_key = S >= j0 && S < j1;
-  // The slice's cached keys go to shared memory while the norms run (the
-  // new key S comes from ks).
+  // One round of asynchronous copies: the group's raw q rows, the raw key and
+  // the slice's cached keys (the new key S comes from ks).
   bf16* kslice = reinterpret_cast<bf16*>(uni + kScoreScratch);
   const int nkeys = max(0, j1 - j0);
   const bool staged = width % 8 == 0 && nkeys * width * 2 <= kPersistUnionBytes - kScoreScratch;
+  const int chunks = width / 8;
+  const bool raw_staged = width % 8 == 0;
+  if (raw_staged) {
+    for (int idx = threadIdx.x; idx < (group + 1) * chunks; idx += kGemvConsumers) {
+      const int r = idx / chunks, q = idx % chunks;
+      const bf16* src = r < group ? a.q_raw + size_t(g * group + r) * width : a.k_raw + size_t(g) * width;
+      cp_async16(raw + (r < group ? r : 7) * 128 + 8 * q, src + 8 * q);
+    }
+  }
   if (staged) {
-    const int chunks = width / 8;
     for (int idx = threadIdx.x; idx < nkeys * chunks; idx += kGemvConsumers) {
       const int j = idx / chunks, q = idx % chunks;
       if (j0 + j != S)
-        cp_async16(kslice + size_t(j) * width + 8 * q, L.k_cache + (size_t(j0 + j) * kv_heads + g) * width + 8 * q);
+        cp_async16(kslice + size_t(j) * width + 8 * q, k_cache + (size_t(j0 + j) * kv_heads + g) * width + 8 * q);
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
   }
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory");
+  named_sync(1, kGemvConsumers);
   if (warp < group || warp == 7) {
     const bool is_q = warp < group;
-    const bf16* src = is_q ? a.q_raw + size_t(g * group + warp) * width : a.k_raw + size_t(g) * width;
-    const bf16* w = is_q ? L.q_norm : L.k_norm;
+    const bf16* src = raw_staged ? raw + warp * 128
+                                 : (is_q ? a.q_raw + size_t(g * group + warp) * width : a.k_raw + size_t(g) * width);
+    const bf16* w = is_q ? q_norm : k_norm;
     float x[4], part[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const int col = lane + 32 * c;
-      x[c] = col < width ? widen(__ldcg(src + col)) : 0.f;
+      x[c] = col < width ? widen(raw_staged ? src[col] : __ldcg(src + col)) : 0.f;
       if (col < width) part[c] = __fmul_rn(x[c], x[c]);
     }
     float sum = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), part[2]), part[3]);
@@ -482,21 +502,19 @@ __device__ void score_unit(const PersistArgs& a, const PLayer& L, int g, int sli
     const int half = width / 2;
     float* dst = is_q ? qs[warp] : ks;
     for (int f = lane; f < half; f += 32) {
-      const float angle = __fmul_rn(static_cast<float>(S), a.inv_freq[f]);
-      const float co = round_bf16(cosf(angle)), si = round_bf16(sinf(angle));
+      const float co = h->rope[f][0], si = h->rope[f][1];
       const float va = nv[f], vb = nv[f + half];
       const float lo = round_bf16(__fsub_rn(round_bf16(__fmul_rn(va, co)), round_bf16(__fmul_rn(vb, si))));
       const float hi = round_bf16(__fadd_rn(round_bf16(__fmul_rn(vb, co)), round_bf16(__fmul_rn(va, si))));
       dst[f] = lo;
       dst[f + half] = hi;
       if (!is_q && owns_new_key) {
-        bf16* kc = L.k_cache + (size_t(S) * kv_heads + g) * width;
+        bf16* kc = k_cache + (size_t(S) * kv_heads + g) * width;
         kc[f] = narrow(lo);
         kc[f + half] = narrow(hi);
       }
     }
   }
-  if (staged) asm volatile("cp.async.wait_all;" ::: "memory");
   named_sync(1, kGemvConsumers);
   const int lane8 = threadIdx.x & 7;
   const int span = width / 8 + (width % 8 != 0);
@@ -519,7 +537,7 @@ __device__ void score_unit(const PersistArgs& a, const PLayer& L, int g, int sli
           w0 = sld16(kr);
           w1 = sld16(kr + 8);
         } else {
-          const uint4* kr = reinterpret_cast<const uint4*>(L.k_cache + (size_t(j) * kv_heads + g) * width + begin);
+          const uint4* kr = reinterpret_cast<const uint4*>(k_cache + (size_t(j) * kv_heads + g) * width + begin);
           w0 = __ldcg(kr);
           w1 = __ldcg(kr + 1);
         }
@@ -537,7 +555,7 @@ __device__ void score_unit(const PersistArgs& a, const PLayer& L, int g, int sli
         }
       }
     } else if (live) {
-      const bf16* kr = L.k_cache + (size_t(j) * kv_heads + g) * width;
+      const bf16* kr = k_cache + (size_t(j) * kv_heads + g) * width;
       const bf16* kl = kslice + size_t(j - j0) * width;
       for (int hh = 0; hh < group; ++hh) {
         float acc = 0.f;
@@ -566,7 +584,7 @@ __device__ void score_unit(const PersistArgs& a, const PLayer& L, int g, int sli
 // e = expf(s - max) + the shuffle-down tree, p = e / den.  The two
 // contiguous key halves are serial chains per feature, added once.  Keys are
 // staged in chunks (V slice and p) so any capacity fits the scratch.
-__device__ void pv_unit(const PersistArgs& a, const PLayer& L, int g, int f0, int S, unsigned char* uni,
+__device__ void pv_unit(const PersistArgs& a, const bf16* const* ap, int g, int f0, int S, unsigned char* uni,
                         PHeader* h) {
   const int width = a.width, kv_heads = a.kv_heads, group = a.query_heads / kv_heads;
   const int fpc = a.pv_features;
@@ -597,7 +615,7 @@ __device__ void pv_unit(const PersistArgs& a, const PLayer& L, int g, int f0, in
     }
     for (int idx = t; idx < count * vchunks; idx += kGemvConsumers) {
       const int j = idx / vchunks, q = idx % vchunks;
-      cp_async16(vs + size_t(j) * fpc + 8 * q, L.v_cache + (size_t(j) * kv_heads + g) * width + f0 + 8 * q);
+      cp_async16(vs + size_t(j) * fpc + 8 * q, ap[3] + (size_t(j) * kv_heads + g) * width + f0 + 8 * q);
     }
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory");
     named_sync(1, kGemvConsumers);
@@ -675,7 +693,7 @@ __device__ void pv_unit(const PersistArgs& a, const PLayer& L, int g, int f0, in
     const int n = min(chunk, count - c0);
     for (int idx = t; idx < n * vchunks; idx += kGemvConsumers) {
       const int j = idx / vchunks, q = idx % vchunks;
-      cp_async16(vs + size_t(j) * fpc + 8 * q, L.v_cache + (size_t(c0 + j) * kv_heads + g) * width + f0 + 8 * q);
+      cp_async16(vs + size_t(j) * fpc + 8 * q, ap[3] + (size_t(c0 + j) * kv_heads + g) * width + f0 + 8 * q);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
     for (int idx = t; idx < group * n; idx += kGemvConsumers) {
@@ -866,6 +884,9 @@ __device__ __forceinline__ void consumer_main(const PersistArgs& a, unsigned cha
     const PGemv* src = p == 0 ? &Lx.qkv : p == 1 ? &Lx.o : p == 2 ? &Lx.gu : &Lx.down;
     if (threadIdx.x < int(sizeof(PGemv) / 16))
       cp_async16(h->desc[idx & 1] + 16 * threadIdx.x, reinterpret_cast<const unsigned char*>(src) + 16 * threadIdx.x);
+    else if (p == 0 && threadIdx.x < int(sizeof(PGemv) / 16) + 2)
+      cp_async16(reinterpret_cast<unsigned char*>(h->attn[(idx >> 2) & 1]) + 16 * (threadIdx.x - sizeof(PGemv) / 16),
+                 reinterpret_cast<const unsigned char*>(&Lx.q_norm) + 16 * (threadIdx.x - sizeof(PGemv) / 16));
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
   const int nproj = 4 * a.nlayers;
@@ -876,6 +897,12 @@ __device__ __forceinline__ void consumer_main(const PersistArgs& a, unsigned cha
     return *reinterpret_cast<const PGemv*>(h->desc[idx & 1]);
   };
   fetch_desc(0);
+  // RoPE factors of this step's position, once per launch (rotary.cu:84-126).
+  for (int f = threadIdx.x; f < a.width / 2; f += kGemvConsumers) {
+    const float angle = __fmul_rn(static_cast<float>(S), a.inv_freq[f]);
+    h->rope[f][0] = round_bf16(cosf(angle));
+    h->rope[f][1] = round_bf16(sinf(angle));
+  }
   auto sync = [&] {
     if (aborted) return;
     target += gridDim.x;
@@ -888,17 +915,16 @@ __device__ __forceinline__ void consumer_main(const PersistArgs& a, unsigned cha
     }
   };
   for (int l = 0; l < a.nlayers && !aborted; ++l) {
-    const PLayer& L = a.layers[l];
     gemv_phase(a, desc(4 * l), uni, ring, h, g, failed, nullptr, none);
     sync();
     if (aborted) break;
     if (threadIdx.x == 0 && a.prefetch_stages > 0) vstore(&h->pf_req, vload(&h->pf_req) + 1);
     for (int u = blockIdx.x; u < score_units; u += gridDim.x)
-      score_unit(a, L, u % a.kv_heads, u / a.kv_heads, int(S), uni);
+      score_unit(a, h->attn[l & 1], u % a.kv_heads, u / a.kv_heads, int(S), uni, h);
     sync();
     if (aborted) break;
     for (int u = blockIdx.x; u < pv_units; u += gridDim.x)
-      pv_unit(a, L, u / fslices, (u % fslices) * a.pv_features, int(S), uni, h);
+      pv_unit(a, h->attn[l & 1], u / fslices, (u % fslices) * a.pv_features, int(S), uni, h);
     sync();
     if (aborted) break;
     gemv_phase(a, desc(4 * l + 1), uni, ring, h, g, failed, nullptr, none);

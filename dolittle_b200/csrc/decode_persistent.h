@@ -35,8 +35,8 @@ namespace dl {
 
 constexpr int kPersistSlots = 6;
 constexpr int kPersistSlotBytes = 32 * 1024;
-constexpr int kPersistHeaderBytes = 1024;
-constexpr int kPersistUnionBytes = 31 * 1024;  // x row, or attention scratch
+constexpr int kPersistHeaderBytes = 2048;
+constexpr int kPersistUnionBytes = 30 * 1024;  // x row, or attention scratch
 constexpr int kPersistSmem =
     kPersistHeaderBytes + kPersistUnionBytes + 1024 /* ring alignment */ + kPersistSlots * kPersistSlotBytes;
 constexpr int kPersistMaxInput = 12288;     // projection input width (features)
@@ -60,6 +60,7 @@ struct alignas(16) PGemv {
 
 struct PLayer {
   PGemv qkv, o, gu, down;
+  // Attention operands (16-byte aligned: copied to shared memory together).
   const bf16* q_norm;
   const bf16* k_norm;
   bf16* k_cache;
