@@ -56,6 +56,8 @@ SIGNATURES = {
     "dl_attention_scale": (C.c_int, [vp, sz, vp]),
     "dl_attention_workspace_bytes": (sz, [sz, sz, sz]),
     "dl_attention": (C.c_int, [C.c_int, vp, vp, vp, vp, sz, sz, sz, sz, vp, sz, vp, sz, vp, vp]),
+    "dl_attention_prefill_fast_workspace_bytes": (sz, [sz, sz, sz]),
+    "dl_attention_prefill_fast": (C.c_int, [vp, vp, vp, vp, sz, sz, sz, sz, vp, sz, sz, vp]),
     "dl_attention_fixed_scratch": (C.c_int, [C.c_int, vp, vp, vp, vp, sz, sz, sz, sz, vp, sz, vp, sz]),
     "dl_embedding": (C.c_int, [C.c_int, vp, vp, vp, sz, sz, vp]),
     "dl_add": (C.c_int, [C.c_int, vp, vp, vp, sz, vp]),

@@ -1,0 +1,356 @@
+// Causal GQA prompt attention on the 5th-generation tensor cores, for the
+// fast prompt pass (tensor-core accumulation order, checked against the
+// reference-order path within tolerance like the tcgen05 GEMMs).
+//
+// One CTA (4 warps) owns 128 query rows of one query head.  Key blocks of 128
+// are visited twice:
+//   pass 1: S = Q K^T (tcgen05.mma, M = N = 128, K = 128 over the head width)
+//           into TMEM; each thread (one query row = one TMEM lane) reads its
+//           row and keeps the running maximum m and sum l of exp2(s - m);
+//   pass 2: S again; p = exp2(s - m) / l, rounded to BF16 and written to
+//           shared memory as a 128-byte-swizzled K-major tile, then
+//           O += P V^T^T (tcgen05.mma with A = P, B = V^T) in TMEM.
+// Scores carry the softmax scale times log2(e); keys beyond the row's
+// position are masked.  Q and K come in by TMA straight from the rotated
+// queries and the K cache; V is read as V^T from a per-block transposed copy
+// (launch_vt_transpose) so both operands of both products are K-major.
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <mutex>
+
+#include "attention_prefill_tc.h"
+#include "tcgen05.cuh"
+
+namespace dl {
+namespace {
+
+using namespace tc;
+
+constexpr int kTile = 128;                    // query rows per CTA, keys per block
+constexpr int kThreads = 128;
+constexpr int kAtomBytes = kTile * 64 * 2;    // [128 rows][64 BF16], one swizzle atom column
+constexpr int kTileBytes = 2 * kAtomBytes;    // [128 rows][128 BF16]
+constexpr int kSmem = 4 * kTileBytes + 1024;  // Q, K, V^T, P + alignment
+constexpr uint32_t kTmemCols = 256;           // S (128 columns) + O (128 columns)
+
+struct alignas(64) AttnArgs {
+  CUtensorMap map_q;   // {d, Hq, rows}: box {64, 1, 128}
+  CUtensorMap map_k;   // {d, Hkv, C, 2L}: box {64, 1, 128, 1}; K of block l at index 2l
+  CUtensorMap map_vt;  // {keys, d, Hkv}: box {64, 128, 1}
+  bf16* out;           // [rows][Hq * d]
+  int rows, layer, query_heads, kv_heads;
+  long long first;     // absolute position of query row 0
+  float scale_log2;    // softmax scale * log2(e)
+  unsigned* err;
+};
+
+__device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load4(void* dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+      "%5}], [%6];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// 8 MMAs of K = 16 across the two swizzle atoms of a 128-wide K dimension.
+__device__ __forceinline__ void mma_tile(uint32_t tmem_d, const unsigned char* a_tile, const unsigned char* b_tile,
+                                         bool accumulate) {
+  constexpr uint32_t idesc = instr_desc_bf16(kTile, kTile);
+  const uint32_t sa = smem_addr(a_tile), sb = smem_addr(b_tile);
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const uint32_t atom = uint32_t(kk >> 2) * kAtomBytes;
+    const uint64_t off = uint64_t((kk & 3) * 2);
+    mma_bf16(tmem_d, smem_desc_sw128(sa + atom) + off, smem_desc_sw128(sb + atom) + off, idesc,
+             (accumulate || kk) ? 1u : 0u);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const __grid_constant__ AttnArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ uint64_t tma_bar, mma_bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  const uint32_t base_s = (smem_addr(smem_raw) + 1023u) & ~1023u;
+  unsigned char* sq = smem_raw + (base_s - smem_addr(smem_raw));
+  unsigned char* sk = sq + kTileBytes;
+  unsigned char* svt = sk + kTileBytes;
+  unsigned char* sp = svt + kTileBytes;
+  const int warp = threadIdx.x >> 5;
+  const int hq = blockIdx.y;
+  const int g = hq / (a.query_heads / a.kv_heads);
+  const int q0 = blockIdx.x * kTile;
+  const int r = threadIdx.x;  // row within the tile = TMEM lane
+  const int row = q0 + r;
+  const bool live = row < a.rows;
+  const long long pos = a.first + row;
+  const long long last_pos = a.first + min(a.rows, q0 + kTile) - 1;
+  const int nkb = int(last_pos / kTile) + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&tma_bar, 1);
+    mbar_init(&mma_bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_base, kTmemCols);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = tmem_base;
+  const uint32_t t_s = tmem, t_o = tmem + 128;
+  const uint32_t lane_base = uint32_t(warp * 32) << 16;
+
+  float m = -INFINITY, l = 0.f;
+  unsigned tma_phase = 0, mma_phase = 0;
+  for (int pass = 0; pass < 2; ++pass) {
+    for (int kb = 0; kb < nkb; ++kb) {
+      // Operands of this block, then S = Q K^T.
+      if (threadIdx.x == 0 && !abort_flag) {
+        const bool with_q = pass == 0 && kb == 0;
+        mbar_arrive_expect_tx(&tma_bar, unsigned(kTileBytes) * (1 + (with_q ? 1 : 0) + (pass ? 1 : 0)));
+        if (with_q) {
+          tma_load(sq, &a.map_q, 0, hq, q0, &tma_bar);
+          tma_load(sq + kAtomBytes, &a.map_q, 64, hq, q0, &tma_bar);
+        }
+        tma_load4(sk, &a.map_k, 0, g, kb * kTile, 2 * a.layer, &tma_bar);
+        tma_load4(sk + kAtomBytes, &a.map_k, 64, g, kb * kTile, 2 * a.layer, &tma_bar);
+        if (pass) {
+          tma_load(svt, &a.map_vt, kb * kTile, 0, g, &tma_bar);
+          tma_load(svt + kAtomBytes, &a.map_vt, kb * kTile + 64, 0, g, &tma_bar);
+        }
+        if (!mbar_wait(&tma_bar, tma_phase)) {
+          record_error(a.err, kErrWaitFull);
+          abort_flag = 1;
+        } else {
+          fence_after_sync();
+          mma_tile(t_s, sq, sk, false);
+          mma_commit(&mma_bar);
+        }
+      }
+      tma_phase ^= 1;
+      __syncthreads();  // abort decision is uniform
+      if (abort_flag) break;
+      if (!mbar_wait(&mma_bar, mma_phase)) {
+        record_error(a.err, kErrWaitFull);
+        abort_flag = 1;
+      }
+      mma_phase ^= 1;
+      fence_after_sync();
+      const int key0 = kb * kTile;
+      if (pass == 0) {
+        // Running max and sum of exp2 over this block's keys.
+        float bm = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t s[32];
+          tmem_ld32(t_s + lane_base + uint32_t(c * 32), s);
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (key0 + c * 32 + i <= pos) bm = fmaxf(bm, __uint_as_float(s[i]) * a.scale_log2);
+        }
+        // TMEM loads are warp-collective: every lane loads, only the
+        // arithmetic is guarded.
+        const float mn = fmaxf(m, bm);
+        const bool use = live && mn != -INFINITY;
+        float sum = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t s[32];
+          tmem_ld32(t_s + lane_base + uint32_t(c * 32), s);
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (use && key0 + c * 32 + i <= pos) sum += exp2f(__uint_as_float(s[i]) * a.scale_log2 - mn);
+        }
+        if (use) {
+          l = (m == -INFINITY ? 0.f : l * exp2f(m - mn)) + sum;
+          m = mn;
+        }
+        fence_before_sync();
+        __syncthreads();  // S is rewritten by the next block's MMA
+      } else {
+        // P = exp2(s - m) / l as BF16 into the swizzled K-major tile.
+        const float inv_l = (live && l > 0.f) ? 1.0f / l : 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t s[32];
+          tmem_ld32(t_s + lane_base + uint32_t(c * 32), s);
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const int k0 = key0 + c * 32 + i;
+            const float p0 = (live && k0 <= pos) ? exp2f(__uint_as_float(s[i]) * a.scale_log2 - m) * inv_l : 0.f;
+            const float p1 =
+                (live && k0 + 1 <= pos) ? exp2f(__uint_as_float(s[i + 1]) * a.scale_log2 - m) * inv_l : 0.f;
+            const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+            packed[i / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+          }
+          // Keys c*32 .. c*32+31 of the block: atom c / 2, chunks (c % 2) * 4 .. + 3.
+          unsigned char* rowp = sp + (c >> 1) * kAtomBytes + r * 128;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int chunk = (c & 1) * 4 + q;
+            *reinterpret_cast<uint4*>(rowp + ((chunk ^ (r & 7)) << 4)) =
+                make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          }
+        }
+        fence_proxy_async_smem();
+        fence_before_sync();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+          fence_after_sync();
+          mma_tile(t_o, sp, svt, kb > 0);
+          mma_commit(&mma_bar);
+        }
+        if (!mbar_wait(&mma_bar, mma_phase)) {
+          record_error(a.err, kErrWaitFull);
+          abort_flag = 1;
+        }
+        mma_phase ^= 1;
+        fence_after_sync();
+        __syncthreads();
+      }
+    }
+    if (abort_flag) break;
+  }
+  if (!abort_flag) {  // uniform: every lane takes part in the TMEM loads
+    bf16* out = a.out + size_t(live ? row : 0) * (size_t(a.query_heads) * 128) + size_t(hq) * 128;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t o[32];
+      tmem_ld32(t_o + lane_base + uint32_t(c * 32), o);
+      if (!live) continue;
+      uint32_t packed[16];
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const __nv_bfloat162 h2 = __floats2bfloat162_rn(__uint_as_float(o[i]), __uint_as_float(o[i + 1]));
+        packed[i / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+    }
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+}
+
+// V^T of one block's cache: vt[g][f][j] = v[j][g][f] for j < keys.
+__global__ void vt_transpose_kernel(const bf16* __restrict__ v, bf16* __restrict__ vt, int keys, int kv_heads,
+                                    int width, int vt_stride) {
+  __shared__ bf16 tile[32][33];
+  const int g = blockIdx.z;
+  const int j0 = blockIdx.x * 32, f0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int j = j0 + i, f = f0 + threadIdx.x;
+    if (j < keys && f < width) tile[i][threadIdx.x] = v[(size_t(j) * kv_heads + g) * width + f];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int f = f0 + i, j = j0 + threadIdx.x;
+    if (j < keys && f < width) vt[(size_t(g) * width + f) * vt_stride + j] = tile[threadIdx.x][i];
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+bool encode(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
+            const cuuint32_t* box) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides_bytes, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+struct AttnTcMaps {
+  CUtensorMap q, k, vt;
+};
+
+bool attention_prefill_tc_supported(int query_heads, int kv_heads, int width) {
+  return width == 128 && kv_heads > 0 && query_heads % kv_heads == 0;
+}
+
+AttnTcMaps* attention_prefill_tc_maps(const bf16* q, int max_rows, int query_heads, const bf16* kv_arena,
+                                      size_t kv_block_bytes, int capacity, int layers, int kv_heads, int width,
+                                      const bf16* vt, int vt_stride) {
+  if (!attention_prefill_tc_supported(query_heads, kv_heads, width) || kv_block_bytes % 16 || vt_stride % 64)
+    return nullptr;
+  auto* m = new AttnTcMaps;
+  const cuuint64_t qd[3] = {uint64_t(width), uint64_t(query_heads), uint64_t(max_rows)};
+  const cuuint64_t qs[2] = {uint64_t(width) * 2, uint64_t(query_heads) * width * 2};
+  const cuuint32_t qb[3] = {64, 1, 128};
+  const cuuint64_t kd[4] = {uint64_t(width), uint64_t(kv_heads), uint64_t(capacity), uint64_t(2 * layers)};
+  const cuuint64_t ks[3] = {uint64_t(width) * 2, uint64_t(kv_heads) * width * 2, kv_block_bytes};
+  const cuuint32_t kb[4] = {64, 1, 128, 1};
+  const cuuint64_t vd[3] = {uint64_t(vt_stride), uint64_t(width), uint64_t(kv_heads)};
+  const cuuint64_t vs[2] = {uint64_t(vt_stride) * 2, uint64_t(width) * vt_stride * 2};
+  const cuuint32_t vb[3] = {64, 128, 1};
+  if (!encode(&m->q, q, 3, qd, qs, qb) || !encode(&m->k, kv_arena, 4, kd, ks, kb) ||
+      !encode(&m->vt, vt, 3, vd, vs, vb)) {
+    delete m;
+    return nullptr;
+  }
+  return m;
+}
+
+void attention_prefill_tc_free(AttnTcMaps* m) { delete m; }
+
+cudaError_t launch_vt_transpose(const bf16* v_cache, bf16* vt, int keys, int kv_heads, int width, int vt_stride,
+                                cudaStream_t stream) {
+  if (keys <= 0) return cudaSuccess;
+  dim3 grid((keys + 31) / 32, (width + 31) / 32, kv_heads);
+  vt_transpose_kernel<<<grid, dim3(32, 8), 0, stream>>>(v_cache, vt, keys, kv_heads, width, vt_stride);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attention_prefill_tc(const AttnTcMaps* maps, bf16* out, int rows, long long first, int layer,
+                                        int query_heads, int kv_heads, float scale, unsigned* err,
+                                        cudaStream_t stream) {
+  if (!maps || rows <= 0) return cudaErrorInvalidValue;
+  AttnArgs a = {};
+  a.map_q = maps->q;
+  a.map_k = maps->k;
+  a.map_vt = maps->vt;
+  a.out = out;
+  a.rows = rows;
+  a.first = first;
+  a.layer = layer;
+  a.query_heads = query_heads;
+  a.kv_heads = kv_heads;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.err = err;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(attention_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  });
+  attention_prefill_tc_kernel<<<dim3((rows + kTile - 1) / kTile, query_heads), kThreads, kSmem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace dl

@@ -10,6 +10,7 @@
 #include <string>
 
 #include "../../include/dolittle_b200.h"
+#include "attention_prefill_tc.h"
 #include "engine.h"
 #include "gemm_tcgen05.h"
 #include "gemv.cuh"
@@ -128,6 +129,38 @@ DL_API dl_status dl_attention_scale(float* output, size_t width, void* stream) {
 
 DL_API size_t dl_attention_workspace_bytes(size_t positions, size_t query_heads, size_t capacity) {
   return positions * query_heads * capacity * sizeof(float);
+}
+
+DL_API size_t dl_attention_prefill_fast_workspace_bytes(size_t kv_heads, size_t width, size_t capacity) {
+  return kv_heads * width * ((capacity + 63) / 64 * 64) * 2;
+}
+
+DL_API dl_status dl_attention_prefill_fast(const void* query, const void* key, const void* value, void* output,
+                                           size_t positions, size_t query_heads, size_t kv_heads, size_t width,
+                                           void* stream, size_t first_position, size_t capacity,
+                                           void* workspace) {
+  if (!query || !key || !value || !output || !workspace || !positions || !kv_heads)
+    return fail(DL_INVALID_ARGUMENT, "attention prefill: arguments");
+  if (!dl::attention_prefill_tc_supported(int(query_heads), int(kv_heads), int(width)))
+    return fail(DL_UNSUPPORTED, "attention prefill: head width 128 and whole GQA groups required");
+  if (first_position + positions > capacity) return fail(DL_INVALID_ARGUMENT, "attention prefill: keys > capacity");
+  const int vt_stride = int((capacity + 63) / 64 * 64);
+  dl::AttnTcMaps* maps = dl::attention_prefill_tc_maps(
+      static_cast<const bf16*>(query), int(positions), int(query_heads), static_cast<const bf16*>(key),
+      capacity * kv_heads * width * 2, int(capacity), 1, int(kv_heads), int(width),
+      static_cast<const bf16*>(workspace), vt_stride);
+  if (!maps) return fail(DL_UNSUPPORTED, "attention prefill: tensor maps");
+  dl_status s = cuda_status(dl::launch_vt_transpose(static_cast<const bf16*>(value), static_cast<bf16*>(workspace),
+                                                    int(first_position + positions), int(kv_heads), int(width),
+                                                    vt_stride, st(stream)),
+                            "attention prefill: V transpose");
+  if (s == DL_OK)
+    s = cuda_status(dl::launch_attention_prefill_tc(maps, static_cast<bf16*>(output), int(positions),
+                                                    (long long)first_position, 0, int(query_heads), int(kv_heads),
+                                                    dl::attention_scale(int(width)), nullptr, st(stream)),
+                    "attention prefill");
+  dl::attention_prefill_tc_free(maps);  // the kernel took the maps by value
+  return s;
 }
 
 DL_API dl_status dl_attention(dl_dtype type, const void* query, const void* key, const void* value,

@@ -7,6 +7,7 @@
 #include <string>
 
 #include "attention_decode.h"
+#include "attention_prefill_tc.h"
 #include "engine.h"
 #include "gemm_tcgen05.h"
 #include "steering.h"
@@ -133,7 +134,8 @@ Engine::Engine(const dl_model_config& cfg, int device, size_t capacity, size_t m
                o_tok = stake(std::max<size_t>(R, 64) * 4), o_hist = stake(history_cap_ * 4),
                o_part = stake(size_t(4 * sms_) * 16), o_state = stake(sizeof(DeviceState)),
                o_inv = stake(d * 2), o_dir = stake(D * 4), o_edit = stake(64),
-               o_cap = stake(capacity * D * 2), o_xn = stake(R * D * 2);
+               o_cap = stake(capacity * D * 2), o_xn = stake(R * D * 2),
+               o_vt = stake(size_t(cfg.kv_heads) * d * align_up(capacity, 64) * 2);
   check(cudaMalloc(&scratch_, s), "scratch");
   check(cudaMemsetAsync(scratch_, 0, s, stream_), "scratch clear");
   auto* sb = static_cast<unsigned char*>(scratch_);
@@ -154,12 +156,17 @@ Engine::Engine(const dl_model_config& cfg, int device, size_t capacity, size_t m
   edit_state_ = reinterpret_cast<uint32_t*>(sb + o_edit);
   capture_arena_ = reinterpret_cast<bf16*>(sb + o_cap);
   xn_ = reinterpret_cast<bf16*>(sb + o_xn);
+  vt_ = reinterpret_cast<bf16*>(sb + o_vt);
+  vt_stride_ = int(align_up(capacity, 64));
+  attn_tc_ = attention_prefill_tc_maps(q_rot_, int(R), int(cfg.query_heads), static_cast<const bf16*>(kv_arena_),
+                                       kv_block, int(capacity), int(L), int(cfg.kv_heads), int(d), vt_, vt_stride_);
   check(launch_inv_freq(inv_freq_, int(d), cfg.theta, stream_), "inv_freq");
   check(cudaStreamSynchronize(stream_), "init sync");
 }
 
 Engine::~Engine() {
   if (decode_exec_) cudaGraphExecDestroy(decode_exec_);
+  attention_prefill_tc_free(attn_tc_);
   cudaFree(persist_layers_);
   cudaFree(persist_maps_);
   for (auto& ev : ev_)
@@ -428,10 +435,18 @@ void Engine::run_layers_fast(int rows, long long first) {
     check(launch_qk_norm_rope(q_raw_, k_raw_, y.q_norm, y.k_norm, inv_freq_, q_rot_, kcache_[l], pos, rows, H, Hk,
                               d, cfg_.epsilon, stream_, false),
           "qk_norm_rope");
-    check(launch_attention_scores(q_rot_, kcache_[l], scores_, pos, rows, H, Hk, d, cap, attention_scale(d),
-                                  score_ctas, stream_, false),
-          "attention scores");
-    check(launch_attention_pv(scores_, vcache_[l], att_, pos, rows, H, Hk, d, cap, stream_, false), "attention pv");
+    if (attn_tc_) {
+      // Tensor-core causal attention over keys 0 .. first+rows-1.
+      check(launch_vt_transpose(vcache_[l], vt_, int(first) + rows, Hk, d, vt_stride_, stream_), "v transpose");
+      check(launch_attention_prefill_tc(attn_tc_, att_, rows, first, int(l), H, Hk, attention_scale(d), &state_->err,
+                                        stream_),
+            "attention prefill");
+    } else {
+      check(launch_attention_scores(q_rot_, kcache_[l], scores_, pos, rows, H, Hk, d, cap, attention_scale(d),
+                                    score_ctas, stream_, false),
+            "attention scores");
+      check(launch_attention_pv(scores_, vcache_[l], att_, pos, rows, H, Hk, d, cap, stream_, false), "attention pv");
+    }
     launches_ += 4;
     {
       const int n0s[1] = {0};

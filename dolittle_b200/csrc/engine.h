@@ -136,6 +136,10 @@ class Engine {
   PLayer* persist_layers_ = nullptr;
   CUtensorMap* persist_maps_ = nullptr;
   PGemv persist_head_ = {};
+  // fast prompt pass: tcgen05 attention (tensor maps) and transposed-V scratch
+  struct AttnTcMaps* attn_tc_ = nullptr;
+  bf16* vt_ = nullptr;
+  int vt_stride_ = 0;
 
  public:
   void set_decode_path(int path);

@@ -22,9 +22,12 @@
 #include <mutex>
 
 #include "gemm_tcgen05.h"
+#include "tcgen05.cuh"
 
 namespace dl {
 namespace {
+
+using namespace tc;
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;   // one 128-byte swizzle atom of BF16
@@ -43,56 +46,12 @@ struct alignas(64) GemmArgs {
   unsigned* err;
 };
 
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
-  // K-major, 128-byte swizzle: LBO = 1 (16 B), SBO = 1024 B between 8-row
-  // groups, version 1 (Blackwell), layout type 2 (SWIZZLE_128B).
-  uint64_t d = 0;
-  d |= uint64_t((addr >> 4) & 0x3FFF);
-  d |= uint64_t(1) << 16;
-  d |= uint64_t(1024 >> 4) << 32;
-  d |= uint64_t(1) << 46;
-  d |= uint64_t(2) << 61;
-  return d;
-}
-
-template <int BN>
-__device__ __forceinline__ constexpr uint32_t instr_desc() {
-  // D = F32, A = B = BF16, both K-major, N = BN, M = 128.
-  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
-}
-
 __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
           "r"(smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
       : "memory");
-}
-
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ float swiglu_law(float a, float b) {
@@ -156,7 +115,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
     }
   } else if (warp == 1 && lane == 0) {
     // MMA issuer.
-    constexpr uint32_t idesc = instr_desc<BN>();
+    constexpr uint32_t idesc = instr_desc_bf16(kBM, BN);
     for (int kt = 0; kt < kt_count; ++kt) {
       const int s = kt % S;
       if (!mbar_wait(&full[s], (kt / S) & 1)) {

@@ -106,6 +106,16 @@ DL_API dl_status dl_attention_fixed_scratch(dl_dtype type, const void* query, co
                                             size_t query_heads, size_t kv_heads, size_t width,
                                             void* stream, size_t first_position,
                                             const size_t* device_position, size_t capacity);
+/* Causal GQA attention of the fast prompt pass on tcgen05 tensor cores
+ * (tensor-core accumulation; not the reference reduction order): query rows
+ * [positions][Hq][d] at absolute positions first .. first+positions-1 attend
+ * keys 0 .. first+positions-1 of key/value [capacity][Hkv][d].  d = 128.
+ * workspace: dl_attention_prefill_fast_workspace_bytes() bytes (transposed V). */
+DL_API size_t dl_attention_prefill_fast_workspace_bytes(size_t kv_heads, size_t width, size_t capacity);
+DL_API dl_status dl_attention_prefill_fast(const void* query, const void* key, const void* value, void* output,
+                                           size_t positions, size_t query_heads, size_t kv_heads, size_t width,
+                                           void* stream, size_t first_position, size_t capacity,
+                                           void* workspace);
 DL_API dl_status dl_embedding(dl_dtype type, const uint32_t* tokens, const void* weight,
                               void* output, size_t rows, size_t width, void* stream);
 DL_API dl_status dl_add(dl_dtype type, const void* left, const void* right, void* output,

@@ -175,6 +175,22 @@ def test_fast_prefill_within_tolerance_of_parity_prefill():
     assert out.status == 0 and len(out.tokens) == 4
 
 
+def test_fast_prefill_chunks_within_tolerance_of_parity_prefill():
+    """Fast prompt pass in 128-row chunks (later chunks attend cached keys
+    through the tensor-core attention) against the parity pass: same
+    tolerance as the single-chunk case."""
+    cap = 320
+    cfg, e = _model_8b_shape(2, cap, max_rows=128)
+    prompt = oracle.uniform_ids(300, 1, 105, cfg.vocabulary)
+    parity = nm.bf16_bits_to_f32(e.consume_view(prompt, dl.DL_PREFILL_PARITY))
+    e.reset()
+    fast = nm.bf16_bits_to_f32(e.consume_view(prompt, dl.DL_PREFILL_FAST))
+    peak = float(np.max(np.abs(parity)))
+    r = nm.compare_values(parity, fast, max(1e-4, 0.0625 * peak), 0.03)
+    assert r["passed"], r
+    assert nm.cosine(parity, fast) > 0.999
+
+
 @needs_ref
 def test_chunked_prefill_is_bit_invariant():
     cap = 64
