@@ -73,7 +73,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
   const uint32_t base_s = (smem_addr(smem_raw) + 1023u) & ~1023u;
   unsigned char* ring = smem_raw + (base_s - smem_addr(smem_raw));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
+  // M tiles vary fastest: the CTAs sharing one weight tile run together, so
+  // each weight tile is read from DRAM once and served from L2 to the rest.
+  const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
   const int kt_count = a.K / kBK;
   const int S = a.stages;
 
@@ -260,7 +262,7 @@ cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool 
   a.stages = std::min(8, (200 * 1024) / stage_bytes);
   const size_t smem = size_t(a.stages) * stage_bytes + 1024;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.N / BN, (p.M + kBM - 1) / kBM);
+  cfg.gridDim = dim3((p.M + kBM - 1) / kBM, p.N / BN);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;

@@ -302,6 +302,50 @@ __global__ void rms_norm_kernel(const bf16* x, const bf16* w, bf16* out, size_t 
     out[r * width + i] = narrow(__fmul_rn(round_bf16(__fmul_rn(xs[i], inv)), widen(w[i])));
 }
 
+// One row per CTA for rows of width % 8 == 0 (at most 8192): the row comes
+// in with 16-byte loads and is held as FP32 in shared memory, one warp runs
+// the reference reduction (rms_inverse_warp: same order as above), and the
+// normalisation goes out with 16-byte stores.  Bit-identical to
+// rms_norm_kernel.
+__global__ void rms_norm_rows_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w, bf16* __restrict__ out,
+                                     int width, float eps) {
+  extern __shared__ float xs[];  // [width]
+  __shared__ float inv_s;
+  const size_t r = blockIdx.x;
+  const int n8 = width / 8;
+  const uint4* src = reinterpret_cast<const uint4*>(x + r * width);
+  for (int q = threadIdx.x; q < n8; q += blockDim.x) {
+    const uint4 v = src[q];
+    const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      xs[8 * q + 2 * i] = bf_lo(wd[i]);
+      xs[8 * q + 2 * i + 1] = bf_hi(wd[i]);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const float inv = rms_inverse_warp(xs, width, eps);
+    if (threadIdx.x == 0) inv_s = inv;
+  }
+  __syncthreads();
+  const float inv = inv_s;
+  const uint4* wv = reinterpret_cast<const uint4*>(w);
+  uint4* dst = reinterpret_cast<uint4*>(out + r * width);
+  for (int q = threadIdx.x; q < n8; q += blockDim.x) {
+    const uint4 g = wv[q];
+    const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const bf16 lo = narrow(__fmul_rn(round_bf16(__fmul_rn(xs[8 * q + 2 * i], inv)), bf_lo(gw[i])));
+      const bf16 hi = narrow(__fmul_rn(round_bf16(__fmul_rn(xs[8 * q + 2 * i + 1], inv)), bf_hi(gw[i])));
+      o[i] = uint32_t(__bfloat16_as_ushort(lo)) | (uint32_t(__bfloat16_as_ushort(hi)) << 16);
+    }
+    dst[q] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 __global__ void rotary_kernel(const bf16* x, bf16* out, size_t pairs, int heads, int width,
                               RowPositions pos, double theta, bool positioned) {
   const int half = width / 2;
@@ -447,6 +491,12 @@ cudaError_t launch_silu_multiply(const bf16* g, const bf16* u, bf16* out, size_t
 cudaError_t launch_rms_norm(const bf16* x, const bf16* w, bf16* out, size_t rows, int width, float eps,
                             cudaStream_t stream) {
   if (width > 32768) return cudaErrorInvalidValue;
+  if (width % 8 == 0 && width <= 8192 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0) {
+    const size_t smem = size_t(width) * sizeof(float);
+    rms_norm_rows_kernel<<<unsigned(rows), 128, smem, stream>>>(x, w, out, width, eps);
+    return cudaGetLastError();
+  }
   const int warps = width > 8192 ? 1 : (width > 2048 ? 2 : 4);
   const size_t smem = size_t(warps) * width * sizeof(float);
   cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
