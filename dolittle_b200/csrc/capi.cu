@@ -297,6 +297,37 @@ DL_API dl_status dl_gemm_bf16(const void* x, size_t ldx, const void* w, void* y,
   return cuda_status(dl::launch_gemm_tcgen05(p, st(stream), false), "gemm");
 }
 
+DL_API size_t dl_gemm_bf16_split_workspace_bytes(size_t M, size_t N) { return 2 * M * N * 4; }
+
+DL_API dl_status dl_gemm_bf16_split(const void* x, size_t ldx, const void* w, void* y, size_t ldy, size_t M,
+                                    size_t N, size_t K, int epilogue, void* stream, void* workspace,
+                                    unsigned* tickets, size_t n_tickets) {
+  if (!workspace || !tickets || n_tickets < ((M + 127) / 128) * (N / 256))
+    return fail(DL_INVALID_ARGUMENT, "gemm split: workspace and one ticket per 128 x 256 tile required");
+  if (!x || !w || !y || !M) return fail(DL_INVALID_ARGUMENT, "gemm: null pointer or empty shape");
+  if (epilogue != dl::kGemmStore && epilogue != dl::kGemmResidual && epilogue != dl::kGemmSwiGLU)
+    return fail(DL_INVALID_ARGUMENT, "gemm: epilogue must be 0, 1 or 3");
+  if (!dl::gemm_tcgen05_supported(int(M), int(N), int(K)) || ldx % 8 || ldy % 8 || ldx < K ||
+      (reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y)) % 16)
+    return fail(DL_UNSUPPORTED, "gemm: K % 64, N % 128, 8-element row strides and 16-byte alignment required");
+  dl::GemmProblem p = {};
+  p.x = static_cast<const bf16*>(x);
+  p.ldx = int(ldx);
+  p.w = static_cast<const bf16*>(w);
+  p.M = int(M);
+  p.N = int(N);
+  p.K = int(K);
+  p.epilogue = epilogue;
+  p.nseg = 1;
+  p.seg_out[0] = static_cast<bf16*>(y);
+  p.seg_ld[0] = int(ldy);
+  p.wide_tiles = true;
+  p.partial = static_cast<float*>(workspace);
+  p.partial_rows = int(M);
+  p.tickets = tickets;
+  return cuda_status(dl::launch_gemm_tcgen05(p, st(stream), false), "gemm split");
+}
+
 DL_API dl_status dl_projection_residual(const void* input, const void* weight, void* residual, size_t rows,
                                         size_t input_width, size_t output_width, void* stream) {
   if (!input || !weight || !residual || !rows || input_width % 8)

@@ -135,7 +135,9 @@ Engine::Engine(const dl_model_config& cfg, int device, size_t capacity, size_t m
                o_part = stake(size_t(4 * sms_) * 16), o_state = stake(sizeof(DeviceState)),
                o_inv = stake(d * 2), o_dir = stake(D * 4), o_edit = stake(64),
                o_cap = stake(capacity * D * 2), o_xn = stake(R * D * 2),
-               o_vt = stake(size_t(cfg.kv_heads) * d * align_up(capacity, 64) * 2);
+               o_vt = stake(size_t(cfg.kv_heads) * d * align_up(capacity, 64) * 2),
+               o_split = stake(2 * std::min<size_t>(R, 1024) * std::max<size_t>(D, Q + 2 * G) * 4),
+               o_tickets = stake(1024 * 4);
   check(cudaMalloc(&scratch_, s), "scratch");
   check(cudaMemsetAsync(scratch_, 0, s, stream_), "scratch clear");
   auto* sb = static_cast<unsigned char*>(scratch_);
@@ -157,6 +159,9 @@ Engine::Engine(const dl_model_config& cfg, int device, size_t capacity, size_t m
   capture_arena_ = reinterpret_cast<bf16*>(sb + o_cap);
   xn_ = reinterpret_cast<bf16*>(sb + o_xn);
   vt_ = reinterpret_cast<bf16*>(sb + o_vt);
+  gemm_partial_ = reinterpret_cast<float*>(sb + o_split);
+  gemm_partial_rows_ = int(std::min<size_t>(R, 1024));
+  gemm_tickets_ = reinterpret_cast<unsigned*>(sb + o_tickets);
   vt_stride_ = int(align_up(capacity, 64));
   attn_tc_ = attention_prefill_tc_maps(q_rot_, int(R), int(cfg.query_heads), static_cast<const bf16*>(kv_arena_),
                                        kv_block, int(capacity), int(L), int(cfg.kv_heads), int(d), vt_, vt_stride_);
@@ -395,6 +400,11 @@ bool Engine::fast_prefill_supported() const {
 // rows appended to the cache by the epilogue), o (+residual), gate|up
 // (+SwiGLU) and down (+residual); QK-norm/RoPE and causal attention use the
 // same kernels as the parity path.  `first` is the absolute position of row 0.
+namespace {
+// Tiles of a 128 x 256 tiling (the split-K ticket count).
+long long mt_tickets(int rows, int N) { return (long long)((rows + 127) / 128) * (N / 256); }
+}  // namespace
+
 void Engine::run_layers_fast(int rows, long long first) {
   const int D = int(cfg_.hidden), Q = int(cfg_.query_heads * cfg_.head_width),
             G = int(cfg_.kv_heads * cfg_.head_width), F = int(cfg_.mlp_width), d = int(cfg_.head_width),
@@ -420,6 +430,13 @@ void Engine::run_layers_fast(int rows, long long first) {
     }
     p.wide_tiles = true;
     p.err = &state_->err;
+    // Split-K only for shapes no wider than the workspace (not gate|up).
+    if (N <= int(std::max(cfg_.hidden, cfg_.query_heads * cfg_.head_width + 2 * cfg_.kv_heads * cfg_.head_width)) &&
+        rows <= gemm_partial_rows_ && size_t(mt_tickets(rows, N)) <= 1024) {
+      p.partial = gemm_partial_;
+      p.partial_rows = gemm_partial_rows_;
+      p.tickets = gemm_tickets_;
+    }
     check(launch_gemm_tcgen05(p, stream_, false), "gemm");
     ++launches_;
   };

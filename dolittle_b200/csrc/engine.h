@@ -140,6 +140,9 @@ class Engine {
   struct AttnTcMaps* attn_tc_ = nullptr;
   bf16* vt_ = nullptr;
   int vt_stride_ = 0;
+  float* gemm_partial_ = nullptr;  // split-K partials of the prompt-pass GEMMs
+  int gemm_partial_rows_ = 0;
+  unsigned* gemm_tickets_ = nullptr;
 
  public:
   void set_decode_path(int path);

@@ -31,7 +31,7 @@ using namespace tc;
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;   // one 128-byte swizzle atom of BF16
-constexpr int kThreads = 128;
+constexpr int kThreads = 192;  // producer warp, MMA warp, 4 epilogue warps
 
 struct alignas(64) GemmArgs {
   CUtensorMap map_a;
@@ -44,6 +44,9 @@ struct alignas(64) GemmArgs {
   bf16* seg_out[3];
   int seg_ld[3];
   unsigned* err;
+  int split;           // 1, or 2 K halves per tile
+  float* partial;      // [2][M][N] FP32 (split 2)
+  unsigned* tickets;   // per tile (split 2)
 };
 
 __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -60,23 +63,78 @@ __device__ __forceinline__ float swiglu_law(float a, float b) {
   return round_bf16(__fmul_rn(round_bf16(__fmul_rn(a, s)), b));
 }
 
+// Epilogue of one accumulator row chunk: 32 FP32 columns of output row `row`
+// starting at column `col` (of the output segment).
+__device__ __forceinline__ void store_chunk(const GemmArgs& a, bf16* out, int ld, int row, int col,
+                                            const uint32_t (&r)[32]) {
+  if (a.epilogue == kGemmSwiGLU) {
+    // Columns (2o, 2o+1) = (gate o, up o).
+    uint32_t packed[8];
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      const float v0 = swiglu_law(round_bf16(__uint_as_float(r[2 * i])), round_bf16(__uint_as_float(r[2 * i + 1])));
+      const float v1 =
+          swiglu_law(round_bf16(__uint_as_float(r[2 * i + 2])), round_bf16(__uint_as_float(r[2 * i + 3])));
+      const __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
+      packed[i / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + size_t(row) * ld + col / 2);
+    dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+    return;
+  }
+  uint32_t packed[16];
+  bf16* dst = out + size_t(row) * ld + col;
+  if (a.epilogue == kGemmResidual) {
+    const uint4* src = reinterpret_cast<const uint4*>(dst);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 old = src[q];
+      const uint32_t ow[4] = {old.x, old.y, old.z, old.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int e = q * 8 + 2 * i;
+        const float y0 = round_bf16(__uint_as_float(r[e])), y1 = round_bf16(__uint_as_float(r[e + 1]));
+        const __nv_bfloat162 h2 = __floats2bfloat162_rn(__fadd_rn(bf_lo(ow[i]), y0), __fadd_rn(bf_hi(ow[i]), y1));
+        packed[q * 4 + i] = *reinterpret_cast<const uint32_t*>(&h2);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const __nv_bfloat162 h2 = __floats2bfloat162_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+      packed[i] = *reinterpret_cast<const uint32_t*>(&h2);
+    }
+  }
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) d4[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+}
+
+// Persistent, warp-specialized: CTA b processes tiles b, b + grid, ... with
+// M tiles varying fastest (the CTAs that share a weight tile run together,
+// so it is read from DRAM once).  Warp 0 streams A/B stages by TMA through
+// the ring, warp 1 issues the MMAs into one of two TMEM accumulators, and
+// warps 2-5 (TMEM lane groups 2, 3, 0, 1) drain the other accumulator, so a
+// tile's epilogue overlaps the next tile's main loop.
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_constant__ GemmArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  __shared__ uint64_t full[8], empty[8], done;
+  __shared__ uint64_t full[8], empty[8], acc_full[2], acc_empty[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
+  __shared__ bool last_half;
   constexpr int kABytes = kBM * kBK * 2;
   constexpr int kBBytes = BN * kBK * 2;
   constexpr int kStageBytes = kABytes + kBBytes;
-  // 1024-byte aligned ring (swizzle atoms).
+  constexpr uint32_t kCols = 2 * BN;
   const uint32_t base_s = (smem_addr(smem_raw) + 1023u) & ~1023u;
   unsigned char* ring = smem_raw + (base_s - smem_addr(smem_raw));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // M tiles vary fastest: the CTAs sharing one weight tile run together, so
-  // each weight tile is read from DRAM once and served from L2 to the rest.
-  const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
-  const int kt_count = a.K / kBK;
+  const int mt = (a.M + kBM - 1) / kBM;
+  const int tiles = mt * (a.N / BN);
+  const int units = tiles * a.split;  // unit u: tile u % tiles, K half u / tiles
+  const int kt_per = (a.K / kBK) / a.split;
   const int S = a.stages;
 
   if (threadIdx.x == 0) {
@@ -84,131 +142,163 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(&done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
     abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
-                 "r"(uint32_t(BN))
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  if (warp == 0) tmem_alloc(&tmem_base, kCols);
+  fence_before_sync();
   __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  fence_after_sync();
   const uint32_t tmem = tmem_base;
   allow_next();
   wait_prior();
 
-  if (warp == 0 && lane == 0) {
-    // Producer.
-    for (int kt = 0; kt < kt_count; ++kt) {
-      const int s = kt % S;
-      if (kt >= S && !mbar_wait(&empty[s], ((kt / S) - 1) & 1)) {
-        record_error(a.err, kErrWaitEmpty);
-        atomicExch(&abort_flag, 1);
-        break;
+  if (warp == 0) {
+    if (lane == 0) {
+      // Producer.
+      int g = 0;
+      for (int u = blockIdx.x; u < units && !*reinterpret_cast<volatile int*>(&abort_flag); u += gridDim.x) {
+        const int tile = u % tiles, half = u / tiles;
+        const int m0 = (tile % mt) * kBM, n0 = (tile / mt) * BN;
+        for (int kt = half * kt_per; kt < (half + 1) * kt_per; ++kt, ++g) {
+          const int s = g % S;
+          if (g >= S && !mbar_wait(&empty[s], ((g / S) - 1) & 1)) {
+            record_error(a.err, kErrWaitEmpty);
+            atomicExch(&abort_flag, 1);
+            break;
+          }
+          unsigned char* st = ring + s * kStageBytes;
+          mbar_arrive_expect_tx(&full[s], kStageBytes);
+          tma_2d(st, &a.map_a, kt * kBK, m0, &full[s]);
+          tma_2d(st + kABytes, &a.map_b, kt * kBK, n0, &full[s]);
+        }
       }
-      unsigned char* st = ring + s * kStageBytes;
-      mbar_arrive_expect_tx(&full[s], kStageBytes);
-      tma_2d(st, &a.map_a, kt * kBK, m0, &full[s]);
-      tma_2d(st + kABytes, &a.map_b, kt * kBK, n0, &full[s]);
     }
-  } else if (warp == 1 && lane == 0) {
-    // MMA issuer.
-    constexpr uint32_t idesc = instr_desc_bf16(kBM, BN);
-    for (int kt = 0; kt < kt_count; ++kt) {
-      const int s = kt % S;
-      if (!mbar_wait(&full[s], (kt / S) & 1)) {
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // MMA issuer.
+      constexpr uint32_t idesc = instr_desc_bf16(kBM, BN);
+      int g = 0, t = 0;
+      for (int u = blockIdx.x; u < units && !*reinterpret_cast<volatile int*>(&abort_flag); u += gridDim.x, ++t) {
+        const int buf = t & 1;
+        if (t >= 2 && !mbar_wait(&acc_empty[buf], ((t >> 1) - 1) & 1)) {
+          record_error(a.err, kErrWaitEmpty);
+          atomicExch(&abort_flag, 1);
+          break;
+        }
+        fence_after_sync();
+        const uint32_t acc = tmem + uint32_t(buf * BN);
+        bool ok = true;
+        for (int kt = 0; kt < kt_per; ++kt, ++g) {
+          const int s = g % S;
+          if (!mbar_wait(&full[s], (g / S) & 1)) {
+            record_error(a.err, kErrWaitFull);
+            atomicExch(&abort_flag, 1);
+            ok = false;
+            break;
+          }
+          fence_after_sync();
+          const uint32_t sa = smem_addr(ring + s * kStageBytes);
+          const uint64_t adesc = smem_desc_sw128(sa);
+          const uint64_t bdesc = smem_desc_sw128(sa + kABytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            mma_bf16(acc, adesc + uint64_t(kk * 2), bdesc + uint64_t(kk * 2), idesc, (kt | kk) != 0);
+          mma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[buf]);
+      }
+    }
+  } else {
+    // Epilogue warps: TMEM lane group q = warp % 4 holds accumulator rows
+    // 32q .. 32q+31 of the tile.
+    const int q = warp & 3;
+    int t = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++t) {
+      const int tile = u % tiles, half = u / tiles;
+      const int buf = t & 1;
+      if (!mbar_wait(&acc_full[buf], (t >> 1) & 1)) {
         record_error(a.err, kErrWaitFull);
         atomicExch(&abort_flag, 1);
         break;
       }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t sa = smem_addr(ring + s * kStageBytes);
-      const uint64_t adesc = smem_desc_sw128(sa);
-      const uint64_t bdesc = smem_desc_sw128(sa + kABytes);
-#pragma unroll
-      for (int kk = 0; kk < kBK / 16; ++kk) {
-        // Advance 16 BF16 (32 bytes) along K inside the swizzled rows.
-        mma_bf16(tmem, adesc + uint64_t(kk * 2), bdesc + uint64_t(kk * 2), idesc, (kt | kk) != 0);
-      }
-      mma_commit(&empty[s]);
-    }
-    mma_commit(&done);
-  }
-  __syncwarp();
-
-  // Epilogue: all 128 threads; warp w owns accumulator rows 32w..32w+31.
-  if (!mbar_wait(&done, 0)) {
-    record_error(a.err, kErrWaitFull);
-    atomicExch(&abort_flag, 1);
-  }
-  __syncthreads();  // the abort decision is uniform across the CTA
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const int row = m0 + warp * 32 + lane;
-  if (!abort_flag) {
-    int si = 0;
-    for (int i = 1; i < a.nseg; ++i)
-      if (n0 >= a.seg_n0[i]) si = i;
-    bf16* out = a.seg_out[si];
-    const int ld = a.seg_ld[si];
-    const int c0 = n0 - a.seg_n0[si];
+      fence_after_sync();
+      const int m0 = (tile % mt) * kBM, n0 = (tile / mt) * BN;
+      const int row = m0 + q * 32 + lane;
+      int si = 0;
+      for (int i = 1; i < a.nseg; ++i)
+        if (n0 >= a.seg_n0[i]) si = i;
+      bf16* out = a.seg_out[si];
+      const int ld = a.seg_ld[si];
+      const int c0 = n0 - a.seg_n0[si];
+      const uint32_t acc = tmem + uint32_t(buf * BN) + (uint32_t(q * 32) << 16);
+      if (a.split == 1) {
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      uint32_t r[32];
-      tmem_ld32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(c * 32), r);
-      if (row >= a.M) continue;
-      const int col = c0 + c * 32;
-      if (a.epilogue == kGemmSwiGLU) {
-        // Columns (2o, 2o+1) = (gate o, up o).
-        uint32_t packed[8];
-#pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          const float v0 = swiglu_law(round_bf16(__uint_as_float(r[2 * i])), round_bf16(__uint_as_float(r[2 * i + 1])));
-          const float v1 =
-              swiglu_law(round_bf16(__uint_as_float(r[2 * i + 2])), round_bf16(__uint_as_float(r[2 * i + 3])));
-          const __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
-          packed[i / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(acc + uint32_t(c * 32), r);
+          if (row < a.M) store_chunk(a, out, ld, row, c0 + c * 32, r);
         }
-        uint4* dst = reinterpret_cast<uint4*>(out + size_t(row) * ld + col / 2);
-        dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-        dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
       } else {
-        uint32_t packed[16];
-        bf16* dst = out + size_t(row) * ld + col;
-        if (a.epilogue == kGemmResidual) {
-          const uint4* src = reinterpret_cast<const uint4*>(dst);
+        // Both K halves publish their FP32 partial; the second to finish
+        // adds the other half (FP32 addition commutes, so the result does
+        // not depend on which half finishes last) and stores.
+        float* mine = a.partial + (size_t(half) * a.M + row) * a.N + n0;
+        const float* other = a.partial + (size_t(1 - half) * a.M + row) * a.N + n0;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(acc + uint32_t(c * 32), r);
+          if (row < a.M) {
+            uint4* d = reinterpret_cast<uint4*>(mine + c * 32);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint4 old = src[q];
-            const uint32_t ow[4] = {old.x, old.y, old.z, old.w};
+            for (int i = 0; i < 8; ++i) d[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+          }
+        }
+        __threadfence();
+        named_sync(1, 128);
+        if (threadIdx.x == 64) last_half = atomicAdd(&a.tickets[tile], 1u) == 1u;
+        named_sync(1, 128);
+        if (last_half) {
+          __threadfence();
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(acc + uint32_t(c * 32), r);
+            if (row < a.M) {
+              const uint4* o4 = reinterpret_cast<const uint4*>(other + c * 32);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int e = q * 8 + 2 * i;
-              const float y0 = round_bf16(__uint_as_float(r[e])), y1 = round_bf16(__uint_as_float(r[e + 1]));
-              const __nv_bfloat162 h2 = __floats2bfloat162_rn(__fadd_rn(bf_lo(ow[i]), y0), __fadd_rn(bf_hi(ow[i]), y1));
-              packed[q * 4 + i] = *reinterpret_cast<const uint32_t*>(&h2);
+              for (int i = 0; i < 8; ++i) {
+                const uint4 v = __ldcg(o4 + i);
+                r[4 * i] = __float_as_uint(__uint_as_float(r[4 * i]) + __uint_as_float(v.x));
+                r[4 * i + 1] = __float_as_uint(__uint_as_float(r[4 * i + 1]) + __uint_as_float(v.y));
+                r[4 * i + 2] = __float_as_uint(__uint_as_float(r[4 * i + 2]) + __uint_as_float(v.z));
+                r[4 * i + 3] = __float_as_uint(__uint_as_float(r[4 * i + 3]) + __uint_as_float(v.w));
+              }
+              store_chunk(a, out, ld, row, c0 + c * 32, r);
             }
           }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const __nv_bfloat162 h2 = __floats2bfloat162_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
-            packed[i] = *reinterpret_cast<const uint32_t*>(&h2);
-          }
+          if (threadIdx.x == 64) a.tickets[tile] = 0;
         }
-        uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) d4[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
       }
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   }
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  fence_before_sync();
   __syncthreads();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(uint32_t(BN)) : "memory");
+  if (warp == 0) tmem_dealloc(tmem, kCols);
 }
+
+}  // namespace
+
+namespace {
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -242,7 +332,20 @@ bool gemm_tcgen05_supported(int M, int N, int K) { return M > 0 && K % kBK == 0 
 cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool pdl) {
   if (!gemm_tcgen05_supported(p.M, p.N, p.K) || p.nseg < 1 || p.nseg > 3) return cudaErrorInvalidValue;
   GemmArgs a = {};
-  const int BN = (p.N % 256 == 0 && p.wide_tiles) ? 256 : 128;
+  // Tile width by waves over the SMs: a 256-wide tile costs about two
+  // 128-wide ones, so 256 only when it needs no more than half the waves.
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long mt = (p.M + kBM - 1) / kBM;
+  const long long waves256 = (mt * (p.N / 256) + sms - 1) / sms, waves128 = (mt * (p.N / 128) + sms - 1) / sms;
+  int BN = (p.N % 256 == 0 && p.wide_tiles && 2 * waves256 <= waves128) ? 256 : 128;
+  // Split K in two when even 128-wide tiles would leave half the SMs idle.
+  int split = 1;
+  if (p.partial && p.tickets && p.M <= p.partial_rows && (p.K / kBK) % 2 == 0 && p.N % 256 == 0 && p.wide_tiles &&
+      2 * mt * (p.N / 256) <= sms) {
+    BN = 256;
+    split = 2;
+  }
   for (int i = 0; i < p.nseg; ++i)
     if (p.seg_n0[i] % BN) return cudaErrorInvalidValue;  // tiles never straddle outputs
   if (!encode_2d(&a.map_a, p.x, uint64_t(p.M), uint64_t(p.K), uint64_t(p.ldx), kBM)) return cudaErrorInvalidValue;
@@ -262,7 +365,11 @@ cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool 
   a.stages = std::min(8, (200 * 1024) / stage_bytes);
   const size_t smem = size_t(a.stages) * stage_bytes + 1024;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((p.M + kBM - 1) / kBM, p.N / BN);
+  a.split = split;
+  a.partial = p.partial;
+  a.tickets = p.tickets;
+  const long long units = mt * (p.N / BN) * split;
+  cfg.gridDim = dim3(unsigned(std::min<long long>(units, sms)));
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;

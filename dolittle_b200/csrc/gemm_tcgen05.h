@@ -23,6 +23,13 @@ struct GemmProblem {
   int seg_ld[3];      // output row stride (elements)
   bool wide_tiles;    // allow 128 x 256 tiles
   unsigned* err;
+  // Optional split-K workspace (both or neither): FP32 partials
+  // [2][partial_rows][N] and per-tile tickets (zeroed, left zeroed).  With
+  // them, shapes that would leave most SMs idle run as two K halves whose
+  // second finisher adds the halves and applies the epilogue.
+  float* partial;
+  int partial_rows;
+  unsigned* tickets;
 };
 
 bool gemm_tcgen05_supported(int M, int N, int K);

@@ -71,6 +71,45 @@ def test_gemm_residual_and_swiglu_epilogues():
     assert r2["passed"], r2
 
 
+@pytest.mark.parametrize("M,N,K,epi", [(512, 4096, 4096, 0), (512, 4096, 12288, 1), (200, 6144, 4096, 0)])
+def test_gemm_split_k_matches_fp32_reference_and_unsplit(M, N, K, epi):
+    """Split-K (two K halves summed in FP32 by the second finisher) against
+    the FP32 reference and against the unsplit kernel: same tolerance, and
+    repeated runs are bit-identical (the order of the halves is fixed)."""
+    torch = _torch()
+    x, w = _case(M, N, K, seed=M + K + epi)
+    res = torch.randn(M, N, device="cuda").to(torch.bfloat16) if epi == 1 else None
+    L = dl.lib()
+    ws = torch.empty(L.dl_gemm_bf16_split_workspace_bytes(M, N), device="cuda", dtype=torch.uint8)
+    n_t = ((M + 127) // 128) * (N // 256)
+    tickets = torch.zeros(n_t, device="cuda", dtype=torch.int32)
+    outs = []
+    for _ in range(2):
+        y = res.clone() if epi == 1 else torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        assert L.dl_gemm_bf16_split(x.data_ptr(), K, w.data_ptr(), y.data_ptr(), N, M, N, K, epi, None,
+                                    ws.data_ptr(), tickets.data_ptr(), n_t) == 0, L.dl_last_error()
+        torch.cuda.synchronize()
+        outs.append(y)
+    assert torch.equal(outs[0], outs[1])
+    assert int(tickets.abs().sum()) == 0
+    proj = x.float() @ w.float().T
+    ref = (res.float() + proj.to(torch.bfloat16).float()).to(torch.bfloat16).float() if epi == 1 else proj
+    got = outs[0].float()
+    if epi == 1:
+        # Residual epilogue: round(res + round(acc)) rounds twice, so a
+        # different (tensor-core) accumulation can move round(acc) by one
+        # BF16 ulp of the projection and the sum by one ulp of the result:
+        # bound 2 ulp of the larger magnitude (ulp = 2^(e-7) on [2^e, 2^(e+1))).
+        mag = torch.maximum(proj.abs(), ref.abs()).clamp_min(1e-30)
+        ulp = torch.exp2(torch.floor(torch.log2(mag)) - 7)
+        assert bool(((got - ref).abs() <= 2 * ulp + 1e-3).all())
+    else:
+        r = nm.compare_elementwise(ref.cpu().numpy(), got.cpu().numpy(), 1e-3, 1.6e-2)
+        assert r["passed"], r
+    rel = ((got - ref).norm() / ref.norm()).item()
+    assert rel < 4e-3, rel
+
+
 def test_gemm_rejects_unsupported_shapes():
     torch = _torch()
     x = torch.zeros(8, 100, device="cuda", dtype=torch.bfloat16)
