@@ -166,6 +166,84 @@ def cpu_tensors_generated(cfg):
     return out
 
 
+def reference_gpu_baseline(steps=20):
+    """The reference's own CUDA kernels (its Ampere build: compute_86 PTX,
+    JIT-compiled by the driver on this B200; oracle/_ref/libref_cuda.so built
+    from the reference sources) driven in its Qwen3 recipe order.  Decode: one
+    single-token forward pass at KV length PROMPT + DECODE/2 captured once in a
+    CUDA graph and replayed (the reference also replays its decode body from a
+    graph), timed with CUDA events; the greedy selection is not included.
+    Prefill: one 16-row chunk from position 0 (the reference re-streams the
+    weights for every 8 rows).  Weights: seeded N(0, 0.02) BF16, norms 1."""
+    import ctypes as C
+    try:
+        import torch
+    except ImportError:
+        return None
+    from oracle import oracle
+    L = oracle.ref_cuda()
+    if L is None or not torch.cuda.is_available():
+        return None
+    D, Q, G, F, V, Lyr, d = model_dims()
+    cfg = oracle.OrConfig(D, 32, 8, 128, F, V, Lyr, 1e-6, 1e6)
+    gen = torch.Generator(device="cuda").manual_seed(SEED)
+
+    def weight(rows, cols):
+        if rows == 1:
+            return torch.ones(cols, device="cuda", dtype=torch.bfloat16)
+        return torch.empty(rows, cols, device="cuda", dtype=torch.bfloat16).normal_(0.0, 0.02, generator=gen)
+
+    shapes = [(V, D), (1, D), (V, D)]
+    for _ in range(Lyr):
+        shapes += [(1, D), (Q, D), (G, D), (G, D), (1, d), (1, d), (D, Q), (1, D), (F, D), (F, D), (D, F)]
+    tensors = [weight(r, c) for r, c in shapes]
+    cap = PROMPT + DECODE + 8
+    cache = [torch.zeros(cap, G, device="cuda", dtype=torch.bfloat16) for _ in range(2 * Lyr)]
+    tp = (C.c_void_p * len(tensors))(*[t.data_ptr() for t in tensors])
+    cp = (C.c_void_p * len(cache))(*[t.data_ptr() for t in cache])
+    rows_pf = 16
+    scratch = torch.zeros(L.ref_qwen3_scratch_bytes(C.byref(cfg), rows_pf) // 2 + 64, device="cuda",
+                          dtype=torch.bfloat16)
+    tokens = torch.tensor(prompt_ids(V)[:rows_pf].astype(np.int64), device="cuda").to(torch.int32)
+    logits = torch.zeros(V, device="cuda", dtype=torch.bfloat16)
+    stream = torch.cuda.Stream()
+    S = PROMPT + DECODE // 2
+
+    def forward(rows, first):
+        return L.ref_qwen3_forward(C.byref(cfg), tp, cp, cap, tokens.data_ptr(), rows, first, logits.data_ptr(),
+                                   -1, None, scratch.data_ptr(), stream.cuda_stream)
+
+    with torch.cuda.stream(stream):
+        assert forward(1, S) == 0  # first launch JIT-compiles the PTX
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            assert forward(1, S) == 0
+        for _ in range(3):
+            graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+        e1.synchronize()
+        decode_ms = e0.elapsed_time(e1) / steps
+        assert forward(rows_pf, 0) == 0
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        assert forward(rows_pf, 0) == 0
+        p1.record(stream)
+        p1.synchronize()
+        prefill_ms = p0.elapsed_time(p1)
+    del graph
+    return {"decode_tok_s": 1000.0 / decode_ms, "decode_ms_per_token": decode_ms,
+            "decode_hbm_gbs": decode_bytes(S) / (decode_ms * 1e-3) / 1e9,
+            "prefill_tok_s": rows_pf * 1000.0 / prefill_ms,
+            "kind": "reference CUDA kernels (compute_86 PTX JIT on this GPU), recipe order",
+            "sample": f"decode: {steps} graph replays of one forward pass at KV length {S}; "
+                      f"prefill: one {rows_pf}-row chunk; logits only (no selection kernel)"}
+
+
 def run_reference(args):
     world, rank, local = dist_setup()
     if rank != 0:
@@ -188,6 +266,12 @@ def run_reference(args):
         per.append(time.perf_counter() - s)
     total = time.perf_counter() - t1
     value = args.steps / total
+    ref_gpu = None
+    if not args.no_ref_gpu:
+        try:
+            ref_gpu = reference_gpu_baseline()
+        except Exception as e:  # the CPU arm stands on its own
+            ref_gpu = {"unavailable": f"{type(e).__name__}: {e}"}
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -200,6 +284,7 @@ def run_reference(args):
                                        "Qwen3-8B through the reference-law restatement (the reference has no "
                                        "whole-model host engine; its host numerical path is per-operation)"},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "ref_gpu": ref_gpu,
             "setup_s": t1 - t0}
     print(json.dumps(line), flush=True)
     return 0
@@ -411,6 +496,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="reference arm: skip timing the reference's CUDA kernels on the GPU")
     ap.add_argument("--prefill", choices=["fast", "parity"], default="fast",
                     help="prompt pass on the tcgen05 GEMMs (fast) or in the reference order (parity)")
     ap.add_argument("--profile", choices=["gemv", "decode", "prefill", "persist"], default=None,
