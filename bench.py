@@ -347,6 +347,7 @@ def run_ours(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120))
     import dolittle_b200 as dl
+    from dolittle_b200 import replicas
     hbm, tflops, kind = peaks()
     cfg = dl.QWEN3_8B
     fast = args.prefill == "fast"
@@ -377,10 +378,8 @@ def run_ours(args):
     prefill_s = sum(g.prefill_ms for g in gens) / 1000.0
     wall_s = sum(walls)
     step_s = decode_s + prefill_s
-    if dist is not None:
-        t = torch.tensor([decode_s, prefill_s, wall_s, step_s], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        decode_s, prefill_s, wall_s, step_s = t.tolist()
+    # The job lasts as long as its slowest replica.
+    decode_s, prefill_s, wall_s, step_s = replicas.max_over_ranks(dist, [decode_s, prefill_s, wall_s, step_s])
     steps_decoded = gens[0].decode_steps
     tokens = world * args.steps * steps_decoded
     value = tokens / decode_s
