@@ -92,6 +92,9 @@ SIGNATURES = {
     "dl_engine_read_capture": (C.c_int, [vp, sz, sz, u16p]),
     "dl_engine_set_intervention": (C.c_int, [vp, C.c_int, sz, C.c_float, C.POINTER(C.c_float)]),
     "dl_engine_set_decode_path": (C.c_int, [vp, C.c_int]),
+    "dl_engine_set_injection": (C.c_int, [vp, C.c_int64, u16p, C.c_float]),
+    "dl_engine_set_reconstruction_head": (C.c_int, [vp, u16p]),
+    "dl_engine_reconstruct": (C.c_int, [vp, u32p, sz, u16p]),
     "dl_engine_read_kv": (C.c_int, [vp, sz, C.c_int, sz, sz, u16p]),
     "dl_engine_generate": (C.c_int, [vp, u32p, sz, sz, C.POINTER(Sampling), C.c_uint64, u32p, sz, C.c_int,
                                      u32p, C.POINTER(sz), u16p, C.POINTER(GenerationStats)]),

@@ -504,6 +504,19 @@ DL_API dl_status dl_engine_set_intervention(dl_engine* e, int layer, size_t sele
 DL_API dl_status dl_engine_set_decode_path(dl_engine* e, int path) {
   DL_ENGINE_CALL(e->impl->set_decode_path(path));
 }
+DL_API dl_status dl_engine_set_injection(dl_engine* e, int64_t position, const uint16_t* source_bits,
+                                         float scale) {
+  if (position >= 0 && !source_bits) return fail(DL_INVALID_ARGUMENT, "injection: source required");
+  DL_ENGINE_CALL(e->impl->set_injection((long long)position, source_bits, scale));
+}
+DL_API dl_status dl_engine_set_reconstruction_head(dl_engine* e, const uint16_t* head_bits) {
+  if (!head_bits) return fail(DL_INVALID_ARGUMENT, "reconstruction head: null");
+  DL_ENGINE_CALL(e->impl->set_reconstruction_head(head_bits));
+}
+DL_API dl_status dl_engine_reconstruct(dl_engine* e, const uint32_t* tokens, size_t n, uint16_t* out_bits) {
+  if (!tokens || !out_bits) return fail(DL_INVALID_ARGUMENT, "reconstruct: null");
+  DL_ENGINE_CALL(e->impl->reconstruct(tokens, n, out_bits));
+}
 DL_API dl_status dl_engine_read_kv(dl_engine* e, size_t layer, int values, size_t first, size_t count,
                                    uint16_t* host) {
   DL_ENGINE_CALL(e->impl->read_kv(layer, values, first, count, host));

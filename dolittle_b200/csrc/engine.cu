@@ -137,7 +137,7 @@ Engine::Engine(const dl_model_config& cfg, int device, size_t capacity, size_t m
                o_cap = stake(capacity * D * 2), o_xn = stake(R * D * 2),
                o_vt = stake(size_t(cfg.kv_heads) * d * align_up(capacity, 64) * 2),
                o_split = stake(2 * std::min<size_t>(R, 1024) * std::max<size_t>(D, Q + 2 * G) * 4),
-               o_tickets = stake(1024 * 4);
+               o_tickets = stake(1024 * 4), o_inject = stake(2 * D * 2), o_inject_misc = stake(64);
   check(cudaMalloc(&scratch_, s), "scratch");
   check(cudaMemsetAsync(scratch_, 0, s, stream_), "scratch clear");
   auto* sb = static_cast<unsigned char*>(scratch_);
@@ -162,6 +162,9 @@ Engine::Engine(const dl_model_config& cfg, int device, size_t capacity, size_t m
   gemm_partial_ = reinterpret_cast<float*>(sb + o_split);
   gemm_partial_rows_ = int(std::min<size_t>(R, 1024));
   gemm_tickets_ = reinterpret_cast<unsigned*>(sb + o_tickets);
+  inject_row_ = reinterpret_cast<bf16*>(sb + o_inject);
+  inject_norm_ = reinterpret_cast<float*>(sb + o_inject_misc);
+  inject_status_ = reinterpret_cast<unsigned*>(sb + o_inject_misc + 16);
   vt_stride_ = int(align_up(capacity, 64));
   attn_tc_ = attention_prefill_tc_maps(q_rot_, int(R), int(cfg.query_heads), static_cast<const bf16*>(kv_arena_),
                                        kv_block, int(capacity), int(L), int(cfg.kv_heads), int(d), vt_, vt_stride_);
@@ -172,6 +175,7 @@ Engine::Engine(const dl_model_config& cfg, int device, size_t capacity, size_t m
 Engine::~Engine() {
   if (decode_exec_) cudaGraphExecDestroy(decode_exec_);
   attention_prefill_tc_free(attn_tc_);
+  cudaFree(recon_head_);
   cudaFree(persist_layers_);
   cudaFree(persist_maps_);
   for (auto& ev : ev_)
@@ -504,6 +508,12 @@ void Engine::consume_rows(const uint32_t* tokens, size_t n, bool pdl, int mode, 
     const int rows = int(std::min(max_rows_, n - c0));
     check(cudaMemcpyAsync(tokens_dev_, tokens + c0, rows * 4, cudaMemcpyHostToDevice, stream_), "tokens");
     check(launch_embedding(tokens_dev_, embed_, residual_, rows, int(cfg_.hidden), stream_, false), "embed");
+    // Verbalizer injection: the marker row's embedding is replaced by the
+    // normalized vector (reference src/kernels/cuda/decode.cu:221-230).
+    if (inject_position_ >= first && inject_position_ < first + rows)
+      check(cudaMemcpyAsync(residual_ + size_t(inject_position_ - first) * cfg_.hidden, inject_row_,
+                            cfg_.hidden * 2, cudaMemcpyDeviceToDevice, stream_),
+            "inject");
     if (fast)
       run_layers_fast(rows, first);
     else
@@ -526,6 +536,53 @@ void Engine::consume(const uint32_t* tokens, size_t n, int mode, uint16_t* logit
     check(cudaMemcpyAsync(logits_out, logits_, size_t(cfg_.vocabulary) * 2, cudaMemcpyDeviceToHost, stream_),
           "logits");
   check(cudaStreamSynchronize(stream_), "consume sync");
+  check_fault();
+}
+
+void Engine::set_injection(long long position, const uint16_t* source_bits, float scale) {
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  if (position < 0) {
+    inject_position_ = -1;
+    return;
+  }
+  if (size_t(position) >= capacity_) throw std::invalid_argument("injection position beyond capacity");
+  if (!(scale > 0.f) || !std::isfinite(scale)) throw std::invalid_argument("injection scale must be finite and > 0");
+  const size_t D = cfg_.hidden;
+  // Source row staged in the injection row itself, normalized into a second
+  // half of the buffer, then kept as the row to insert.
+  check(cudaMemcpyAsync(inject_row_ + D, source_bits, D * 2, cudaMemcpyHostToDevice, stream_), "injection source");
+  check(launch_normalize_injection(inject_row_ + D, inject_row_, inject_norm_, inject_status_, int(D), scale, stream_),
+        "normalize injection");
+  unsigned status = 0;
+  check(cudaMemcpyAsync(&status, inject_status_, 4, cudaMemcpyDeviceToHost, stream_), "injection status");
+  check(cudaStreamSynchronize(stream_), "injection sync");
+  if (status) throw std::invalid_argument("injection source has zero or non-finite norm");
+  inject_position_ = position;
+}
+
+void Engine::set_reconstruction_head(const uint16_t* host_bits) {
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  const size_t D = cfg_.hidden;
+  if (!recon_head_) check(cudaMalloc(&recon_head_, D * D * 2), "reconstruction head");
+  check(cudaMemcpyAsync(recon_head_, host_bits, D * D * 2, cudaMemcpyHostToDevice, stream_), "reconstruction head");
+  check(cudaStreamSynchronize(stream_), "reconstruction head sync");
+}
+
+// AR forward-only pass (reference src/inference/executor.cpp:1750-1771,
+// src/models/qwen3/model.cpp:395-404): the prompt through every block from a
+// fresh sequence, then the last position's residual (no final norm) through
+// the D x D reconstruction head under the projection law.
+void Engine::reconstruct(const uint32_t* tokens, size_t n, uint16_t* out_host) {
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  if (!recon_head_) throw std::invalid_argument("reconstruction head not set");
+  if (!n || n > capacity_) throw std::invalid_argument("reconstruction prompt length");
+  reset();
+  consume_rows(tokens, n, true, DL_PREFILL_PARITY, 0);
+  const int D = int(cfg_.hidden);
+  GemvSegment seg = make_segment(static_cast<const bf16*>(recon_head_), xn_, nullptr, D, projection_partials(D, D), D);
+  project(residual_ + size_t(last_rows_ - 1) * D, D, 1, D, kProloguePlain, nullptr, kEpilogueStore, &seg, 1, true);
+  check(cudaMemcpyAsync(out_host, xn_, size_t(D) * 2, cudaMemcpyDeviceToHost, stream_), "reconstruction out");
+  check(cudaStreamSynchronize(stream_), "reconstruct sync");
   check_fault();
 }
 

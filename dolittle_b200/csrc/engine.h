@@ -65,6 +65,9 @@ class Engine {
   void read_capture(size_t first, size_t count, uint16_t* host);
   void set_intervention(int layer, size_t selected, float strength, const float* direction);
   void read_kv(size_t layer, int values, size_t first, size_t count, uint16_t* host);
+  void set_injection(long long position, const uint16_t* source_bits, float scale);
+  void set_reconstruction_head(const uint16_t* host_bits);
+  void reconstruct(const uint32_t* tokens, size_t n, uint16_t* out_host);
   void generate(const uint32_t* prompt, size_t n_prompt, size_t max_new, const dl_sampling& s,
                 uint64_t seed, const uint32_t* stop_ids, size_t n_stop, int prefill_mode,
                 uint32_t* tokens_out, size_t* n_out, uint16_t* logits_out,
@@ -143,6 +146,12 @@ class Engine {
   float* gemm_partial_ = nullptr;  // split-K partials of the prompt-pass GEMMs
   int gemm_partial_rows_ = 0;
   unsigned* gemm_tickets_ = nullptr;
+  // verbalizer injection (marker row) and reconstruction head
+  long long inject_position_ = -1;
+  bf16* inject_row_ = nullptr;  // [2][D]: the row to insert, then the staged source
+  float* inject_norm_ = nullptr;
+  unsigned* inject_status_ = nullptr;
+  void* recon_head_ = nullptr;
 
  public:
   void set_decode_path(int path);

@@ -161,6 +161,31 @@ class Engine:
         DL_DECODE_KERNELS (per-operation kernels); the results are identical."""
         check(lib().dl_engine_set_decode_path(self._h, path))
 
+    def set_injection(self, position: int, source_bits=None, scale: float = 150.0) -> None:
+        """Verbalizer injection: prompt position `position` gets
+        BF16((h/||h||) * scale) of the BF16 row `source_bits` instead of its
+        embedding; position < 0 clears it (ValueError on a zero/non-finite h)."""
+        if position < 0:
+            check(lib().dl_engine_set_injection(self._h, -1, None, 0.0))
+            return
+        h = np.ascontiguousarray(source_bits, np.uint16)
+        if h.size != self.config.hidden:
+            raise ValueError("injection source must have the hidden width")
+        check(lib().dl_engine_set_injection(self._h, position, h.ctypes.data_as(_lib.u16p), scale))
+
+    def set_reconstruction_head(self, head_bits) -> None:
+        w = np.ascontiguousarray(head_bits, np.uint16)
+        if w.size != self.config.hidden ** 2:
+            raise ValueError("reconstruction head must be D x D")
+        check(lib().dl_engine_set_reconstruction_head(self._h, w.ctypes.data_as(_lib.u16p)))
+
+    def reconstruct(self, tokens) -> np.ndarray:
+        """AR forward-only: BF16 bits [D] of head(residual of the last token)."""
+        t = _u32(tokens)
+        out = np.empty(self.config.hidden, np.uint16)
+        check(lib().dl_engine_reconstruct(self._h, t.ctypes.data_as(_lib.u32p), t.size, out.ctypes.data_as(_lib.u16p)))
+        return out
+
     def read_kv(self, layer: int, values: bool, first: int, count: int) -> np.ndarray:
         g = self.config.kv_heads * self.config.head_width
         out = np.empty((count, g), np.uint16)

@@ -270,6 +270,19 @@ DL_API dl_status dl_engine_read_capture(dl_engine* e, size_t first, size_t count
 DL_API dl_status dl_engine_set_intervention(dl_engine* e, int layer, size_t selected,
                                             float strength, const float* host_direction);
 DL_API dl_status dl_engine_set_decode_path(dl_engine* e, int path);
+/* Verbalizer (AV) injection: every later prompt pass replaces the embedding
+ * of absolute position `position` with BF16((h / ||h||) * scale) of the BF16
+ * row `source_bits` [D] (DeviceInjection::normalize + the marker-row replace,
+ * src/kernels/cuda/injection.cu:48-102, decode.cu:221-230).  position < 0
+ * clears it.  A zero or non-finite source is rejected (DL_INVALID_ARGUMENT). */
+DL_API dl_status dl_engine_set_injection(dl_engine* e, int64_t position, const uint16_t* source_bits,
+                                         float scale);
+/* Reconstructor (AR) forward-only pass: the D x D BF16 head, then for a
+ * prompt the last position's residual after the final block (no final norm)
+ * through the head under the projection law -> out_bits [D] (host).  Starts
+ * a fresh sequence (executor.cpp:1750-1771, qwen3/model.cpp:395-404). */
+DL_API dl_status dl_engine_set_reconstruction_head(dl_engine* e, const uint16_t* head_bits);
+DL_API dl_status dl_engine_reconstruct(dl_engine* e, const uint32_t* tokens, size_t n, uint16_t* out_bits);
 DL_API dl_status dl_engine_read_kv(dl_engine* e, size_t layer, int values, size_t first,
                                    size_t count, uint16_t* host);
 /* Live generation: prompt pass, first selection, then decode steps replayed
