@@ -15,6 +15,8 @@ constexpr int kConsumerWarps = kGemvConsumers / 32;
 constexpr long long kSpinLimit = 1ll << 32;  // ~2 s of SM cycles
 constexpr int kMaxInput8 = kPersistMaxInput / 8 / kGemvConsumers;  // 16-byte input loads per thread
 constexpr int kMaxNorm8 = kPersistMaxNormInput / 8 / kGemvConsumers;
+// Normed prologue: x row + norm weight (BF16) and the RMS law's 128 partials.
+static_assert(4 * kPersistMaxNormInput + 128 * 4 <= kPersistUnionBytes, "prologue scratch");
 // Score unit scratch: qs, ks, norm_vals (FP32) and the raw q / k rows (BF16).
 constexpr int kScoreScratch = (8 * 128 + 128 + 8 * 128) * 4 + 8 * 128 * 2;
 
@@ -398,9 +400,30 @@ __device__ void gemv_phase(const PersistArgs& a, const PGemv& ph, unsigned char*
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory");
   named_sync(1, kGemvConsumers);
   if (wg) {
+    // The RMS law's partial c of lane L is the serial sum of squares of
+    // x[4L + c + 128k], k = 0, 1, ...: 128 independent chains, one per
+    // thread here (thread 4L + c reads x[t + 128k]).  Lane L of warp 0 then
+    // adds its four partials in order and the shuffle-down tree finishes,
+    // exactly as rms_inverse_smem does in one warp.
+    float* parts = reinterpret_cast<float*>(uni + 4 * kPersistMaxNormInput);
+    if (threadIdx.x < 128) {
+      float p = 0.f;
+#pragma unroll 8
+      for (int col = threadIdx.x; col < I; col += 128) {
+        const float v = widen(xs[col]);
+        p = __fadd_rn(p, __fmul_rn(v, v));
+      }
+      parts[threadIdx.x] = p;
+    }
+    named_sync(1, kGemvConsumers);
     if (warp == 0) {
-      const float inv = rms_inverse_smem(xs, I, a.eps);
-      if ((threadIdx.x & 31) == 0) h->row_inv = inv;
+      const int lane = threadIdx.x & 31;
+      float sum = __fadd_rn(__fadd_rn(__fadd_rn(parts[4 * lane], parts[4 * lane + 1]), parts[4 * lane + 2]),
+                            parts[4 * lane + 3]);
+      sum = shuffle_down_tree32(sum);
+      const float total = __shfl_sync(0xffffffffu, sum, 0);
+      const float inv = rsqrtf(__fadd_rn(__fmul_rn(total, 1.0f / static_cast<float>(I)), a.eps));
+      if (lane == 0) h->row_inv = inv;
     }
     named_sync(1, kGemvConsumers);
     const float inv = h->row_inv;
@@ -475,6 +498,13 @@ __device__ void score_unit(const PersistArgs& a, const bf16* const* ap, int g, i
     }
   }
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory");
+  // The PV phase reads every group's V rows of this key slice: pull them
+  // into L2 now (one bulk prefetch of the contiguous rows j0 .. j1-1).
+  if (threadIdx.x == 0 && g == 0 && nkeys > 0) {
+    const bf16* v0 = ap[3] + size_t(j0) * kv_heads * width;
+    const unsigned bytes = unsigned(nkeys) * kv_heads * width * 2;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(v0), "r"(bytes) : "memory");
+  }
   named_sync(1, kGemvConsumers);
   if (warp < group || warp == 7) {
     const bool is_q = warp < group;
@@ -622,22 +652,30 @@ __device__ void pv_unit(const PersistArgs& a, const bf16* const* ap, int g, int 
     if (hq < group) {
       float* srow = ss + size_t(hq) * c4;
       float m = -INFINITY;
+#pragma unroll 4
       for (int j = t64; j < count; j += 64) m = fmaxf(m, srow[j]);
 #pragma unroll
       for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
       if (lane == 0) h->wmax[warp] = m;
       named_sync(2 + hq, 64);
       const float maximum = fmaxf(h->wmax[2 * hq], h->wmax[2 * hq + 1]);
+      // e = expf(s - max) once, by both warps; then the 32 strided serial
+      // partials of the den law over the stored e; then p = e / den.
+#pragma unroll 4
+      for (int j = t64; j < count; j += 64) srow[j] = expf(srow[j] - maximum);
+      named_sync(2 + hq, 64);
       if (warp == 2 * hq) {
         float acc = 0.f;
-        for (int j = lane; j < count; j += 32) acc = __fadd_rn(acc, expf(srow[j] - maximum));
+#pragma unroll 8
+        for (int j = lane; j < count; j += 32) acc = __fadd_rn(acc, srow[j]);
 #pragma unroll
         for (int off = 16; off; off >>= 1) acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, off));
         if (lane == 0) h->den_s[hq] = acc;
       }
       named_sync(2 + hq, 64);
       const float den = h->den_s[hq];
-      for (int j = t64; j < count; j += 64) srow[j] = expf(srow[j] - maximum) / den;
+#pragma unroll 4
+      for (int j = t64; j < count; j += 64) srow[j] = srow[j] / den;
     }
     named_sync(1, kGemvConsumers);
     float acc = 0.f;
