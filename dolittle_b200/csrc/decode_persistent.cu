@@ -17,8 +17,15 @@ constexpr int kMaxInput8 = kPersistMaxInput / 8 / kGemvConsumers;  // 16-byte in
 constexpr int kMaxNorm8 = kPersistMaxNormInput / 8 / kGemvConsumers;
 // Normed prologue: x row + norm weight (BF16) and the RMS law's 128 partials.
 static_assert(4 * kPersistMaxNormInput + 128 * 4 <= kPersistUnionBytes, "prologue scratch");
-// Score unit scratch: qs, ks, norm_vals (FP32) and the raw q / k rows (BF16).
-constexpr int kScoreScratch = (8 * 128 + 128 + 8 * 128) * 4 + 8 * 128 * 2;
+// Score unit scratch: qs, ks, norm_vals (FP32), the raw q / k rows and the
+// q / k norm weights (BF16).
+constexpr int kScoreScratch = (8 * 128 + 128 + 8 * 128) * 4 + 8 * 128 * 2 + 2 * 128 * 2;
+
+// Position of feature f of a 128-wide query row in the score unit's layout:
+// lane l of the 8-lane dot product owns features 16l .. 16l+15 and reads them
+// as four float4 at [k][l][4] (k = 0..3), so the 8 lanes of one key read 128
+// contiguous bytes per load (no bank conflicts).
+__device__ __forceinline__ int q_slot(int f) { return ((f & 15) >> 2) * 32 + (f >> 4) * 4 + (f & 3); }
 
 // RMSNorm apply (two rounding points, normalization.cu:82-186) on 8 packed
 // BF16 features.
@@ -467,6 +474,7 @@ __device__ void score_unit(const PersistArgs& a, const bf16* const* ap, int g, i
   float* ks = reinterpret_cast<float*>(uni + 8 * 128 * 4);
   float(*norm_vals)[128] = reinterpret_cast<float(*)[128]>(uni + 8 * 128 * 4 + 128 * 4);
   bf16* raw = reinterpret_cast<bf16*>(uni + (8 * 128 + 128 + 8 * 128) * 4);  // [8][128]: q heads, key in row 7
+  bf16* wnorm = raw + 8 * 128;                                                // [2][128]: q_norm, k_norm
   const bf16* q_norm = ap[0];
   const bf16* k_norm = ap[1];
   bf16* k_cache = const_cast<bf16*>(ap[2]);
@@ -489,6 +497,10 @@ __device__ void score_unit(const PersistArgs& a, const bf16* const* ap, int g, i
       const bf16* src = r < group ? a.q_raw + size_t(g * group + r) * width : a.k_raw + size_t(g) * width;
       cp_async16(raw + (r < group ? r : 7) * 128 + 8 * q, src + 8 * q);
     }
+    for (int idx = threadIdx.x; idx < 2 * chunks; idx += kGemvConsumers) {
+      const int r = idx / chunks, q = idx % chunks;
+      cp_async16(wnorm + r * 128 + 8 * q, (r == 0 ? q_norm : k_norm) + 8 * q);
+    }
   }
   if (staged) {
     for (int idx = threadIdx.x; idx < nkeys * chunks; idx += kGemvConsumers) {
@@ -510,7 +522,7 @@ __device__ void score_unit(const PersistArgs& a, const bf16* const* ap, int g, i
     const bool is_q = warp < group;
     const bf16* src = raw_staged ? raw + warp * 128
                                  : (is_q ? a.q_raw + size_t(g * group + warp) * width : a.k_raw + size_t(g) * width);
-    const bf16* w = is_q ? q_norm : k_norm;
+    const bf16* w = raw_staged ? wnorm + (is_q ? 0 : 128) : (is_q ? q_norm : k_norm);
     float x[4], part[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
@@ -531,13 +543,14 @@ __device__ void score_unit(const PersistArgs& a, const bf16* const* ap, int g, i
     __syncwarp();
     const int half = width / 2;
     float* dst = is_q ? qs[warp] : ks;
+    const bool permute = is_q && width == 128;
     for (int f = lane; f < half; f += 32) {
       const float co = h->rope[f][0], si = h->rope[f][1];
       const float va = nv[f], vb = nv[f + half];
       const float lo = round_bf16(__fsub_rn(round_bf16(__fmul_rn(va, co)), round_bf16(__fmul_rn(vb, si))));
       const float hi = round_bf16(__fadd_rn(round_bf16(__fmul_rn(vb, co)), round_bf16(__fmul_rn(va, si))));
-      dst[f] = lo;
-      dst[f + half] = hi;
+      dst[permute ? q_slot(f) : f] = lo;
+      dst[permute ? q_slot(f + half) : f + half] = hi;
       if (!is_q && owns_new_key) {
         bf16* kc = k_cache + (size_t(S) * kv_heads + g) * width;
         kc[f] = narrow(lo);
@@ -578,9 +591,16 @@ __device__ void score_unit(const PersistArgs& a, const bf16* const* ap, int g, i
 #pragma unroll
       for (int hh = 0; hh < 8; ++hh) {
         if (hh < group) {
+          const float4* q4 = reinterpret_cast<const float4*>(qs[hh]) + lane8;
           float acc = 0.f;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) acc = __fmaf_rn(qs[hh][begin + i], kv[i], acc);
+          for (int k = 0; k < 4; ++k) {
+            const float4 qv = q4[8 * k];
+            acc = __fmaf_rn(qv.x, kv[4 * k], acc);
+            acc = __fmaf_rn(qv.y, kv[4 * k + 1], acc);
+            acc = __fmaf_rn(qv.z, kv[4 * k + 2], acc);
+            acc = __fmaf_rn(qv.w, kv[4 * k + 3], acc);
+          }
           part[hh] = acc;
         }
       }
@@ -596,11 +616,13 @@ __device__ void score_unit(const PersistArgs& a, const bf16* const* ap, int g, i
     }
 #pragma unroll
     for (int hh = 0; hh < 8; ++hh) {
-      float v = part[hh];
-      v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
-      v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
-      v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
-      part[hh] = v;
+      if (hh < group) {
+        float v = part[hh];
+        v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+        v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+        v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+        part[hh] = v;
+      }
     }
     if (live && lane8 == 0)
       for (int hh = 0; hh < group; ++hh)
@@ -680,14 +702,21 @@ __device__ void pv_unit(const PersistArgs& a, const bf16* const* ap, int g, int 
     named_sync(1, kGemvConsumers);
     float acc = 0.f;
     if (live) {
+      // Serial chain over this half's keys: p four keys at a time (one
+      // aligned float4), unrolled so the loads run ahead of the FMAs.
       const float* ph = ss + size_t(hh) * c4;
       const bf16* col = vs + fl;
       int j = jb;
-      for (; j + 4 <= je; j += 4) {
-        acc = __fmaf_rn(ph[j], widen(col[size_t(j) * fpc]), acc);
-        acc = __fmaf_rn(ph[j + 1], widen(col[size_t(j + 1) * fpc]), acc);
-        acc = __fmaf_rn(ph[j + 2], widen(col[size_t(j + 2) * fpc]), acc);
-        acc = __fmaf_rn(ph[j + 3], widen(col[size_t(j + 3) * fpc]), acc);
+      for (; j < je && (j & 3); ++j) acc = __fmaf_rn(ph[j], widen(col[size_t(j) * fpc]), acc);
+      if (fpc == 8) {
+#pragma unroll 4
+        for (; j + 4 <= je; j += 4) {
+          const float4 p4 = *reinterpret_cast<const float4*>(ph + j);
+          acc = __fmaf_rn(p4.x, widen(col[8 * j]), acc);
+          acc = __fmaf_rn(p4.y, widen(col[8 * j + 8]), acc);
+          acc = __fmaf_rn(p4.z, widen(col[8 * j + 16]), acc);
+          acc = __fmaf_rn(p4.w, widen(col[8 * j + 24]), acc);
+        }
       }
       for (; j < je; ++j) acc = __fmaf_rn(ph[j], widen(col[size_t(j) * fpc]), acc);
     }
