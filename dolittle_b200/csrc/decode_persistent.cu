@@ -226,7 +226,11 @@ __device__ __forceinline__ void producer_main(const PersistArgs& a, unsigned cha
           if (mbar_test_wait(&h->empty[st], parity)) break;
           const unsigned req = vload(&h->pf_req);
           if (req != pf_seen) {
+            // A burst starts at the load cursor (the prefetch cursor jumps
+            // there instead of walking the stages already loaded).
             pf_seen = req;
+            pf = ld;
+            pfc = g;
             burst_end = g + unsigned(a.prefetch_stages);
           }
           if (pf.valid && pfc < burst_end) {

@@ -41,7 +41,11 @@ constexpr int kPersistSmem =
     kPersistHeaderBytes + kPersistUnionBytes + 1024 /* ring alignment */ + kPersistSlots * kPersistSlotBytes;
 constexpr int kPersistMaxInput = 12288;     // projection input width (features)
 constexpr int kPersistMaxNormInput = 4096;  // width of an RMSNorm prologue input
-constexpr int kPersistPrefetchStages = 28;  // L2 prefetch burst (stages past the ring) per attention stall
+// L2 prefetch burst (stages past the ring) per attention stall.  The phases
+// already stream at the HBM read rate (~7.8 TB/s) and L2 hits do not arrive
+// faster, so longer bursts only compete with the attention loads: 12 measured
+// best (0 to 40 span ~1 %).
+constexpr int kPersistPrefetchStages = 12;
 
 struct PSeg {
   const CUtensorMap* map;    // device copy, 3D box {64, tile_rows, kc / 64}
