@@ -42,6 +42,11 @@ class GenerationStats(C.Structure):
                 ("status", C.c_uint32), ("fault", C.c_uint32)]
 
 
+class ServeStats(C.Structure):
+    _fields_ = [("prefill_ms", C.c_double), ("decode_ms", C.c_double), ("decode_steps", C.c_uint64),
+                ("kernels_per_decode_step", C.c_uint64)]
+
+
 _lib = None
 
 vp, sz, u32p, u16p = C.c_void_p, C.c_size_t, C.POINTER(C.c_uint32), C.POINTER(C.c_uint16)
@@ -98,6 +103,21 @@ SIGNATURES = {
     "dl_engine_read_kv": (C.c_int, [vp, sz, C.c_int, sz, sz, u16p]),
     "dl_engine_generate": (C.c_int, [vp, u32p, sz, sz, C.POINTER(Sampling), C.c_uint64, u32p, sz, C.c_int,
                                      u32p, C.POINTER(sz), u16p, C.POINTER(GenerationStats)]),
+    "dl_serve_create": (C.c_int, [C.POINTER(ModelConfig), C.c_int, sz, sz, sz, C.c_int, C.c_int, C.POINTER(vp)]),
+    "dl_serve_destroy": (None, [vp]),
+    "dl_serve_nccl_id": (C.c_int, [vp]),
+    "dl_serve_connect": (C.c_int, [vp, vp]),
+    "dl_serve_init_random": (C.c_int, [vp, C.c_uint64, C.c_float]),
+    "dl_serve_set_tensor": (C.c_int, [vp, sz, vp, sz]),
+    "dl_serve_get_tensor": (C.c_int, [vp, sz, vp, sz]),
+    "dl_serve_slice_shape": (C.c_int, [vp, sz, C.POINTER(sz), C.POINTER(sz), C.POINTER(sz), C.POINTER(sz)]),
+    "dl_serve_prefill": (C.c_int, [vp, u32p, sz, C.POINTER(Sampling), C.c_uint64, u32p]),
+    "dl_serve_decode": (C.c_int, [vp, sz, u32p, u16p, C.POINTER(ServeStats)]),
+    "dl_serve_position": (sz, [vp]),
+    "dl_gemm_bf16_parts_workspace_bytes": (sz, [sz, sz, sz, sz]),
+    "dl_gemm_bf16_parts": (C.c_int, [vp, sz, vp, vp, sz, sz, sz, sz, C.c_int, sz, vp, vp]),
+    "dl_attention_decode_batched_workspace_bytes": (sz, [sz, sz, sz, sz]),
+    "dl_attention_decode_batched": (C.c_int, [vp, vp, sz, sz, sz, vp, sz, sz, sz, sz, vp, vp, vp]),
 }
 
 

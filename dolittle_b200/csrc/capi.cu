@@ -16,6 +16,8 @@
 #include "gemv.cuh"
 #include "launch.h"
 #include "sampler.h"
+#include "serve.h"
+#include "serve_kernels.h"
 #include "steering.h"
 
 namespace {
@@ -57,6 +59,9 @@ struct dl_engine {
 };
 struct dl_sampler {
   dl::Sampler s;
+};
+struct dl_serve {
+  dl::Server* impl;
 };
 
 extern "C" {
@@ -528,6 +533,145 @@ DL_API dl_status dl_engine_generate(dl_engine* e, const uint32_t* prompt, size_t
   if (!settings || !prompt || !tokens_out || !n_out) return fail(DL_INVALID_ARGUMENT, "generate: arguments");
   DL_ENGINE_CALL(e->impl->generate(prompt, n_prompt, max_new, *settings, seed, stop_ids, n_stop, prefill_mode,
                                    tokens_out, n_out, logits_out, stats));
+}
+
+
+// ---- batched serving ----
+DL_API dl_status dl_serve_create(const dl_model_config* config, int device, size_t batch, size_t capacity,
+                                 size_t chunk_rows, int tp_rank, int tp_size, dl_serve** out) {
+  if (!config || !out) return fail(DL_INVALID_ARGUMENT, "serve_create: arguments");
+  return guarded([&] {
+    *out = new dl_serve{new dl::Server(*config, device, batch, capacity, chunk_rows, tp_rank, tp_size)};
+    return DL_OK;
+  });
+}
+
+DL_API void dl_serve_destroy(dl_serve* s) {
+  if (!s) return;
+  delete s->impl;
+  delete s;
+}
+
+DL_API dl_status dl_serve_nccl_id(unsigned char* id128) {
+  if (!id128) return fail(DL_INVALID_ARGUMENT, "serve_nccl_id: null");
+  return guarded([&] {
+    dl::Server::nccl_id(id128);
+    return DL_OK;
+  });
+}
+
+#define DL_SERVE_CALL(body)                                            \
+  if (!s || !s->impl) return fail(DL_INVALID_ARGUMENT, "null server"); \
+  return guarded([&] {                                                 \
+    body;                                                              \
+    return DL_OK;                                                      \
+  })
+
+DL_API dl_status dl_serve_connect(dl_serve* s, const unsigned char* id128) {
+  if (!id128) return fail(DL_INVALID_ARGUMENT, "serve_connect: null id");
+  DL_SERVE_CALL(s->impl->connect(id128));
+}
+DL_API dl_status dl_serve_init_random(dl_serve* s, uint64_t seed, float sigma) {
+  DL_SERVE_CALL(s->impl->init_random(seed, sigma));
+}
+DL_API dl_status dl_serve_set_tensor(dl_serve* s, size_t index, const void* host_bits, size_t bytes) {
+  if (!host_bits) return fail(DL_INVALID_ARGUMENT, "serve_set_tensor: null");
+  DL_SERVE_CALL(s->impl->set_tensor(index, host_bits, bytes));
+}
+DL_API dl_status dl_serve_get_tensor(dl_serve* s, size_t index, void* host_bits, size_t bytes) {
+  if (!host_bits) return fail(DL_INVALID_ARGUMENT, "serve_get_tensor: null");
+  DL_SERVE_CALL(s->impl->get_tensor(index, host_bits, bytes));
+}
+DL_API dl_status dl_serve_slice_shape(dl_serve* s, size_t index, size_t* rows, size_t* cols, size_t* r0,
+                                      size_t* c0) {
+  if (!rows || !cols || !r0 || !c0) return fail(DL_INVALID_ARGUMENT, "serve_slice_shape: null");
+  DL_SERVE_CALL(if (!s->impl->slice_shape(index, rows, cols, r0, c0)) throw std::invalid_argument("tensor index"));
+}
+DL_API dl_status dl_serve_prefill(dl_serve* s, const uint32_t* tokens, size_t prompt_len,
+                                  const dl_sampling* settings, uint64_t seed, uint32_t* first_tokens) {
+  if (!tokens || !settings) return fail(DL_INVALID_ARGUMENT, "serve_prefill: null");
+  DL_SERVE_CALL(s->impl->prefill(tokens, prompt_len, *settings, seed, first_tokens));
+}
+DL_API dl_status dl_serve_decode(dl_serve* s, size_t steps, uint32_t* tokens_out, uint16_t* logits_out,
+                                 dl_serve_stats* stats) {
+  DL_SERVE_CALL(s->impl->decode(steps, tokens_out, logits_out, stats));
+}
+DL_API size_t dl_serve_position(dl_serve* s) {
+  if (!s || !s->impl) return 0;
+  try {
+    return s->impl->position();
+  } catch (const std::exception& e) {
+    fail(DL_CUDA_ERROR, e.what());
+    return 0;
+  }
+}
+
+DL_API size_t dl_gemm_bf16_parts_workspace_bytes(size_t M, size_t N, size_t K, size_t parts) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const size_t p = parts ? parts : size_t(dl::gemm_splitk_parts(int(M), int(N), int(K), sms));
+  return p * M * N * 4;
+}
+
+DL_API dl_status dl_gemm_bf16_parts(const void* x, size_t ldx, const void* w, void* y, size_t ldy, size_t M,
+                                    size_t N, size_t K, int epilogue, size_t parts, void* workspace,
+                                    void* stream) {
+  if (!x || !w || !y || !M || !workspace) return fail(DL_INVALID_ARGUMENT, "gemm parts: null pointer or empty shape");
+  if (epilogue != dl::kGemmStore && epilogue != dl::kGemmResidual && epilogue != dl::kGemmSwiGLU)
+    return fail(DL_INVALID_ARGUMENT, "gemm parts: epilogue must be 0, 1 or 3");
+  if (!dl::gemm_tcgen05_supported(int(M), int(N), int(K)) || ldx % 8 || ldx < K ||
+      (reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) % 16)
+    return fail(DL_UNSUPPORTED, "gemm parts: K % 64, N % 128, 8-element row stride and 16-byte alignment required");
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int p = parts ? int(parts) : dl::gemm_splitk_parts(int(M), int(N), int(K), sms);
+  if (p < 1 || p > 16 || (K / 64) % size_t(p)) return fail(DL_INVALID_ARGUMENT, "gemm parts: parts must divide K/64");
+  dl::GemmProblem g = {};
+  g.x = static_cast<const bf16*>(x);
+  g.ldx = int(ldx);
+  g.w = static_cast<const bf16*>(w);
+  g.M = int(M);
+  g.N = int(N);
+  g.K = int(K);
+  const dl_status s1 = cuda_status(dl::launch_gemm_tcgen05_parts(g, p, static_cast<float*>(workspace), st(stream)),
+                                   "gemm parts");
+  if (s1 != DL_OK) return s1;
+  return cuda_status(dl::launch_gemm_splitk_epilogue(static_cast<const float*>(workspace), p, int(M), int(N), epilogue,
+                                                     static_cast<bf16*>(y), int(ldy), nullptr, st(stream)),
+                     "gemm parts epilogue");
+}
+
+DL_API size_t dl_attention_decode_batched_workspace_bytes(size_t batch, size_t query_heads, size_t kv_heads,
+                                                          size_t capacity) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int splits = dl::attention_decode_splits(int(batch), int(kv_heads), int(capacity), sms);
+  return dl::attention_decode_ws_floats(int(batch), int(query_heads), splits) * 4;
+}
+
+DL_API dl_status dl_attention_decode_batched(const void* query, const void* kv, size_t seq_stride,
+                                             size_t k_offset, size_t v_offset, const int64_t* position,
+                                             size_t batch, size_t query_heads, size_t kv_heads, size_t capacity,
+                                             void* output, void* workspace, void* stream) {
+  if (!query || !kv || !position || !output || !workspace || !batch || !kv_heads)
+    return fail(DL_INVALID_ARGUMENT, "attention decode batched: null pointer or empty shape");
+  if (query_heads % kv_heads || query_heads / kv_heads > 8 ||
+      (seq_stride | k_offset | v_offset) % 8 || reinterpret_cast<uintptr_t>(kv) % 16)
+    return fail(DL_UNSUPPORTED, "attention decode batched: group <= 8, 16-byte aligned rows");
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int splits = dl::attention_decode_splits(int(batch), int(kv_heads), int(capacity), sms);
+  const dl::KvPlanes planes{static_cast<bf16*>(const_cast<void*>(kv)), seq_stride, k_offset, v_offset};
+  return cuda_status(dl::launch_attention_decode_batched(static_cast<const bf16*>(query), planes,
+                                                         reinterpret_cast<const long long*>(position), int(batch),
+                                                         int(query_heads), int(kv_heads), splits,
+                                                         dl::attention_scale(128), static_cast<float*>(workspace),
+                                                         static_cast<bf16*>(output), st(stream)),
+                     "attention decode batched");
 }
 
 }  // extern "C"

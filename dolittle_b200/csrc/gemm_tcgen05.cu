@@ -44,9 +44,10 @@ struct alignas(64) GemmArgs {
   bf16* seg_out[3];
   int seg_ld[3];
   unsigned* err;
-  int split;           // 1, or 2 K halves per tile
-  float* partial;      // [2][M][N] FP32 (split 2)
-  unsigned* tickets;   // per tile (split 2)
+  int split;           // K parts per tile
+  float* partial;      // [split][M][N] FP32
+  unsigned* tickets;   // per tile (split 2 with the epilogue in the kernel)
+  int partial_only;    // every part stores its FP32 partial; no epilogue
 };
 
 __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -237,7 +238,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
       const int ld = a.seg_ld[si];
       const int c0 = n0 - a.seg_n0[si];
       const uint32_t acc = tmem + uint32_t(buf * BN) + (uint32_t(q * 32) << 16);
-      if (a.split == 1) {
+      if (a.partial_only) {
+        // K part `half` of the tile as FP32; the split-K epilogue kernel adds
+        // the parts in order.
+        float* mine = a.partial + (size_t(half) * a.M + row) * a.N + n0;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(acc + uint32_t(c * 32), r);
+          if (row < a.M) {
+            uint4* d = reinterpret_cast<uint4*>(mine + c * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) d[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+          }
+        }
+      } else if (a.split == 1) {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
@@ -329,6 +344,89 @@ bool encode_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
 
 bool gemm_tcgen05_supported(int M, int N, int K) { return M > 0 && K % kBK == 0 && N % 128 == 0; }
 
+namespace {
+
+// Sum of the K parts in part order, then the epilogue of the un-split kernel
+// (store / residual / SwiGLU), or the FP32 sum itself.  One thread per pair
+// of columns.
+__global__ void splitk_epilogue_kernel(const float* __restrict__ parts, int splits, int M, int N, int epilogue,
+                                       bf16* out, int ld, float* sum_out) {
+  const size_t pairs = size_t(M) * (N / 2);
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < pairs; i += size_t(gridDim.x) * blockDim.x) {
+    const int m = int(i / (N / 2)), n = int(i % (N / 2)) * 2;
+    float2 acc = *reinterpret_cast<const float2*>(parts + size_t(m) * N + n);
+    for (int s = 1; s < splits; ++s) {
+      const float2 v = *reinterpret_cast<const float2*>(parts + (size_t(s) * M + m) * N + n);
+      acc.x = __fadd_rn(acc.x, v.x);
+      acc.y = __fadd_rn(acc.y, v.y);
+    }
+    if (sum_out) {
+      *reinterpret_cast<float2*>(sum_out + size_t(m) * N + n) = acc;
+      continue;
+    }
+    if (epilogue == kGemmSwiGLU) {
+      out[size_t(m) * ld + n / 2] = narrow(swiglu_law(round_bf16(acc.x), round_bf16(acc.y)));
+    } else if (epilogue == kGemmResidual) {
+      bf16* d = out + size_t(m) * ld + n;
+      const float y0 = round_bf16(acc.x), y1 = round_bf16(acc.y);
+      const __nv_bfloat162 h2 = __floats2bfloat162_rn(__fadd_rn(widen(d[0]), y0), __fadd_rn(widen(d[1]), y1));
+      *reinterpret_cast<__nv_bfloat162*>(d) = h2;
+    } else {
+      *reinterpret_cast<__nv_bfloat162*>(out + size_t(m) * ld + n) = __floats2bfloat162_rn(acc.x, acc.y);
+    }
+  }
+}
+
+}  // namespace
+
+int gemm_splitk_parts(int M, int N, int K, int sms) {
+  const int mt = (M + kBM - 1) / kBM, tiles = mt * (N / 128), kt = K / kBK;
+  int best = 1;
+  for (int s = 1; s <= 16; ++s)
+    if (kt % s == 0 && kt / s >= 4 && tiles * s <= sms) best = s;
+  return best;
+}
+
+cudaError_t launch_gemm_tcgen05_parts(const GemmProblem& p, int splits, float* parts, cudaStream_t stream) {
+  if (!gemm_tcgen05_supported(p.M, p.N, p.K) || splits < 1 || splits > 16 || (p.K / kBK) % splits || !parts)
+    return cudaErrorInvalidValue;
+  GemmArgs a = {};
+  constexpr int BN = 128;
+  if (!encode_2d(&a.map_a, p.x, uint64_t(p.M), uint64_t(p.K), uint64_t(p.ldx), kBM)) return cudaErrorInvalidValue;
+  if (!encode_2d(&a.map_b, p.w, uint64_t(p.N), uint64_t(p.K), uint64_t(p.K), uint32_t(BN))) return cudaErrorInvalidValue;
+  a.M = p.M;
+  a.N = p.N;
+  a.K = p.K;
+  a.epilogue = kGemmStore;
+  a.nseg = 1;
+  a.err = p.err;
+  a.split = splits;
+  a.partial = parts;
+  a.partial_only = 1;
+  const int stage_bytes = (kBM + BN) * kBK * 2;
+  a.stages = std::min(8, (200 * 1024) / stage_bytes);
+  const size_t smem = size_t(a.stages) * stage_bytes + 1024;
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long units = (long long)((p.M + kBM - 1) / kBM) * (p.N / BN) * splits;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(std::min<long long>(units, sms)));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaFuncSetAttribute(gemm_tcgen05_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  return cudaLaunchKernelEx(&cfg, gemm_tcgen05_kernel<BN>, a);
+}
+
+cudaError_t launch_gemm_splitk_epilogue(const float* parts, int splits, int M, int N, int epilogue, bf16* out,
+                                        int ld, float* sum_out, cudaStream_t stream) {
+  if (N % 2 || splits < 1 || (!out && !sum_out)) return cudaErrorInvalidValue;
+  const size_t pairs = size_t(M) * (N / 2);
+  const unsigned blocks = unsigned(std::min<size_t>((pairs + 255) / 256, 148 * 16));
+  splitk_epilogue_kernel<<<blocks, 256, 0, stream>>>(parts, splits, M, N, epilogue, out, ld, sum_out);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool pdl) {
   if (!gemm_tcgen05_supported(p.M, p.N, p.K) || p.nseg < 1 || p.nseg > 3) return cudaErrorInvalidValue;
   GemmArgs a = {};
@@ -338,10 +436,12 @@ cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool 
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const long long mt = (p.M + kBM - 1) / kBM;
   const long long waves256 = (mt * (p.N / 256) + sms - 1) / sms, waves128 = (mt * (p.N / 128) + sms - 1) / sms;
-  int BN = (p.N % 256 == 0 && p.wide_tiles && 2 * waves256 <= waves128) ? 256 : 128;
+  bool aligned256 = p.N % 256 == 0;
+  for (int i = 0; i < p.nseg; ++i) aligned256 = aligned256 && p.seg_n0[i] % 256 == 0;
+  int BN = (aligned256 && p.wide_tiles && 2 * waves256 <= waves128) ? 256 : 128;
   // Split K in two when even 128-wide tiles would leave half the SMs idle.
   int split = 1;
-  if (p.partial && p.tickets && p.M <= p.partial_rows && (p.K / kBK) % 2 == 0 && p.N % 256 == 0 && p.wide_tiles &&
+  if (p.partial && p.tickets && p.M <= p.partial_rows && (p.K / kBK) % 2 == 0 && aligned256 && p.wide_tiles &&
       2 * mt * (p.N / 256) <= sms) {
     BN = 256;
     split = 2;

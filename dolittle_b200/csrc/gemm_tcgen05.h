@@ -35,4 +35,14 @@ struct GemmProblem {
 bool gemm_tcgen05_supported(int M, int N, int K);
 cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool pdl);
 
+// Split-K for few rows (batched decode): the K extent in `splits` equal parts,
+// each (tile, part) unit storing its FP32 partial into parts[splits][M][N];
+// then the epilogue kernel adds the parts in part order and applies
+// `epilogue` into out (row stride ld), or writes the FP32 sum to sum_out.
+// Only p.x, p.ldx, p.w, M, N, K and err are read from p.
+int gemm_splitk_parts(int M, int N, int K, int sms);  // parts that fill the SMs
+cudaError_t launch_gemm_tcgen05_parts(const GemmProblem& p, int splits, float* parts, cudaStream_t stream);
+cudaError_t launch_gemm_splitk_epilogue(const float* parts, int splits, int M, int N, int epilogue, bf16* out,
+                                        int ld, float* sum_out, cudaStream_t stream);
+
 }  // namespace dl

@@ -6,6 +6,7 @@
 #include <cmath>
 
 #include "launch.h"
+#include "qknorm.cuh"
 
 namespace dl {
 namespace {
@@ -45,47 +46,17 @@ __global__ void qk_norm_rope_kernel(const bf16* __restrict__ q_raw, const bf16* 
   __shared__ float vals[kNormWarps][128];
   allow_next();
   wait_prior();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   const int r = blockIdx.x;
   const int head = blockIdx.y * kNormWarps + warp;
   if (head >= query_heads + kv_heads) return;
   const bool is_q = head < query_heads;
   const bf16* src = is_q ? q_raw + (size_t(r) * query_heads + head) * width
                          : k_raw + (size_t(r) * kv_heads + (head - query_heads)) * width;
-  const bf16* w = is_q ? qw : kw;
-  float x[4];
-  float part[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const int col = lane + 32 * c;
-    x[c] = col < width ? widen(src[col]) : 0.f;
-    if (col < width) part[c] = __fmul_rn(x[c], x[c]);
-  }
-  float sum = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), part[2]), part[3]);
-  sum = shuffle_down_tree32(sum);
-  const float total = __shfl_sync(0xffffffffu, sum, 0);
-  const float inv = rsqrtf(__fadd_rn(__fmul_rn(total, 1.0f / static_cast<float>(width)), eps));
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const int col = lane + 32 * c;
-    if (col < width)
-      vals[warp][col] = round_bf16(__fmul_rn(round_bf16(__fmul_rn(x[c], inv)), widen(w[col])));
-  }
-  __syncwarp();
   const int p = row_position(pos, r);
-  const int half = width / 2;
   bf16* dst = is_q ? q_out + (size_t(r) * query_heads + head) * width
                    : k_cache + (size_t(p) * kv_heads + (head - query_heads)) * width;
-  for (int f = lane; f < half; f += 32) {
-    const float angle = __fmul_rn(static_cast<float>(p), inv_freq[f]);
-    const float co = round_bf16(cosf(angle));
-    const float si = round_bf16(sinf(angle));
-    const float a = vals[warp][f], b = vals[warp][f + half];
-    const float ac = round_bf16(__fmul_rn(a, co)), bs = round_bf16(__fmul_rn(b, si));
-    const float bc = round_bf16(__fmul_rn(b, co)), as = round_bf16(__fmul_rn(a, si));
-    dst[f] = narrow(__fsub_rn(ac, bs));
-    dst[f + half] = narrow(__fadd_rn(bc, as));
-  }
+  qk_norm_rope_warp(src, is_q ? qw : kw, inv_freq, p, dst, width, eps, vals[warp]);
 }
 
 // ---------------------------------------------------------------------------
@@ -381,33 +352,12 @@ __global__ void inv_freq_kernel(float* out, int width, double theta) {
 // BF16 rounding.  Integer-only up to the multiply, so a host restatement of
 // the same algorithm reproduces the bits.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void philox4x32_10(uint32_t (&c)[4], uint32_t k0, uint32_t k1) {
-#pragma unroll
-  for (int round = 0; round < 10; ++round) {
-    const uint64_t p0 = uint64_t(0xD2511F53u) * c[0];
-    const uint64_t p1 = uint64_t(0xCD9E8D57u) * c[2];
-    const uint32_t n0 = uint32_t(p1 >> 32) ^ c[1] ^ k0;
-    const uint32_t n1 = uint32_t(p1);
-    const uint32_t n2 = uint32_t(p0 >> 32) ^ c[3] ^ k1;
-    const uint32_t n3 = uint32_t(p0);
-    c[0] = n0; c[1] = n1; c[2] = n2; c[3] = n3;
-    k0 += 0x9E3779B9u;
-    k1 += 0xBB67AE85u;
-  }
-}
-
 // Element i of a logical [rows][cols] tensor lands at row (i/cols) of a
 // resident layout with `row_stride` elements per row.
 __global__ void fill_normal_kernel(bf16* out, size_t n, size_t cols, size_t row_stride, uint64_t seed,
                                    uint32_t stream_id, float scale) {
-  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
-    uint32_t c[4] = {uint32_t(i), uint32_t(uint64_t(i) >> 32), stream_id, 0u};
-    philox4x32_10(c, uint32_t(seed), uint32_t(seed >> 32));
-    int s = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) s += int(c[j] & 0xffffu) + int(c[j] >> 16);
-    out[(i / cols) * row_stride + i % cols] = narrow(__fmul_rn(static_cast<float>(s - 262140), scale));
-  }
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
+    out[(i / cols) * row_stride + i % cols] = normal_bf16(uint64_t(i), seed, stream_id, scale);
 }
 
 __global__ void fill_const_kernel(bf16* out, size_t n, float value) {

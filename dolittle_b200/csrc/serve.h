@@ -1,0 +1,108 @@
+// Server: lockstep batched serving of B sequences on one GPU, or on one rank
+// of a tensor-parallel group over KV-head groups.  The long-context serving
+// workload of the reference runs each sequence through CachedForwardPlan
+// (src/inference/executor.cpp:1482-1716) one at a time; here the B sequences
+// share every weight read:
+//  * prompt pass per sequence in chunks: tcgen05 GEMMs (M = chunk rows),
+//    the tcgen05 causal attention over that sequence's cache;
+//  * decode step for all B rows at once: split-K tcgen05 GEMMs (M = B), the
+//    exact QK-norm + RoPE + KV append, split-K flash decoding over each
+//    sequence's cache, per-row sampling;
+//  * tensor parallelism over KV-head groups (rank r of t holds query heads
+//    [r Hq/t, (r+1) Hq/t), the matching KV heads and MLP columns): q/k/v and
+//    gate/up are column slices, o_proj and down_proj row slices whose FP32
+//    partial sums meet in an NCCL all-reduce before the residual add.
+// All sequences have the same prompt length and advance together, so one
+// device position serves the batch.  The decode step is one CUDA graph
+// (the all-reduces included).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <vector>
+
+#include "../../include/dolittle_b200.h"
+#include "engine.h"
+#include "sampler.h"
+#include "serve_kernels.h"
+
+namespace dl {
+
+class Server {
+ public:
+  Server(const dl_model_config& cfg, int device, size_t batch, size_t capacity, size_t chunk_rows, int tp_rank,
+         int tp_size);
+  ~Server();
+
+  static void nccl_id(unsigned char* out128);
+  void connect(const unsigned char* id128);
+  void init_random(uint64_t seed, float sigma);
+  // Full tensor `index` (engine order) from the host; this rank keeps its slice.
+  void set_tensor(size_t index, const void* host, size_t bytes);
+  // This rank's slice of tensor `index` ([rows][cols] as held).
+  void get_tensor(size_t index, void* host, size_t bytes);
+  bool slice_shape(size_t index, size_t* rows, size_t* cols, size_t* r0, size_t* c0);
+  void prefill(const uint32_t* tokens, size_t prompt_len, const dl_sampling& s, uint64_t seed, uint32_t* first_out);
+  void decode(size_t steps, uint32_t* tokens_out, uint16_t* logits_out, dl_serve_stats* stats);
+  size_t position();
+
+ private:
+  struct Slice {
+    bf16* ptr;
+    size_t rows, cols, stride, r0, c0, full_cols;
+  };
+  Slice slice(size_t index);
+  KvPlanes planes(size_t layer) const;
+  bf16* vcache(size_t b, size_t layer) const;
+  bf16* kcache(size_t b, size_t layer) const;
+  void gemm(const bf16* x, int ldx, const bf16* w, int M, int N, int K, int epi, int nseg, const int* n0s,
+            bf16* const* outs, const int* lds);
+  void row_projection_out(const bf16* x, int ldx, const bf16* w, int M, int K, bool decode);  // o / down
+  void prefill_sequence(size_t b, const uint32_t* tokens, size_t n);
+  void decode_body();
+  void all_reduce(float* buf, size_t n);
+  void check(cudaError_t e, const char* what);
+  void check_nccl(ncclResult_t r, const char* what);
+  void check_fault();
+
+  dl_model_config cfg_;
+  int device_, sms_ = 148;
+  size_t batch_, capacity_, chunk_;
+  int rank_, tp_;
+  int hq_, hkv_;        // local heads
+  size_t D_, Ql_, Gl_, Fl_, V_, d_, L_;
+  cudaStream_t stream_ = nullptr;
+  ncclComm_t comm_ = nullptr;
+  // weights (local slices)
+  void* weight_arena_ = nullptr;
+  bf16 *embed_ = nullptr, *final_norm_ = nullptr, *lm_head_ = nullptr;
+  std::vector<Layer> layers_;
+  float* inv_freq_ = nullptr;
+  // KV: [B][L][2][C][Gl]
+  void* kv_arena_ = nullptr;
+  size_t plane_elems_ = 0, seq_elems_ = 0;
+  // scratch
+  void* scratch_ = nullptr;
+  bf16 *residual_, *xn_, *qkv_, *q_raw_, *k_raw_, *q_rot_, *att_, *act_, *logits_, *xlast_, *vt_;
+  float *parts_, *attn_ws_;
+  size_t parts_floats_ = 0;
+  uint32_t* tokens_dev_;
+  uint32_t* history_;
+  int* steps_;
+  long long* position_;
+  unsigned* err_;
+  size_t history_cap_ = 0;
+  int vt_stride_ = 0;
+  int attn_splits_ = 1;
+  std::vector<AttnTcMaps*> attn_maps_;
+  std::vector<Sampler> samplers_;
+  dl_sampling settings_ = {0, 1.0, 0, 1.0};
+  bool started_ = false;
+  cudaGraphExec_t step_exec_ = nullptr;
+  size_t kernels_per_step_ = 0;
+  size_t launches_ = 0;
+  cudaEvent_t ev_[2] = {};
+};
+
+}  // namespace dl

@@ -1,0 +1,48 @@
+// Kernels of the batched serving step (serve_kernels.cu): lockstep batches of
+// sequences, each with its own KV arena, and tensor-parallel slices.
+#pragma once
+
+#include "launch.h"
+
+namespace dl {
+
+// Where block l's K / V rows of sequence b live: kv + b * seq_stride + k_off
+// (or v_off) + position * (kv_heads * width), elements.
+struct KvPlanes {
+  bf16* kv;
+  size_t seq_stride;
+  size_t k_off, v_off;
+};
+
+// Rows [r0, r0 + rows) x columns [c0, c0 + cols) of the seeded tensor with
+// `full_cols` columns (element index r * full_cols + c), into out (row stride
+// out_stride): any tensor-parallel slice of the same weights.
+cudaError_t launch_fill_normal_slice(bf16* out, size_t rows, size_t cols, size_t out_stride, size_t full_cols,
+                                     size_t r0, size_t c0, uint64_t seed, uint32_t stream_id, float scale,
+                                     cudaStream_t stream);
+
+// Batched decode: row b of qkv [B][Hq*d + 2*Hkv*d] (row stride ld) is
+// sequence b's token at the shared position *position.  Queries get QK-norm
+// + RoPE into q_out [B][Hq][d]; keys get QK-norm + RoPE and values are copied,
+// both into sequence b's cache at that position.
+cudaError_t launch_norm_rope_append_rows(const bf16* qkv, int ld, const bf16* q_norm_w, const bf16* k_norm_w,
+                                         const float* inv_freq, bf16* q_out, KvPlanes planes,
+                                         const long long* position, int batch, int query_heads, int kv_heads,
+                                         int width, float eps, cudaStream_t stream);
+
+// Split-K flash decoding: for every sequence b and query head h, attention of
+// q [B][Hq][128] over keys 0 .. *position of b's cache, the keys cut into
+// `splits` ranges whose (max, sum, unnormalised output) go to ws
+// [B][Hq][splits][130] FP32; the combine kernel merges them into out
+// [B][Hq*128] BF16.  Online softmax: not the reference's reduction order.
+size_t attention_decode_ws_floats(int batch, int query_heads, int splits);
+int attention_decode_splits(int batch, int kv_heads, int capacity, int sms);
+cudaError_t launch_attention_decode_batched(const bf16* q, KvPlanes planes, const long long* position, int batch,
+                                            int query_heads, int kv_heads, int splits, float scale, float* ws,
+                                            bf16* out, cudaStream_t stream);
+
+// residual[m][n] = round(residual + round(sum[m][n])): the residual epilogue
+// applied to an FP32 sum (after the tensor-parallel all-reduce).
+cudaError_t launch_add_fp32_residual(const float* sum, bf16* residual, size_t n, cudaStream_t stream);
+
+}  // namespace dl

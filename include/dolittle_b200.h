@@ -295,6 +295,73 @@ DL_API dl_status dl_engine_generate(dl_engine* e, const uint32_t* prompt, size_t
                                     uint32_t* tokens_out, size_t* n_out, uint16_t* logits_out,
                                     dl_generation_stats* stats);
 
+/* ------------------------------------------------------------------------ */
+/* Batched serving (the long-context serving workload): B sequences of one  */
+/* prompt length advancing in lockstep, on one GPU or one rank of a        */
+/* tensor-parallel group over KV-head groups.  Replaces running each       */
+/* sequence through CachedForwardPlan::prepare_device_generation /         */
+/* start_sequence (src/inference/executor.cpp:1482-1716) one at a time.    */
+/* Fast path: tcgen05 GEMMs, online-softmax flash decoding; checked        */
+/* against the reference law within tolerance.                              */
+/* ------------------------------------------------------------------------ */
+typedef struct dl_serve dl_serve;
+
+typedef struct {
+  double prefill_ms;
+  double decode_ms;       /* device time of the decode steps */
+  uint64_t decode_steps;
+  uint64_t kernels_per_decode_step;
+} dl_serve_stats;
+
+/* Rank tp_rank of tp_size (1 = single GPU): query heads, KV heads and MLP
+ * columns are split in tp_size equal slices (tp_size must divide the KV
+ * heads).  chunk_rows: prompt rows per pass (<= 4096). */
+DL_API dl_status dl_serve_create(const dl_model_config* config, int device, size_t batch, size_t capacity,
+                                 size_t chunk_rows, int tp_rank, int tp_size, dl_serve** out);
+DL_API void dl_serve_destroy(dl_serve* s);
+/* NCCL communicator: rank 0 makes the 128-byte id, every rank passes the
+ * same id to dl_serve_connect (all ranks concurrently). */
+DL_API dl_status dl_serve_nccl_id(unsigned char* id128);
+DL_API dl_status dl_serve_connect(dl_serve* s, const unsigned char* id128);
+/* Seeded weights as dl_engine_init_random; each rank generates only its
+ * slice of the same tensors. */
+DL_API dl_status dl_serve_init_random(dl_serve* s, uint64_t seed, float sigma);
+/* Full tensor `index` (engine order, host BF16 bits); the rank keeps its
+ * slice.  dl_serve_get_tensor returns the slice [rows][cols] held, at
+ * rows r0.., columns c0.. of the full tensor (dl_serve_slice_shape). */
+DL_API dl_status dl_serve_set_tensor(dl_serve* s, size_t index, const void* host_bits, size_t bytes);
+DL_API dl_status dl_serve_get_tensor(dl_serve* s, size_t index, void* host_bits, size_t bytes);
+DL_API dl_status dl_serve_slice_shape(dl_serve* s, size_t index, size_t* rows, size_t* cols, size_t* r0,
+                                      size_t* c0);
+/* tokens [batch][prompt_len] (host): prompt pass of every sequence, then
+ * each sequence's first selection (sampler seed = seed + sequence index)
+ * into first_tokens [batch] (host). */
+DL_API dl_status dl_serve_prefill(dl_serve* s, const uint32_t* tokens, size_t prompt_len,
+                                  const dl_sampling* settings, uint64_t seed, uint32_t* first_tokens);
+/* `steps` decode steps of every sequence: tokens_out [steps][batch] (host),
+ * logits_out (optional, host) [steps][batch][V] BF16. */
+DL_API dl_status dl_serve_decode(dl_serve* s, size_t steps, uint32_t* tokens_out, uint16_t* logits_out,
+                                 dl_serve_stats* stats);
+DL_API size_t dl_serve_position(dl_serve* s);
+
+/* Split-K GEMM for few rows: Y = epilogue(X W^T) as dl_gemm_bf16, the K
+ * extent cut in `parts` (0 = fill the SMs) whose FP32 partials
+ * (dl_gemm_bf16_parts_workspace_bytes) are added in part order. */
+DL_API size_t dl_gemm_bf16_parts_workspace_bytes(size_t M, size_t N, size_t K, size_t parts);
+DL_API dl_status dl_gemm_bf16_parts(const void* x, size_t ldx, const void* w, void* y, size_t ldy, size_t M,
+                                    size_t N, size_t K, int epilogue, size_t parts, void* workspace,
+                                    void* stream);
+/* Batched decode attention (head width 128): query [B][Hq][128]; sequence
+ * b's keys 0..*position at kv + b*seq_stride + k_offset (values at
+ * v_offset) + j*Hkv*128, elements; out [B][Hq*128] BF16; workspace of
+ * dl_attention_decode_batched_workspace_bytes FP32. */
+DL_API size_t dl_attention_decode_batched_workspace_bytes(size_t batch, size_t query_heads, size_t kv_heads,
+                                                          size_t capacity);
+DL_API dl_status dl_attention_decode_batched(const void* query, const void* kv, size_t seq_stride,
+                                             size_t k_offset, size_t v_offset, const int64_t* position,
+                                             size_t batch, size_t query_heads, size_t kv_heads, size_t capacity,
+                                             void* output, void* workspace, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

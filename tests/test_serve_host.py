@@ -1,0 +1,76 @@
+"""Tensor-parallel host logic on CPU: the slice layout every rank holds, and
+the NCCL id exchange over a two-rank gloo group (stand-in server; the id
+factory is the only library call and is replaced here)."""
+import os
+import socket
+
+import pytest
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import dolittle_b200 as dl
+from dolittle_b200 import serve
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("size", [1, 2, 4, 8])
+def test_slices_tile_every_tensor_exactly_once(size):
+    cfg = dl.Qwen3Config(layers=2)
+    per_rank = [serve.tp_slices(cfg, r, size) for r in range(size)]
+    for i in range(cfg.tensor_count()):
+        rows, cols = cfg.tensor_shape(i)
+        pieces = [p[i] for p in per_rank]
+        if all(p == (rows, cols, 0, 0) for p in pieces):
+            continue  # replicated
+        covered = set()
+        for r, c, r0, c0 in pieces:
+            assert (r == rows) != (c == cols), (i, pieces)  # cut along exactly one dimension
+            span = range(r0, r0 + r) if c == cols else range(c0, c0 + c)
+            assert not covered & set(span)
+            covered |= set(span)
+        assert covered == set(range(rows if pieces[0][1] == cols else cols)), i
+
+
+def test_slices_follow_kv_head_groups():
+    cfg = dl.Qwen3Config(layers=1)
+    q, k, v, o, gate, down = 3 + 1, 3 + 2, 3 + 3, 3 + 6, 3 + 8, 3 + 10
+    s = serve.tp_slices(cfg, 1, 4)
+    assert s[q] == (1024, 4096, 1024, 0)       # query heads 8..15
+    assert s[k] == s[v] == (256, 4096, 256, 0)  # KV heads 2..3 (the same GQA groups)
+    assert s[o] == (4096, 1024, 0, 1024)
+    assert s[gate] == (3072, 4096, 3072, 0)
+    assert s[down] == (4096, 3072, 0, 3072)
+    with pytest.raises(ValueError):
+        serve.tp_slices(cfg, 0, 3)
+
+
+class _FakeServer:
+    def __init__(self):
+        self.got = None
+
+    def connect(self, nccl_id):
+        self.got = nccl_id
+
+
+def _rank_main(rank, world, port):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        srv = _FakeServer()
+        made = []
+        got = serve.connect_group(srv, dist, make_id=lambda: made.append(1) or bytes(range(128)))
+        assert srv.got == got == bytes(range(128))
+        assert made == ([1] if rank == 0 else [])  # only rank 0 makes the id
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_nccl_id_reaches_every_rank():
+    mp.spawn(_rank_main, args=(2, _free_port()), nprocs=2, join=True)
