@@ -447,6 +447,106 @@ def run_ours(args):
     return 0
 
 
+def run_serve(args):
+    """Config 5 (batched long-context serving): B sequences of P uniform IDs,
+    then decode steps at temperature 0.8 / top-p 0.95, tensor-parallel over
+    KV-head groups across the launched ranks (TP = N)."""
+    world, rank, local = dist_setup()
+    import torch
+    torch.cuda.set_device(local)
+    import torch.distributed as dist
+    from datetime import timedelta
+    import numpy as np
+    import dolittle_b200 as dl
+    from dolittle_b200 import replicas
+    from dolittle_b200.serve import Server, connect_group
+    pg = world > 1
+    if pg:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+    hbm, tflops, kind = peaks()
+    cfg = dl.QWEN3_8B
+    B, P, steps = args.serve_batch, args.serve_prompt, args.serve_steps
+    srv = Server(cfg, batch=B, capacity=P + steps * (args.steps + args.warmup) + 8, chunk_rows=2048, device=local,
+                 tp_rank=rank, tp_size=world)
+    srv.init_random(SEED, 0.02)
+    if pg:
+        connect_group(srv, dist)
+    V = cfg.vocabulary
+    rng = np.random.default_rng(SEED + 5)
+    prompts = rng.integers(0, V, size=(B, P), dtype=np.uint32)
+    settings = dl.Settings(dl.SelectionMode.categorical, temperature=0.8, top_p=0.95)
+    t0 = time.perf_counter()
+    srv.prefill(prompts, settings, seed=7)
+    wall_prefill = time.perf_counter() - t0
+    first = srv.decode(steps)  # warm-up: graph capture and the first steps
+    for _ in range(args.warmup - 1):
+        srv.decode(steps)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if pg:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    clocks = Clocks(local)
+    barrier()
+    outs = []
+    t1 = time.perf_counter()
+    for _ in range(args.steps):
+        outs.append(srv.decode(steps))
+    wall = time.perf_counter() - t1
+    barrier()
+    clk = clocks.stop()
+    decode_s = sum(o.decode_ms for o in outs) / 1000.0
+    prefill_s = first.prefill_ms / 1000.0
+    decode_s, prefill_s, wall = replicas.max_over_ranks(dist if pg else None, [decode_s, prefill_s, wall])
+    total_steps = args.steps * steps
+    value = B * total_steps / decode_s
+    if rank == 0:
+        # Bytes one decode step must move per GPU: this rank's weights plus its
+        # KV heads of every sequence (mean context over the timed steps).
+        Dm, Lm = cfg.hidden, cfg.layers
+        d = cfg.head_width
+        w_layer = Dm * (cfg.query_heads * d + 2 * cfg.kv_heads * d) + cfg.query_heads * d * Dm + 3 * Dm * cfg.mlp_width
+        weights = 2 * (Lm * w_layer / world + Dm * V)
+        S0 = P + (1 + args.warmup) * steps
+        mean_S = S0 + total_steps / 2.0
+        kv_bytes = B * mean_S * Lm * 2 * (cfg.kv_heads // world) * d * 2
+        step_bytes = weights + kv_bytes
+        ms_step = 1000 * decode_s / total_steps
+        achieved = step_bytes / (ms_step * 1e-3) / 1e9
+        pf_flops = B * prefill_flops(P) / world
+        line = {
+            "metric": "Qwen3-8B batched serving decode tok/s (config 5)", "value": value, "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init BF16 weights ~N(0,0.02), uniform prompt IDs)",
+            "config": {"workload": f"Qwen3-8B config 5: batch {B}, prompts of {P} uniform IDs, decode at "
+                                   f"temperature 0.8 / top-p 0.95, {steps} decode steps per timed call",
+                       "parallelism": f"tp{world} over KV-head groups (NCCL all-reduce after o_proj, down_proj)"
+                                      if world > 1 else "single GPU",
+                       "l2": "weights + KV cache (tens of GB) exceed L2"},
+            "prefill_tok_s": B * P / prefill_s,
+            "prefill_roofline": {"bound": "tensor", "achieved": pf_flops / prefill_s / 1e12, "peak": tflops,
+                                 "unit": "TFLOP/s", "frac": pf_flops / prefill_s / 1e12 / tflops},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "traffic": None, "bytes_per_step_per_gpu": step_bytes, "peak_kind": kind,
+                         "kernel": "decode step graph (split-K tcgen05 GEMMs + flash decoding + sampling)"},
+            "e2e": {"value": B * total_steps / wall, "unit": "tok/s (host loop incl. token readback)",
+                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": B * 4},
+            "gpu_launches": outs[0].kernels_per_decode_step * total_steps,
+            "kernels_per_decode_step": outs[0].kernels_per_decode_step,
+            "wall_prefill_s": wall_prefill,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    srv.close()
+    if pg:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_profile_case(args):
     """Small standalone cases for ncu captures (a few hundred MB on device).
 
@@ -502,7 +602,14 @@ def main():
                     help="prompt pass on the tcgen05 GEMMs (fast) or in the reference order (parity)")
     ap.add_argument("--profile", choices=["gemv", "decode", "prefill", "persist"], default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
+    ap.add_argument("--workload", choices=["decode", "serve"], default="decode",
+                    help="decode: config 2 (headline); serve: config 5 batched serving, TP over the ranks")
+    ap.add_argument("--serve-batch", type=int, default=32)
+    ap.add_argument("--serve-prompt", type=int, default=8192)
+    ap.add_argument("--serve-steps", type=int, default=32, help="decode steps per timed call (config 5)")
     args = ap.parse_args()
+    if args.workload == "serve" and args.impl == "ours":
+        return run_serve(args)
     if args.profile:
         return run_profile_case(args)
     if args.impl == "reference":

@@ -15,6 +15,7 @@
 // the high 16 bits alone gives the same order (two passes instead of four).
 #include <cstring>
 #include <stdexcept>
+#include <type_traits>
 #include <vector>
 
 #include "sampler.h"
@@ -71,6 +72,14 @@ Layout layout(void* arena, size_t n) {
   return L;
 }
 
+// Row r of a batched sampler (blockIdx.y) owns the arena slice at r * stride
+// bytes; its logits row sits at r * row_bytes past row 0.
+template <class T>
+__device__ __forceinline__ T* at_row(T* p, size_t stride) {
+  using U = typename std::conditional<std::is_const<T>::value, const unsigned char, unsigned char>::type;
+  return p ? reinterpret_cast<T*>(reinterpret_cast<U*>(p) + blockIdx.y * stride) : p;
+}
+
 __device__ __forceinline__ float load_logit(const void* row, unsigned i, bool bf16_in) {
   return bf16_in ? widen(static_cast<const bf16*>(row)[i]) : static_cast<const float*>(row)[i];
 }
@@ -83,7 +92,9 @@ __device__ __forceinline__ unsigned descending_key(float v) {
 }
 
 // ---- MT19937-64 -----------------------------------------------------------
-__global__ void seed_kernel(SamplerState* s, uint64_t seed) {
+__global__ void seed_kernel(SamplerState* s, uint64_t seed, size_t stride) {
+  s = at_row(s, stride);
+  seed += blockIdx.y;  // row r draws from the stream seeded with seed + r
   s->words[0] = seed;
   for (unsigned i = 1; i < 312; ++i) {
     const uint64_t p = s->words[i - 1];
@@ -95,7 +106,8 @@ __global__ void seed_kernel(SamplerState* s, uint64_t seed) {
   s->previous[0] = s->previous[1] = 0;
 }
 
-__global__ void next_random_kernel(SamplerState* s, bool greedy) {
+__global__ void next_random_kernel(SamplerState* s, bool greedy, size_t stride) {
+  s = at_row(s, stride);
   if (s->terminal || greedy) return;
   if (s->index == 312) {
     for (unsigned i = 0; i < 312; ++i) {
@@ -112,7 +124,10 @@ __global__ void next_random_kernel(SamplerState* s, bool greedy) {
   s->draw = static_cast<double>(x >> 11) * 0x1.0p-53;
 }
 
-__global__ void commit_kernel(SamplerState* s, unsigned* result, const unsigned char* stops) {
+__global__ void commit_kernel(SamplerState* s, unsigned* result, const unsigned char* stops, size_t stride) {
+  s = at_row(s, stride);
+  result = at_row(result, stride);
+  stops = at_row(stops, stride);
   if (s->terminal) {
     result[0] = s->previous[0];
     result[1] = s->previous[1];
@@ -129,9 +144,13 @@ __device__ __forceinline__ bool better(float v, unsigned id, float bv, unsigned 
 }
 
 __global__ void greedy_kernel(const void* row, bool bf16_in, unsigned n, uint4* best, ScanState* scan,
-                              unsigned* result) {
+                              unsigned* result, size_t stride, size_t row_bytes) {
   __shared__ uint4 warp_best[kWarps];
   __shared__ bool last;
+  row = static_cast<const unsigned char*>(row) + blockIdx.y * row_bytes;
+  best = at_row(best, stride);
+  scan = at_row(scan, stride);
+  result = at_row(result, stride);
   const unsigned i = blockIdx.x * kW + threadIdx.x;
   float v = -INFINITY;
   unsigned id = 0xffffffffu, flags = 0;
@@ -176,7 +195,11 @@ __global__ void greedy_kernel(const void* row, bool bf16_in, unsigned n, uint4* 
 }
 
 // ---- categorical -------------------------------------------------------------
-__global__ void keys_kernel(const void* row, bool bf16_in, unsigned n, uint2* keys, unsigned* result) {
+__global__ void keys_kernel(const void* row, bool bf16_in, unsigned n, uint2* keys, unsigned* result, size_t stride,
+                            size_t row_bytes) {
+  row = static_cast<const unsigned char*>(row) + blockIdx.y * row_bytes;
+  keys = at_row(keys, stride);
+  result = at_row(result, stride);
   const unsigned i = blockIdx.x * kW + threadIdx.x;
   if (i >= n) return;
   const float v = load_logit(row, i, bf16_in);
@@ -195,8 +218,10 @@ __device__ __forceinline__ void block_digit_ranks(unsigned digit, bool live, uns
   __syncthreads();
 }
 
-__global__ void histogram_kernel(const uint2* keys, unsigned n, unsigned shift, unsigned* counts) {
+__global__ void histogram_kernel(const uint2* keys, unsigned n, unsigned shift, unsigned* counts, size_t stride) {
   __shared__ unsigned bins[kWarps][kW];
+  keys = at_row(keys, stride);
+  counts = at_row(counts, stride);
   const unsigned i = blockIdx.x * kW + threadIdx.x;
   const bool live = i < n;
   const unsigned digit = live ? (keys[i].x >> shift) & 0xffu : 0u;
@@ -207,36 +232,63 @@ __global__ void histogram_kernel(const uint2* keys, unsigned n, unsigned shift, 
   counts[blockIdx.x * kW + threadIdx.x] = total;
 }
 
-// Exclusive offsets in (digit, block) order.  One CTA, thread = digit.
-__global__ void digit_offsets_kernel(unsigned* counts, unsigned blocks) {
-  __shared__ unsigned totals[kW];
-  const unsigned d = threadIdx.x;
-  unsigned run = 0;
-  for (unsigned b = 0; b < blocks; ++b) {
-    const unsigned c = counts[b * kW + d];
-    counts[b * kW + d] = run;
-    run += c;
-  }
-  totals[d] = run;
-  __syncthreads();
-  // Exclusive scan of the 256 digit totals (integer: order-free).
-  unsigned v = run;
-  const unsigned lane = d & 31, warp = d >> 5;
-  for (unsigned off = 1; off < 32; off <<= 1) {
-    const unsigned o = __shfl_up_sync(0xffffffffu, v, off);
-    if (lane >= off) v += o;
-  }
+// Exclusive offsets in (digit, block) order: offset[b][d] = (sum of all
+// counts of digits < d) + (sum of counts[b' < b][d]).  Integer sums, so any
+// order gives the same offsets; one CTA per row, four block segments per
+// digit, loads batched ahead of the stores.
+constexpr unsigned kSeg = 4;
+__global__ void __launch_bounds__(kW * kSeg) digit_offsets_kernel(unsigned* counts, unsigned blocks, size_t stride) {
+  __shared__ unsigned seg[kSeg][kW];
+  __shared__ unsigned digit_base[kW];
   __shared__ unsigned warp_sum[kWarps];
-  if (lane == 31) warp_sum[warp] = v;
+  counts = at_row(counts, stride);
+  const unsigned d = threadIdx.x % kW, q = threadIdx.x / kW;
+  const unsigned per = (blocks + kSeg - 1) / kSeg;
+  const unsigned b0 = min(blocks, q * per), b1 = min(blocks, b0 + per);
+  unsigned sum = 0;
+#pragma unroll 8
+  for (unsigned b = b0; b < b1; ++b) sum += counts[b * kW + d];
+  seg[q][d] = sum;
   __syncthreads();
-  unsigned base = 0;
-  for (unsigned w = 0; w < warp; ++w) base += warp_sum[w];
-  const unsigned exclusive = base + v - run;
-  for (unsigned b = 0; b < blocks; ++b) counts[b * kW + d] += exclusive;
+  unsigned before = 0;
+  for (unsigned k = 0; k < q; ++k) before += seg[k][d];
+  if (q == 0) {
+    // Exclusive scan of the 256 digit totals.
+    unsigned total = 0;
+    for (unsigned k = 0; k < kSeg; ++k) total += seg[k][d];
+    unsigned v = total;
+    const unsigned lane = d & 31, warp = d >> 5;
+    for (unsigned off = 1; off < 32; off <<= 1) {
+      const unsigned o = __shfl_up_sync(0xffffffffu, v, off);
+      if (lane >= off) v += o;
+    }
+    if (lane == 31) warp_sum[warp] = v;
+    __syncwarp();
+    digit_base[d] = v - total;  // exclusive inside the warp; warp bases added below
+  }
+  __syncthreads();
+  unsigned base = digit_base[d];
+  for (unsigned w = 0; w < (d >> 5); ++w) base += warp_sum[w];
+  unsigned run = base + before;
+  for (unsigned b = b0; b < b1; b += 8) {
+    unsigned c[8];
+#pragma unroll
+    for (unsigned k = 0; k < 8; ++k) c[k] = b + k < b1 ? counts[(b + k) * kW + d] : 0u;
+#pragma unroll
+    for (unsigned k = 0; k < 8; ++k)
+      if (b + k < b1) {
+        counts[(b + k) * kW + d] = run;
+        run += c[k];
+      }
+  }
 }
 
-__global__ void scatter_kernel(const uint2* in, uint2* out, unsigned n, unsigned shift, const unsigned* offsets) {
+__global__ void scatter_kernel(const uint2* in, uint2* out, unsigned n, unsigned shift, const unsigned* offsets,
+                               size_t stride) {
   __shared__ unsigned bins[kWarps][kW];
+  in = at_row(in, stride);
+  out = at_row(out, stride);
+  offsets = at_row(offsets, stride);
   const unsigned i = blockIdx.x * kW + threadIdx.x;
   const bool live = i < n;
   const uint2 k = live ? in[i] : make_uint2(0, 0);
@@ -251,8 +303,13 @@ __global__ void scatter_kernel(const uint2* in, uint2* out, unsigned n, unsigned
 }
 
 __global__ void weights_kernel(const void* row, bool bf16_in, const uint2* sorted, unsigned keep,
-                               double temperature, double* prefix, double* tile_totals) {
+                               double temperature, double* prefix, double* tile_totals, size_t stride,
+                               size_t row_bytes) {
   __shared__ double tile[kW];
+  row = static_cast<const unsigned char*>(row) + blockIdx.y * row_bytes;
+  sorted = at_row(sorted, stride);
+  prefix = at_row(prefix, stride);
+  tile_totals = at_row(tile_totals, stride);
   const unsigned i = blockIdx.x * kW + threadIdx.x;
   double w = 0.0;
   if (i < keep) {
@@ -274,18 +331,31 @@ __global__ void weights_kernel(const void* row, bool bf16_in, const uint2* sorte
   if (i < keep) prefix[i] = tile[threadIdx.x];
 }
 
-__global__ void scan_tiles_kernel(double* tile_totals, unsigned keep, ScanState* scan, unsigned* result) {
+// Serial exclusive scan of the tile totals (the law's FP64 order), on a
+// shared-memory copy so the serial loop does not wait on global loads.
+__global__ void scan_tiles_kernel(double* tile_totals, unsigned keep, ScanState* scan, unsigned* result,
+                                  size_t stride) {
+  extern __shared__ double tiles_s[];
+  tile_totals = at_row(tile_totals, stride);
+  scan = at_row(scan, stride);
+  result = at_row(result, stride);
   const unsigned tiles = (keep + kW - 1) / kW;
-  double total = 0.0;
-  for (unsigned b = 0; b < tiles; ++b) {
-    const double v = tile_totals[b];
-    tile_totals[b] = total;
-    total += v;
+  for (unsigned b = threadIdx.x; b < tiles; b += blockDim.x) tiles_s[b] = tile_totals[b];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double total = 0.0;
+    for (unsigned b = 0; b < tiles; ++b) {
+      const double v = tiles_s[b];
+      tiles_s[b] = total;
+      total += v;
+    }
+    scan->total = total;
+    scan->cutoff = keep - 1;
+    scan->selected = keep - 1;
+    if (!(total > 0.0)) result[1] = 2;
   }
-  scan->total = total;
-  scan->cutoff = keep - 1;
-  scan->selected = keep - 1;
-  if (!(total > 0.0)) result[1] = 2;
+  __syncthreads();
+  for (unsigned b = threadIdx.x; b < tiles; b += blockDim.x) tile_totals[b] = tiles_s[b];
 }
 
 __device__ unsigned block_min(unsigned v) {
@@ -299,7 +369,10 @@ __device__ unsigned block_min(unsigned v) {
 }
 
 __global__ void cutoff_kernel(const double* prefix, const double* offsets, unsigned keep, double top_p,
-                              ScanState* scan) {
+                              ScanState* scan, size_t stride) {
+  prefix = at_row(prefix, stride);
+  offsets = at_row(offsets, stride);
+  scan = at_row(scan, stride);
   const unsigned i = blockIdx.x * kW + threadIdx.x;
   unsigned c = 0xffffffffu;
   if (i < keep && (offsets[blockIdx.x] + prefix[i]) / scan->total >= top_p) c = i;
@@ -308,7 +381,11 @@ __global__ void cutoff_kernel(const double* prefix, const double* offsets, unsig
 }
 
 __global__ void select_kernel(const double* prefix, const double* offsets, unsigned keep, double draw,
-                              const SamplerState* state, ScanState* scan) {
+                              const SamplerState* state, ScanState* scan, size_t stride) {
+  prefix = at_row(prefix, stride);
+  offsets = at_row(offsets, stride);
+  state = at_row(state, stride);
+  scan = at_row(scan, stride);
   const unsigned i = blockIdx.x * kW + threadIdx.x;
   const unsigned last = scan->cutoff;
   const double retained = offsets[last / kW] + prefix[last];
@@ -319,12 +396,23 @@ __global__ void select_kernel(const double* prefix, const double* offsets, unsig
   if (threadIdx.x == 0 && first != 0xffffffffu) atomicMin(&scan->selected, first);
 }
 
-__global__ void finish_kernel(const uint2* sorted, const ScanState* scan, unsigned* result) {
+__global__ void finish_kernel(const uint2* sorted, const ScanState* scan, unsigned* result, size_t stride) {
+  sorted = at_row(sorted, stride);
+  scan = at_row(scan, stride);
+  result = at_row(result, stride);
   if (!result[1]) result[0] = sorted[min(scan->selected, scan->cutoff)].y;
 }
 
+// Row r: history row r (history_stride elements apart), step[r], residual
+// row r; the shared position advances once (row 0).
 __global__ void feed_kernel(const unsigned* result, unsigned* history, int* step, const bf16* embed,
-                            bf16* residual, int width, long long* position) {
+                            bf16* residual, int width, long long* position, size_t stride, size_t history_stride) {
+  const unsigned r = blockIdx.y;
+  result = at_row(result, stride);
+  if (history) history += r * history_stride;
+  if (step) step += r;
+  if (residual) residual += size_t(r) * width;
+  if (r) position = nullptr;
   const unsigned token = result[0];
   if (threadIdx.x == 0) {
     if (history) history[step ? *step : 0] = token;
@@ -366,12 +454,14 @@ size_t sampler_required_bytes(size_t n) {
   return o + n;
 }
 
-cudaError_t sampler_init(Sampler& s, size_t vocabulary, bool bf16_input) {
+cudaError_t sampler_init(Sampler& s, size_t vocabulary, bool bf16_input, unsigned rows) {
   s.vocabulary = vocabulary;
   s.bf16_input = bf16_input;
-  cudaError_t e = cudaMalloc(&s.arena, sampler_required_bytes(vocabulary));
+  s.rows = rows ? rows : 1;
+  s.stride = align_up(sampler_required_bytes(vocabulary), 256);
+  cudaError_t e = cudaMalloc(&s.arena, s.stride * s.rows);
   if (e != cudaSuccess) return e;
-  e = cudaMemset(s.arena, 0, sampler_required_bytes(vocabulary));
+  e = cudaMemset(s.arena, 0, s.stride * s.rows);
   const Layout L = layout(s.arena, vocabulary);
   s.state = L.state;
   s.result = L.result;
@@ -388,50 +478,55 @@ cudaError_t sampler_start(Sampler& s, const dl_sampling& settings, uint64_t seed
                           size_t n_stop, cudaStream_t stream) {
   std::vector<unsigned char> mask(s.vocabulary, 0);
   for (size_t i = 0; i < n_stop; ++i) mask[stop_ids[i]] = 1;
-  cudaError_t e = cudaMemcpyAsync(s.stop_mask, mask.data(), mask.size(), cudaMemcpyHostToDevice, stream);
+  cudaError_t e = cudaSuccess;
+  for (unsigned r = 0; r < s.rows && e == cudaSuccess; ++r)
+    e = cudaMemcpyAsync(s.stop_mask + r * s.stride, mask.data(), mask.size(), cudaMemcpyHostToDevice, stream);
   if (e != cudaSuccess) return e;
   e = cudaStreamSynchronize(stream);
   if (e != cudaSuccess) return e;
-  seed_kernel<<<1, 1, 0, stream>>>(s.state, seed);
+  seed_kernel<<<dim3(1, s.rows), 1, 0, stream>>>(s.state, seed, s.stride);
   s.settings = settings;
   s.started = true;
   return cudaGetLastError();
 }
 
 cudaError_t sampler_submit(Sampler& s, const void* row, const dl_sampling& st, uint64_t bits, bool owned,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, size_t row_stride) {
   const Layout L = layout(s.arena, s.vocabulary);
-  const unsigned n = unsigned(s.vocabulary), blocks = (n + kW - 1) / kW;
-  cudaError_t e = cudaMemsetAsync(L.result, 0, 8, stream);
+  const unsigned n = unsigned(s.vocabulary), blocks = (n + kW - 1) / kW, R = s.rows;
+  const size_t S = s.stride, row_bytes = row_stride * (s.bf16_input ? 2 : 4);
+  cudaError_t e = cudaSuccess;
+  for (unsigned r = 0; r < R && e == cudaSuccess; ++r) e = cudaMemsetAsync(L.result + r * S / 4, 0, 8, stream);
   if (e != cudaSuccess) return e;
   const bool greedy = st.mode == 0;
-  if (owned) next_random_kernel<<<1, 1, 0, stream>>>(L.state, greedy);
+  if (owned) next_random_kernel<<<dim3(1, R), 1, 0, stream>>>(L.state, greedy, S);
   if (greedy) {
-    greedy_kernel<<<blocks, kW, 0, stream>>>(row, s.bf16_input, n, L.best, L.scan, L.result);
+    greedy_kernel<<<dim3(blocks, R), kW, 0, stream>>>(row, s.bf16_input, n, L.best, L.scan, L.result, S, row_bytes);
   } else {
-    keys_kernel<<<blocks, kW, 0, stream>>>(row, s.bf16_input, n, L.keys_a, L.result);
+    keys_kernel<<<dim3(blocks, R), kW, 0, stream>>>(row, s.bf16_input, n, L.keys_a, L.result, S, row_bytes);
     uint2* in = L.keys_a;
     uint2* out = L.keys_b;
     for (unsigned shift = s.bf16_input ? 16 : 0; shift < 32; shift += 8) {
-      histogram_kernel<<<blocks, kW, 0, stream>>>(in, n, shift, L.counts);
-      digit_offsets_kernel<<<1, kW, 0, stream>>>(L.counts, blocks);
-      scatter_kernel<<<blocks, kW, 0, stream>>>(in, out, n, shift, L.counts);
+      histogram_kernel<<<dim3(blocks, R), kW, 0, stream>>>(in, n, shift, L.counts, S);
+      digit_offsets_kernel<<<dim3(1, R), kW * kSeg, 0, stream>>>(L.counts, blocks, S);
+      scatter_kernel<<<dim3(blocks, R), kW, 0, stream>>>(in, out, n, shift, L.counts, S);
       uint2* t = in;
       in = out;
       out = t;
     }
     const unsigned keep = st.top_k ? unsigned(st.top_k) : n;
     const unsigned kept_blocks = (keep + kW - 1) / kW;
-    weights_kernel<<<kept_blocks, kW, 0, stream>>>(row, s.bf16_input, in, keep, st.temperature, L.prefix,
-                                                   L.tile_totals);
-    scan_tiles_kernel<<<1, 1, 0, stream>>>(L.tile_totals, keep, L.scan, L.result);
-    cutoff_kernel<<<kept_blocks, kW, 0, stream>>>(L.prefix, L.tile_totals, keep, st.top_p, L.scan);
+    weights_kernel<<<dim3(kept_blocks, R), kW, 0, stream>>>(row, s.bf16_input, in, keep, st.temperature, L.prefix,
+                                                            L.tile_totals, S, row_bytes);
+    scan_tiles_kernel<<<dim3(1, R), kW, kept_blocks * sizeof(double), stream>>>(L.tile_totals, keep, L.scan, L.result,
+                                                                                 S);
+    cutoff_kernel<<<dim3(kept_blocks, R), kW, 0, stream>>>(L.prefix, L.tile_totals, keep, st.top_p, L.scan, S);
     const double draw = static_cast<double>(bits >> 11) * 0x1.0p-53;
-    select_kernel<<<kept_blocks, kW, 0, stream>>>(L.prefix, L.tile_totals, keep, draw, owned ? L.state : nullptr,
-                                                  L.scan);
-    finish_kernel<<<1, 1, 0, stream>>>(in, L.scan, L.result);
+    select_kernel<<<dim3(kept_blocks, R), kW, 0, stream>>>(L.prefix, L.tile_totals, keep, draw,
+                                                           owned ? L.state : nullptr, L.scan, S);
+    finish_kernel<<<dim3(1, R), 1, 0, stream>>>(in, L.scan, L.result, S);
   }
-  if (owned) commit_kernel<<<1, 1, 0, stream>>>(L.state, L.result, L.stop_mask);
+  if (owned) commit_kernel<<<dim3(1, R), 1, 0, stream>>>(L.state, L.result, L.stop_mask, S);
   return cudaGetLastError();
 }
 
@@ -441,9 +536,14 @@ int sampler_launch_count(const Sampler& s, const dl_sampling& st, bool owned) {
   return body + (owned ? 2 : 0);
 }
 
+unsigned* sampler_result(const Sampler& s, unsigned row) {
+  return reinterpret_cast<unsigned*>(reinterpret_cast<unsigned char*>(s.result) + row * s.stride);
+}
+
 cudaError_t sampler_feed(Sampler& s, unsigned* history, int* step, const bf16* embed, bf16* residual, int width,
-                         long long* position, cudaStream_t stream) {
-  feed_kernel<<<1, 256, 0, stream>>>(s.result, history, step, embed, residual, width, position);
+                         long long* position, cudaStream_t stream, size_t history_stride) {
+  feed_kernel<<<dim3(1, s.rows), 256, 0, stream>>>(s.result, history, step, embed, residual, width, position,
+                                                   s.stride, history_stride);
   return cudaGetLastError();
 }
 

@@ -14,12 +14,17 @@ namespace dl {
 
 struct SamplerState;  // device-resident MT19937-64 words + latches
 
+// One sampler serves `rows` logits rows at once (every kernel launches with
+// gridDim.y = rows); row r owns the arena slice at r * stride bytes and draws
+// from the MT19937-64 stream seeded with seed + r.
 struct Sampler {
   size_t vocabulary = 0;
   bool bf16_input = true;
-  void* arena = nullptr;       // device scratch (sampler_required_bytes)
+  unsigned rows = 1;
+  size_t stride = 0;           // bytes per row's arena slice
+  void* arena = nullptr;       // device scratch (rows * stride)
   SamplerState* state = nullptr;
-  unsigned* result = nullptr;  // {token, status}
+  unsigned* result = nullptr;  // {token, status} of row 0 (sampler_result for row r)
   unsigned char* stop_mask = nullptr;
   dl_sampling settings = {0, 1.0, 0, 1.0};
   bool started = false;
@@ -30,18 +35,21 @@ struct Sampler {
 void validate_sampling(const dl_sampling& s, size_t vocabulary);
 
 size_t sampler_required_bytes(size_t vocabulary);
-cudaError_t sampler_init(Sampler& s, size_t vocabulary, bool bf16_input);
+cudaError_t sampler_init(Sampler& s, size_t vocabulary, bool bf16_input, unsigned rows = 1);
 void sampler_free(Sampler& s);
 cudaError_t sampler_start(Sampler& s, const dl_sampling& settings, uint64_t seed, const uint32_t* stop_ids,
                           size_t n_stop, cudaStream_t stream);
 // owned = device-owned MT stream (submit_next); otherwise `bits` is the draw.
+// Row r's logits are at row + r * row_stride elements.
 cudaError_t sampler_submit(Sampler& s, const void* row, const dl_sampling& settings, uint64_t bits, bool owned,
-                           cudaStream_t stream);
+                           cudaStream_t stream, size_t row_stride = 0);
 // Kernels one sampler_submit enqueues (for launch accounting).
 int sampler_launch_count(const Sampler& s, const dl_sampling& settings, bool owned);
-// After a selection: history[*step] = token, ++*step, residual = embed[token],
-// ++*position (each optional).
+// After a selection, per row r: history[r * history_stride + step[r]] =
+// token, ++step[r], residual row r = embed[token]; ++*position once (each
+// optional).
 cudaError_t sampler_feed(Sampler& s, unsigned* history, int* step, const bf16* embed, bf16* residual,
-                         int width, long long* position, cudaStream_t stream);
+                         int width, long long* position, cudaStream_t stream, size_t history_stride = 0);
+unsigned* sampler_result(const Sampler& s, unsigned row);
 
 }  // namespace dl

@@ -143,8 +143,7 @@ Server::Server(const dl_model_config& cfg, int device, size_t batch, size_t capa
     if (!m) throw std::runtime_error("prompt attention tensor maps");
     attn_maps_.push_back(m);
   }
-  samplers_.resize(B);
-  for (auto& s : samplers_) check(sampler_init(s, V_, true), "sampler init");
+  check(sampler_init(sampler_, V_, true, unsigned(B)), "sampler init");
   check(launch_inv_freq(inv_freq_, int(d_), cfg.theta, stream_), "inv_freq");
   check(cudaStreamSynchronize(stream_), "init sync");
 }
@@ -155,7 +154,7 @@ Server::~Server() {
   if (step_exec_) cudaGraphExecDestroy(step_exec_);
   if (comm_) ncclCommDestroy(comm_);
   for (auto* m : attn_maps_) attention_prefill_tc_free(m);
-  for (auto& s : samplers_) sampler_free(s);
+  sampler_free(sampler_);
   for (auto& ev : ev_)
     if (ev) cudaEventDestroy(ev);
   cudaFree(scratch_);
@@ -397,6 +396,7 @@ void Server::prefill(const uint32_t* tokens, size_t prompt_len, const dl_samplin
   if (tp_ > 1 && !comm_) throw std::logic_error("tensor-parallel server is not connected");
   validate_sampling(s, V_);
   settings_ = s;
+  check(cudaEventRecord(ev_[0], stream_), "event");
   for (size_t b = 0; b < batch_; ++b) prefill_sequence(b, tokens + b * prompt_len, prompt_len);
   // Vocabulary head on the B last rows, then each row's first selection
   // (the sampler feeds the token's embedding row in as the next input).
@@ -409,20 +409,22 @@ void Server::prefill(const uint32_t* tokens, size_t prompt_len, const dl_samplin
     gemm(xn_, int(D_), lm_head_, B, int(V_), int(D_), kGemmStore, 1, n0s, outs, lds);
   }
   check(cudaMemsetAsync(steps_, 0, batch_ * 4, stream_), "steps");
-  for (size_t b = 0; b < batch_; ++b) {
-    check(sampler_start(samplers_[b], s, seed + b, nullptr, 0, stream_), "sampler start");
-    check(sampler_submit(samplers_[b], logits_ + b * V_, s, 0, true, stream_), "sampler");
-    check(sampler_feed(samplers_[b], history_ + b * history_cap_, steps_ + b, embed_, residual_ + b * D_, int(D_),
-                       nullptr, stream_),
-          "sampler feed");
-  }
+  // Row b draws from the stream seeded with seed + b.
+  check(sampler_start(sampler_, s, seed, nullptr, 0, stream_), "sampler start");
+  check(sampler_submit(sampler_, logits_, s, 0, true, stream_, V_), "sampler");
+  check(sampler_feed(sampler_, history_, steps_, embed_, residual_, int(D_), nullptr, stream_, history_cap_),
+        "sampler feed");
   const long long pos = (long long)prompt_len;
   check(cudaMemcpyAsync(position_, &pos, 8, cudaMemcpyHostToDevice, stream_), "position");
   std::vector<uint32_t> first(batch_);
   for (size_t b = 0; b < batch_; ++b)
     check(cudaMemcpyAsync(&first[b], history_ + b * history_cap_, 4, cudaMemcpyDeviceToHost, stream_), "first");
+  check(cudaEventRecord(ev_[1], stream_), "event");
   check(cudaStreamSynchronize(stream_), "prefill sync");
   check_fault();
+  float ms = 0.f;
+  check(cudaEventElapsedTime(&ms, ev_[0], ev_[1]), "elapsed");
+  prefill_ms_ = ms;
   if (first_out) std::memcpy(first_out, first.data(), batch_ * 4);
   started_ = true;
   if (step_exec_) {
@@ -473,13 +475,9 @@ void Server::decode_body() {
     const int lds[1] = {int(V_)};
     gemm(xn_, D, lm_head_, B, int(V_), D, kGemmStore, 1, n0s, outs, lds);
   }
-  for (size_t b = 0; b < batch_; ++b) {
-    check(sampler_submit(samplers_[b], logits_ + b * V_, settings_, 0, true, stream_), "sampler");
-    check(sampler_feed(samplers_[b], history_ + b * history_cap_, steps_ + b, embed_, residual_ + b * D_, D, nullptr,
-                       stream_),
-          "sampler feed");
-    launches_ += sampler_launch_count(samplers_[b], settings_, true) + 1;
-  }
+  check(sampler_submit(sampler_, logits_, settings_, 0, true, stream_, V_), "sampler");
+  check(sampler_feed(sampler_, history_, steps_, embed_, residual_, D, nullptr, stream_, history_cap_), "sampler feed");
+  launches_ += sampler_launch_count(sampler_, settings_, true) + 1;
   check(launch_add_position(position_, 1, stream_), "advance");
   launches_ += 2;
 }
@@ -528,6 +526,7 @@ void Server::decode(size_t steps, uint32_t* tokens_out, uint16_t* logits_out, dl
         tokens_out[i * batch_ + b] = h[b * history_cap_ + size_t(step_count) - steps + i];
   }
   if (stats) {
+    stats->prefill_ms = prefill_ms_;
     stats->decode_ms = ms;
     stats->decode_steps = steps;
     stats->kernels_per_decode_step = kernels_per_step_;

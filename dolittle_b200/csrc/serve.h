@@ -96,12 +96,13 @@ class Server {
   int vt_stride_ = 0;
   int attn_splits_ = 1;
   std::vector<AttnTcMaps*> attn_maps_;
-  std::vector<Sampler> samplers_;
+  Sampler sampler_;  // one row per sequence
   dl_sampling settings_ = {0, 1.0, 0, 1.0};
   bool started_ = false;
   cudaGraphExec_t step_exec_ = nullptr;
   size_t kernels_per_step_ = 0;
   size_t launches_ = 0;
+  double prefill_ms_ = 0.0;
   cudaEvent_t ev_[2] = {};
 };
 

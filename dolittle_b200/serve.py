@@ -25,6 +25,7 @@ class ServeResult:
     tokens: np.ndarray            # [steps][batch]
     logits: np.ndarray | None     # [steps][batch][V] BF16 bits
     decode_ms: float
+    prefill_ms: float             # device time of the last prefill (prompt passes + first selections)
     kernels_per_decode_step: int
 
 
@@ -101,7 +102,7 @@ class Server:
         check(lib().dl_serve_decode(self._h, steps, tokens.ctypes.data_as(_lib.u32p),
                                     logits.ctypes.data_as(_lib.u16p) if logits is not None else None,
                                     C.byref(stats)))
-        return ServeResult(tokens, logits, stats.decode_ms, int(stats.kernels_per_decode_step))
+        return ServeResult(tokens, logits, stats.decode_ms, stats.prefill_ms, int(stats.kernels_per_decode_step))
 
 
 # Per-block tensor roles (engine order) and how tensor parallelism cuts them:

@@ -307,7 +307,7 @@ DL_API dl_status dl_engine_generate(dl_engine* e, const uint32_t* prompt, size_t
 typedef struct dl_serve dl_serve;
 
 typedef struct {
-  double prefill_ms;
+  double prefill_ms;      /* device time of the last dl_serve_prefill */
   double decode_ms;       /* device time of the decode steps */
   uint64_t decode_steps;
   uint64_t kernels_per_decode_step;

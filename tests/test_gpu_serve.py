@@ -184,3 +184,24 @@ def test_server_rejects_bad_shapes():
         srv.decode(1)   # decode before prefill
     with pytest.raises(dl.DolittleError):
         srv.prefill(np.zeros((2, 16), np.uint32))  # prompt fills the capacity
+
+
+def test_batched_categorical_selection_follows_the_device_law():
+    """One sampler launch per kernel serves every row: row b's selections
+    equal the device law on its own logits with the words of the MT19937-64
+    stream seeded with seed + b (the prompt pass's selection used word 0)."""
+    cfg = _small_cfg(1)
+    B, seed = 3, 7
+    srv = Server(cfg, batch=B, capacity=48, chunk_rows=32)
+    srv.init_random(6, 0.02)
+    prompts = np.stack([oracle.uniform_ids(16, 90 + b, 0, cfg.vocabulary) for b in range(B)])
+    st = dl.Settings(dl.SelectionMode.categorical, 0.8, 0, 0.95)
+    srv.prefill(prompts, st, seed=seed)
+    res = srv.decode(5, want_logits=True)
+    for b in range(B):
+        mt = oracle.MT64(seed + b)
+        mt()
+        for i in range(5):
+            logits = nm.bf16_bits_to_f32(res.logits[i, b])
+            token, status = oracle.select_device(logits, True, 0.8, 0, 0.95, mt())
+            assert status == 0 and token == int(res.tokens[i, b]), (b, i)
