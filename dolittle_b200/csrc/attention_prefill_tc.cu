@@ -1,19 +1,23 @@
 // Causal GQA prompt attention on the 5th-generation tensor cores, for the
-// fast prompt pass (tensor-core accumulation order, checked against the
-// reference-order path within tolerance like the tcgen05 GEMMs).
+// fast prompt pass (tensor-core accumulation order, online softmax; checked
+// against the reference-order path within tolerance like the tcgen05 GEMMs).
 //
-// One CTA (4 warps) owns 128 query rows of one query head.  Key blocks of 128
-// are visited twice:
-//   pass 1: S = Q K^T (tcgen05.mma, M = N = 128, K = 128 over the head width)
-//           into TMEM; each thread (one query row = one TMEM lane) reads its
-//           row and keeps the running maximum m and sum l of exp2(s - m);
-//   pass 2: S again; p = exp2(s - m) / l, rounded to BF16 and written to
-//           shared memory as a 128-byte-swizzled K-major tile, then
-//           O += P V^T^T (tcgen05.mma with A = P, B = V^T) in TMEM.
-// Scores carry the softmax scale times log2(e); keys beyond the row's
-// position are masked.  Q and K come in by TMA straight from the rotated
-// queries and the K cache; V is read as V^T from a per-block transposed copy
-// (launch_vt_transpose) so both operands of both products are K-major.
+// One CTA (4 warps) owns 128 query rows of one query head; thread r owns
+// query row r = TMEM lane r.  Key blocks of 128, one pass:
+//   S[kb] = Q K[kb]^T (tcgen05.mma, M = N = 128, K = 128 over the head width)
+//           into one of two TMEM score buffers;
+//   each thread reads its row of S, updates its running max m and sum l of
+//   exp2(s - m) (masked beyond the row's position), writes p = exp2(s - m)
+//   as BF16 into a 128-byte-swizzled K-major tile;
+//   O[kb] = P V[kb] (A = P, B = V^T) into TMEM; each thread rescales its
+//   register copy of the output row by exp2(m_old - m_new) and adds its row
+//   of O[kb]; the output is O / l at the end.
+// K and V^T blocks stream through two TMA stages, and the next block's score
+// MMA is issued as soon as this block's P is written, so it overlaps the
+// output update.  Scores carry the softmax scale times log2(e).  Q and K come
+// in by TMA from the rotated queries and the K cache; V is read as V^T from a
+// transposed copy (launch_vt_transpose) so both operands of both products are
+// K-major.
 #include <cudaTypedefs.h>
 
 #include <cmath>
@@ -31,8 +35,8 @@ constexpr int kTile = 128;                    // query rows per CTA, keys per bl
 constexpr int kThreads = 128;
 constexpr int kAtomBytes = kTile * 64 * 2;    // [128 rows][64 BF16], one swizzle atom column
 constexpr int kTileBytes = 2 * kAtomBytes;    // [128 rows][128 BF16]
-constexpr int kSmem = 4 * kTileBytes + 1024;  // Q, K, V^T, P + alignment
-constexpr uint32_t kTmemCols = 256;           // S (128 columns) + O (128 columns)
+constexpr int kSmem = 6 * kTileBytes + 1024;  // Q, 2 x K, 2 x V^T, P + alignment
+constexpr uint32_t kTmemCols = 512;           // S0, S1, O (128 columns each)
 
 struct alignas(64) AttnArgs {
   CUtensorMap map_q;   // {d, Hq, rows}: box {64, 1, 128}
@@ -78,14 +82,15 @@ __device__ __forceinline__ void mma_tile(uint32_t tmem_d, const unsigned char* a
 
 __global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const __grid_constant__ AttnArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  __shared__ uint64_t tma_bar, mma_bar;
+  __shared__ uint64_t q_bar, kv_bar[2], s_bar[2], o_bar;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   const uint32_t base_s = (smem_addr(smem_raw) + 1023u) & ~1023u;
   unsigned char* sq = smem_raw + (base_s - smem_addr(smem_raw));
-  unsigned char* sk = sq + kTileBytes;
-  unsigned char* svt = sk + kTileBytes;
-  unsigned char* sp = svt + kTileBytes;
+  // Stage st: K at sq + (1 + st) tiles, V^T at sq + (3 + st) tiles.
+  auto sk = [&](int st) { return sq + (1 + st) * kTileBytes; };
+  auto svt = [&](int st) { return sq + (3 + st) * kTileBytes; };
+  unsigned char* sp = sq + 5 * kTileBytes;
   const int warp = threadIdx.x >> 5;
   const int hq = blockIdx.y;
   const int g = hq / (a.query_heads / a.kv_heads);
@@ -98,8 +103,12 @@ __global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const
   const int nkb = int(last_pos / kTile) + 1;
 
   if (threadIdx.x == 0) {
-    mbar_init(&tma_bar, 1);
-    mbar_init(&mma_bar, 1);
+    mbar_init(&q_bar, 1);
+    mbar_init(&kv_bar[0], 1);
+    mbar_init(&kv_bar[1], 1);
+    mbar_init(&s_bar[0], 1);
+    mbar_init(&s_bar[1], 1);
+    mbar_init(&o_bar, 1);
     abort_flag = 0;
     fence_barrier_init();
   }
@@ -108,137 +117,135 @@ __global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const
   __syncthreads();
   fence_after_sync();
   const uint32_t tmem = tmem_base;
-  const uint32_t t_s = tmem, t_o = tmem + 128;
+  auto t_s = [&](int st) { return tmem + uint32_t(st * 128); };
+  const uint32_t t_o = tmem + 256;
   const uint32_t lane_base = uint32_t(warp * 32) << 16;
 
-  float m = -INFINITY, l = 0.f;
-  unsigned tma_phase = 0, mma_phase = 0;
-  for (int pass = 0; pass < 2; ++pass) {
-    for (int kb = 0; kb < nkb; ++kb) {
-      // Operands of this block, then S = Q K^T.
-      if (threadIdx.x == 0 && !abort_flag) {
-        const bool with_q = pass == 0 && kb == 0;
-        mbar_arrive_expect_tx(&tma_bar, unsigned(kTileBytes) * (1 + (with_q ? 1 : 0) + (pass ? 1 : 0)));
-        if (with_q) {
-          tma_load(sq, &a.map_q, 0, hq, q0, &tma_bar);
-          tma_load(sq + kAtomBytes, &a.map_q, 64, hq, q0, &tma_bar);
-        }
-        tma_load4(sk, &a.map_k, 0, g, kb * kTile, 2 * a.layer, &tma_bar);
-        tma_load4(sk + kAtomBytes, &a.map_k, 64, g, kb * kTile, 2 * a.layer, &tma_bar);
-        if (pass) {
-          tma_load(svt, &a.map_vt, kb * kTile, 0, g, &tma_bar);
-          tma_load(svt + kAtomBytes, &a.map_vt, kb * kTile + 64, 0, g, &tma_bar);
-        }
-        if (!mbar_wait(&tma_bar, tma_phase)) {
-          record_error(a.err, kErrWaitFull);
-          abort_flag = 1;
-        } else {
-          fence_after_sync();
-          mma_tile(t_s, sq, sk, false);
-          mma_commit(&mma_bar);
-        }
-      }
-      tma_phase ^= 1;
-      __syncthreads();  // abort decision is uniform
-      if (abort_flag) break;
-      if (!mbar_wait(&mma_bar, mma_phase)) {
-        record_error(a.err, kErrWaitFull);
-        abort_flag = 1;
-      }
-      mma_phase ^= 1;
+  // Thread 0 issues every TMA load and MMA.
+  auto load_kv = [&](int kb) {
+    const int st = kb & 1;
+    mbar_arrive_expect_tx(&kv_bar[st], unsigned(2 * kTileBytes));
+    tma_load4(sk(st), &a.map_k, 0, g, kb * kTile, 2 * a.layer, &kv_bar[st]);
+    tma_load4(sk(st) + kAtomBytes, &a.map_k, 64, g, kb * kTile, 2 * a.layer, &kv_bar[st]);
+    tma_load(svt(st), &a.map_vt, kb * kTile, 0, g, &kv_bar[st]);
+    tma_load(svt(st) + kAtomBytes, &a.map_vt, kb * kTile + 64, 0, g, &kv_bar[st]);
+  };
+  auto fail = [&] {
+    record_error(a.err, kErrWaitFull);
+    abort_flag = 1;
+  };
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&q_bar, unsigned(kTileBytes));
+    tma_load(sq, &a.map_q, 0, hq, q0, &q_bar);
+    tma_load(sq + kAtomBytes, &a.map_q, 64, hq, q0, &q_bar);
+    load_kv(0);
+    if (nkb > 1) load_kv(1);
+    if (!mbar_wait(&q_bar, 0) || !mbar_wait(&kv_bar[0], 0)) {
+      fail();
+    } else {
       fence_after_sync();
-      const int key0 = kb * kTile;
-      if (pass == 0) {
-        // Running max and sum of exp2 over this block's keys.
-        float bm = -INFINITY;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t s[32];
-          tmem_ld32(t_s + lane_base + uint32_t(c * 32), s);
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (key0 + c * 32 + i <= pos) bm = fmaxf(bm, __uint_as_float(s[i]) * a.scale_log2);
-        }
-        // TMEM loads are warp-collective: every lane loads, only the
-        // arithmetic is guarded.
-        const float mn = fmaxf(m, bm);
-        const bool use = live && mn != -INFINITY;
-        float sum = 0.f;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t s[32];
-          tmem_ld32(t_s + lane_base + uint32_t(c * 32), s);
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (use && key0 + c * 32 + i <= pos) sum += exp2f(__uint_as_float(s[i]) * a.scale_log2 - mn);
-        }
-        if (use) {
-          l = (m == -INFINITY ? 0.f : l * exp2f(m - mn)) + sum;
-          m = mn;
-        }
-        fence_before_sync();
-        __syncthreads();  // S is rewritten by the next block's MMA
-      } else {
-        // P = exp2(s - m) / l as BF16 into the swizzled K-major tile.
-        const float inv_l = (live && l > 0.f) ? 1.0f / l : 0.f;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t s[32];
-          tmem_ld32(t_s + lane_base + uint32_t(c * 32), s);
-          uint32_t packed[16];
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const int k0 = key0 + c * 32 + i;
-            const float p0 = (live && k0 <= pos) ? exp2f(__uint_as_float(s[i]) * a.scale_log2 - m) * inv_l : 0.f;
-            const float p1 =
-                (live && k0 + 1 <= pos) ? exp2f(__uint_as_float(s[i + 1]) * a.scale_log2 - m) * inv_l : 0.f;
-            const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
-            packed[i / 2] = *reinterpret_cast<const uint32_t*>(&h2);
-          }
-          // Keys c*32 .. c*32+31 of the block: atom c / 2, chunks (c % 2) * 4 .. + 3.
-          unsigned char* rowp = sp + (c >> 1) * kAtomBytes + r * 128;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int chunk = (c & 1) * 4 + q;
-            *reinterpret_cast<uint4*>(rowp + ((chunk ^ (r & 7)) << 4)) =
-                make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-          }
-        }
-        fence_proxy_async_smem();
-        fence_before_sync();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-          fence_after_sync();
-          mma_tile(t_o, sp, svt, kb > 0);
-          mma_commit(&mma_bar);
-        }
-        if (!mbar_wait(&mma_bar, mma_phase)) {
-          record_error(a.err, kErrWaitFull);
-          abort_flag = 1;
-        }
-        mma_phase ^= 1;
-        fence_after_sync();
-        __syncthreads();
-      }
+      mma_tile(t_s(0), sq, sk(0), false);
+      mma_commit(&s_bar[0]);
     }
-    if (abort_flag) break;
   }
-  if (!abort_flag) {  // uniform: every lane takes part in the TMEM loads
-    bf16* out = a.out + size_t(live ? row : 0) * (size_t(a.query_heads) * 128) + size_t(hq) * 128;
+  __syncthreads();
+
+  float o[128];
+#pragma unroll
+  for (int i = 0; i < 128; ++i) o[i] = 0.f;
+  float m = -INFINITY, l = 0.f;
+  unsigned o_phase = 0;
+  for (int kb = 0; kb < nkb && !abort_flag; ++kb) {
+    const int st = kb & 1;
+    if (!mbar_wait(&s_bar[st], unsigned(kb >> 1) & 1)) fail();
+    fence_after_sync();
+    const int key0 = kb * kTile;
+    // Block max over this row's visible keys (TMEM loads are warp-collective:
+    // every lane loads, only the arithmetic is guarded).
+    float bm = -INFINITY;
 #pragma unroll 1
     for (int c = 0; c < 4; ++c) {
-      uint32_t o[32];
-      tmem_ld32(t_o + lane_base + uint32_t(c * 32), o);
-      if (!live) continue;
+      uint32_t sv[32];
+      tmem_ld32(t_s(st) + lane_base + uint32_t(c * 32), sv);
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (key0 + c * 32 + i <= pos) bm = fmaxf(bm, __uint_as_float(sv[i]) * a.scale_log2);
+    }
+    const float mn = fmaxf(m, bm);
+    const bool use = live && mn != -INFINITY;
+    const float alpha = (use && m != -INFINITY) ? exp2f(m - mn) : 0.f;
+    float sum = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t sv[32];
+      tmem_ld32(t_s(st) + lane_base + uint32_t(c * 32), sv);
       uint32_t packed[16];
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
-        const __nv_bfloat162 h2 = __floats2bfloat162_rn(__uint_as_float(o[i]), __uint_as_float(o[i + 1]));
+        const int k0 = key0 + c * 32 + i;
+        const float p0 = (use && k0 <= pos) ? exp2f(__uint_as_float(sv[i]) * a.scale_log2 - mn) : 0.f;
+        const float p1 = (use && k0 + 1 <= pos) ? exp2f(__uint_as_float(sv[i + 1]) * a.scale_log2 - mn) : 0.f;
+        const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+        sum += __low2float(h2) + __high2float(h2);  // l sums the BF16 weights the MMA sees
         packed[i / 2] = *reinterpret_cast<const uint32_t*>(&h2);
       }
-      uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
+      // Keys c*32 .. c*32+31 of the block: atom c / 2, chunks (c % 2) * 4 .. + 3.
+      unsigned char* rowp = sp + (c >> 1) * kAtomBytes + r * 128;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+      for (int q = 0; q < 4; ++q) {
+        const int chunk = (c & 1) * 4 + q;
+        *reinterpret_cast<uint4*>(rowp + ((chunk ^ (r & 7)) << 4)) =
+            make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+      }
+    }
+    if (use) {
+      l = l * alpha + sum;
+      m = mn;
+    }
+    fence_proxy_async_smem();
+    fence_before_sync();
+    __syncthreads();  // P complete; S[st] consumed
+    if (threadIdx.x == 0 && !abort_flag) {
+      fence_after_sync();
+      mma_tile(t_o, sp, svt(st), false);
+      mma_commit(&o_bar);
+      if (kb + 1 < nkb) {
+        // The next block's scores overlap this block's output update.
+        if (!mbar_wait(&kv_bar[st ^ 1], unsigned((kb + 1) >> 1) & 1)) {
+          fail();
+        } else {
+          fence_after_sync();
+          mma_tile(t_s(st ^ 1), sq, sk(st ^ 1), false);
+          mma_commit(&s_bar[st ^ 1]);
+        }
+      }
+    }
+    if (!mbar_wait(&o_bar, o_phase)) fail();
+    o_phase ^= 1;
+    fence_after_sync();
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t ov[32];
+      tmem_ld32(t_o + lane_base + uint32_t(c * 32), ov);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha, __uint_as_float(ov[i]));
+    }
+    fence_before_sync();
+    __syncthreads();  // O and P free; stage st free once both MMAs of this block completed
+    if (threadIdx.x == 0 && kb + 2 < nkb && !abort_flag) load_kv(kb + 2);
+  }
+  if (!abort_flag && live) {
+    const float inv_l = l > 0.f ? 1.0f / l : 0.f;
+    bf16* out = a.out + size_t(row) * (size_t(a.query_heads) * 128) + size_t(hq) * 128;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      uint32_t packed[4];
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        const __nv_bfloat162 h2 = __floats2bfloat162_rn(o[c * 8 + i] * inv_l, o[c * 8 + i + 1] * inv_l);
+        packed[i / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+      }
+      reinterpret_cast<uint4*>(out)[c] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
     }
   }
   fence_before_sync();

@@ -5,6 +5,8 @@
 #include <stdexcept>
 #include <string>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "attention_prefill_tc.h"
 #include "gemm_tcgen05.h"
 #include "serve.h"
@@ -503,6 +505,7 @@ void Server::decode(size_t steps, uint32_t* tokens_out, uint16_t* logits_out, dl
     cudaGraphDestroy(graph);
     kernels_per_step_ = launches_ - before;
   }
+  nvtxRangePushA("serve_decode");  // profilers can select the decode steps alone
   check(cudaEventRecord(ev_[0], stream_), "event");
   for (size_t i = 0; i < steps; ++i) {
     check(cudaGraphLaunch(step_exec_, stream_), "graph launch");
@@ -511,6 +514,7 @@ void Server::decode(size_t steps, uint32_t* tokens_out, uint16_t* logits_out, dl
             "logits");
   }
   check(cudaEventRecord(ev_[1], stream_), "event");
+  nvtxRangePop();
   check(cudaStreamSynchronize(stream_), "decode sync");
   check_fault();
   float ms = 0.f;
