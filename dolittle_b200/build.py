@@ -69,9 +69,9 @@ def build(verbose_ptxas: bool = False, force: bool = False) -> str:
             if r.returncode != 0:
                 raise RuntimeError(f"nvcc failed: {' '.join(cmd)}")
     if force or jobs or _stale(OUT, objs):
-        # NCCL: the tensor-parallel all-reduce of the batched server.
+        # NCCL (tensor-parallel all-reduce) is resolved with dlopen at run time.
         cmd = [NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", OUT, *objs,
-               "-lcudart", "-lnccl"]
+               "-lcudart", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n" + r.stdout + r.stderr)

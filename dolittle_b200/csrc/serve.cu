@@ -5,6 +5,7 @@
 #include <stdexcept>
 #include <string>
 
+#include <dlfcn.h>
 #include <nvtx3/nvToolsExt.h>
 
 #include "attention_prefill_tc.h"
@@ -15,6 +16,35 @@ namespace dl {
 
 namespace {
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// NCCL is resolved at run time, only when a tensor-parallel group connects:
+// a process that already loaded libnccl.so.2 (PyTorch's bundled copy, say)
+// keeps using that copy, and single-GPU use never loads NCCL at all.
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*);
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int);
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+  ncclResult_t (*comm_destroy)(ncclComm_t);
+  const char* (*error_string)(ncclResult_t);
+};
+
+const NcclApi& nccl() {
+  static const NcclApi api = [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) throw std::runtime_error("tensor parallelism needs libnccl.so.2");
+    NcclApi a{};
+    a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    a.comm_init_rank = reinterpret_cast<decltype(a.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
+    if (!a.get_unique_id || !a.comm_init_rank || !a.all_reduce || !a.comm_destroy || !a.error_string)
+      throw std::runtime_error("libnccl.so.2 lacks the NCCL 2 API");
+    return a;
+  }();
+  return api;
+}
 }  // namespace
 
 void Server::check(cudaError_t e, const char* what) {
@@ -22,7 +52,7 @@ void Server::check(cudaError_t e, const char* what) {
 }
 
 void Server::check_nccl(ncclResult_t r, const char* what) {
-  if (r != ncclSuccess) throw std::runtime_error(std::string(what) + ": " + ncclGetErrorString(r));
+  if (r != ncclSuccess) throw std::runtime_error(std::string(what) + ": " + nccl().error_string(r));
 }
 
 Server::Server(const dl_model_config& cfg, int device, size_t batch, size_t capacity, size_t chunk_rows, int tp_rank,
@@ -154,7 +184,7 @@ Server::~Server() {
   cudaSetDevice(device_);
   if (stream_) cudaStreamSynchronize(stream_);
   if (step_exec_) cudaGraphExecDestroy(step_exec_);
-  if (comm_) ncclCommDestroy(comm_);
+  if (comm_) nccl().comm_destroy(comm_);
   for (auto* m : attn_maps_) attention_prefill_tc_free(m);
   sampler_free(sampler_);
   for (auto& ev : ev_)
@@ -167,7 +197,7 @@ Server::~Server() {
 
 void Server::nccl_id(unsigned char* out128) {
   ncclUniqueId id;
-  if (ncclGetUniqueId(&id) != ncclSuccess) throw std::runtime_error("ncclGetUniqueId failed");
+  if (nccl().get_unique_id(&id) != ncclSuccess) throw std::runtime_error("ncclGetUniqueId failed");
   static_assert(sizeof(id) == 128, "NCCL unique id size");
   std::memcpy(out128, &id, sizeof(id));
 }
@@ -178,7 +208,7 @@ void Server::connect(const unsigned char* id128) {
   check(cudaSetDevice(device_), "cudaSetDevice");
   ncclUniqueId id;
   std::memcpy(&id, id128, sizeof(id));
-  check_nccl(ncclCommInitRank(&comm_, tp_, id, rank_), "ncclCommInitRank");
+  check_nccl(nccl().comm_init_rank(&comm_, tp_, id, rank_), "ncclCommInitRank");
 }
 
 // Slice of tensor `index` held by this rank.  q/k/v and gate/up: row ranges
@@ -308,7 +338,7 @@ void Server::gemm(const bf16* x, int ldx, const bf16* w, int M, int N, int K, in
 }
 
 void Server::all_reduce(float* buf, size_t n) {
-  check_nccl(ncclAllReduce(buf, buf, n, ncclFloat, ncclSum, comm_, stream_), "ncclAllReduce");
+  check_nccl(nccl().all_reduce(buf, buf, n, ncclFloat, ncclSum, comm_, stream_), "ncclAllReduce");
 }
 
 // o_proj / down_proj of M rows into the residual.  One rank: the GEMM adds
