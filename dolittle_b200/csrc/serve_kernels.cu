@@ -54,38 +54,66 @@ __global__ void norm_rope_append_rows_kernel(const bf16* __restrict__ qkv, int l
 }
 
 // ---------------------------------------------------------------------------
-// Split-K flash decoding.  CTA (split s, kv head g, sequence b) streams keys
-// [j0, j1) of b's cache in tiles of 64 through a two-stage cp.async ring
-// (K and V rows padded to 272 bytes: conflict-free 16-byte reads), computes
-// the group's scores (one (key, head) per thread), keeps a running max and
-// sum per head and rescales the per-thread output pairs.
+// Split-K flash decoding on the tensor cores (mma.sync m16n8k16, BF16 in,
+// FP32 accumulate).  CTA (kv head g, split s, sequence b) streams keys
+// [j0, j1) of b's cache in tiles of 64 through a three-stage cp.async ring
+// (K and V rows padded to 272 bytes so fragment reads are conflict-free; two
+// CTAs fit on an SM).  The GQA group's query heads are the rows of a 16-row
+// A operand (rows >= group are zero):
+//   S = Q K^T: warp w computes keys 8w .. 8w+7 (8 MMAs over the 128
+//   features); the running max / sum per head and p = exp(s - max) follow,
+//   p goes to shared memory as BF16;
+//   O += P V: warp w computes features 16w .. 16w+15 (2 n-tiles x 4 MMAs
+//   over the 64 keys, V fragments by ldmatrix.trans), after rescaling its
+//   accumulator rows by exp(max_old - max_new).
+// Kernel fast enough to stream the cache at the HBM rate: the CUDA-core form
+// spent ~4 FLOP per cache byte plus conversions and ran instruction-bound.
 // ---------------------------------------------------------------------------
 constexpr int kAdThreads = 256;
 constexpr int kAdKeys = 64;
-constexpr int kAdPitch = 136;   // BF16 per smem row (128 + 8)
-constexpr int kAdQPitch = 132;  // FP32 per query row
+constexpr int kAdPitch = 136;   // BF16 per K / V smem row (128 + 8)
+constexpr int kAdPPitch = 72;   // BF16 per P row (64 + 8)
 constexpr int kAdMaxGroup = 8;
 constexpr int kAdWs = 130;      // m, l, 128 outputs
+constexpr int kAdStages = 3;
 constexpr int kAdStageElems = 2 * kAdKeys * kAdPitch;  // K then V
-constexpr size_t kAdSmem =
-    size_t(2) * kAdStageElems * 2 + size_t(kAdMaxGroup) * kAdQPitch * 4 + size_t(kAdMaxGroup) * kAdKeys * 4 +
-    3 * kAdMaxGroup * 4;
+constexpr size_t kAdSmem = size_t(kAdStages) * kAdStageElems * 2 + size_t(16) * kAdPPitch * 2 + 2 * 8 * 8 * 4;
 
 __device__ __forceinline__ void cp16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
+// Zero-filled 16 bytes (no global read): rows past the last key.
+__device__ __forceinline__ void cp16_zero(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, 0;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x2_trans(uint32_t& b0, uint32_t& b1, const void* row_addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
+               : "=r"(b0), "=r"(b1)
+               : "r"(smem_addr(row_addr)));
+}
+
+__device__ __forceinline__ uint32_t lds32(const bf16* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
 __global__ void __launch_bounds__(kAdThreads) attention_decode_split_kernel(
     const bf16* __restrict__ q, KvPlanes planes, const long long* __restrict__ position, int query_heads,
     int kv_heads, int splits, float scale, float* __restrict__ ws) {
   extern __shared__ __align__(16) unsigned char smem[];
   bf16* stage = reinterpret_cast<bf16*>(smem);
-  float* qs = reinterpret_cast<float*>(smem + size_t(2) * kAdStageElems * 2);
-  float* ps = qs + kAdMaxGroup * kAdQPitch;
-  float* mrun = ps + kAdMaxGroup * kAdKeys;
-  float* lrun = mrun + kAdMaxGroup;
-  float* alpha = lrun + kAdMaxGroup;
-  const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z, t = threadIdx.x;
+  bf16* ps = reinterpret_cast<bf16*>(smem + size_t(kAdStages) * kAdStageElems * 2);  // [16][72]
+  float* wred = reinterpret_cast<float*>(ps + 16 * kAdPPitch);                          // [2][8 warps][8 heads]
+  // KV head fastest: the heads of one (sequence, split) run side by side and
+  // together read whole cache rows (Hkv x 256 bytes per position).
+  const int g = blockIdx.x, s = blockIdx.y, b = blockIdx.z, t = threadIdx.x;
+  const int warp = t >> 5, lane = t & 31, r = lane >> 2, c2 = (lane & 3) * 2;
   const int group = query_heads / kv_heads;
   const int count = int(*position) + 1;
   const int per = ((count + splits - 1) / splits + kAdKeys - 1) / kAdKeys * kAdKeys;
@@ -93,127 +121,116 @@ __global__ void __launch_bounds__(kAdThreads) attention_decode_split_kernel(
   const size_t G = size_t(kv_heads) * 128;
   const bf16* kbase = planes.kv + size_t(b) * planes.seq_stride + planes.k_off + size_t(g) * 128;
   const bf16* vbase = planes.kv + size_t(b) * planes.seq_stride + planes.v_off + size_t(g) * 128;
-  for (int i = t; i < group * 128; i += kAdThreads) {
-    const int h = i / 128, f = i % 128;
-    qs[h * kAdQPitch + f] = widen(q[(size_t(b) * query_heads + g * group + h) * 128 + f]);
-  }
-  if (t < group) {
-    mrun[t] = -INFINITY;
-    lrun[t] = 0.f;
+  // P rows >= group stay zero.
+  for (int i = t; i < 16 * kAdPPitch / 2; i += kAdThreads) reinterpret_cast<uint32_t*>(ps)[i] = 0u;
+  // Q fragments of the 8 k-steps (rows r < group; rows 8..15 are zero).
+  uint32_t qa[8][2];
+  const bool qrow = r < group;
+  const bf16* qh = q + (size_t(b) * query_heads + g * group + (qrow ? r : 0)) * 128;
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    qa[kk][0] = qrow ? *reinterpret_cast<const uint32_t*>(qh + 16 * kk + c2) : 0u;
+    qa[kk][1] = qrow ? *reinterpret_cast<const uint32_t*>(qh + 16 * kk + 8 + c2) : 0u;
   }
   auto load_tile = [&](int tile, int slot) {
     const int base = j0 + tile * kAdKeys;
     const int n = min(kAdKeys, j1 - base);
     bf16* ks = stage + slot * kAdStageElems;
     bf16* vs = ks + kAdKeys * kAdPitch;
-    for (int i = t; i < n * 16; i += kAdThreads) {
+    for (int i = t; i < kAdKeys * 16; i += kAdThreads) {
       const int kk = i >> 4, c = i & 15;
-      cp16(ks + kk * kAdPitch + 8 * c, kbase + size_t(base + kk) * G + 8 * c);
-      cp16(vs + kk * kAdPitch + 8 * c, vbase + size_t(base + kk) * G + 8 * c);
+      if (kk < n) {
+        cp16(ks + kk * kAdPitch + 8 * c, kbase + size_t(base + kk) * G + 8 * c);
+        cp16(vs + kk * kAdPitch + 8 * c, vbase + size_t(base + kk) * G + 8 * c);
+      } else {
+        cp16_zero(ks + kk * kAdPitch + 8 * c, kbase);
+        cp16_zero(vs + kk * kAdPitch + 8 * c, vbase);
+      }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
   const int tiles = (j1 - j0 + kAdKeys - 1) / kAdKeys;
-  constexpr int kMaxPairs = kAdMaxGroup * 64 / kAdThreads;  // output feature pairs per thread
-  float acc[kMaxPairs][2] = {};
-  if (tiles > 0) load_tile(0, 0);
+  float o[2][4] = {};                // this warp's 2 n-tiles (rows r and r + 8)
+  float m_run = -INFINITY, l_run = 0.f;  // head r (identical in every warp)
+  // Tiles t+1 and t+2 load while tile t is processed (one commit group per
+  // tile; an empty group keeps the count when fewer tiles remain).
+  for (int i = 0; i < kAdStages - 1; ++i) {
+    if (i < tiles) load_tile(i, i);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+  }
   for (int tile = 0; tile < tiles; ++tile) {
-    const int slot = tile & 1;
-    if (tile + 1 < tiles) {
-      load_tile(tile + 1, slot ^ 1);
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-    } else {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-    }
-    __syncthreads();
+    const int slot = tile % kAdStages;
+    asm volatile("cp.async.wait_group %0;" ::"n"(kAdStages - 2) : "memory");
+    __syncthreads();  // tile landed; every thread is done with tile - 1, whose slot refills now
+    if (tile + kAdStages - 1 < tiles) load_tile(tile + kAdStages - 1, (tile + kAdStages - 1) % kAdStages);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
     const bf16* ks = stage + slot * kAdStageElems;
     const bf16* vs = ks + kAdKeys * kAdPitch;
     const int n = min(kAdKeys, j1 - (j0 + tile * kAdKeys));
-    // Scores of (key kk, head h), scaled; masked keys are -inf.
-    for (int i = t; i < group * kAdKeys; i += kAdThreads) {
-      const int h = i % group, kk = i / group;
-      float sc = -INFINITY;
-      if (kk < n) {
-        const bf16* kr = ks + kk * kAdPitch;
-        const float* qh = qs + h * kAdQPitch;
-        float d = 0.f;
+    // S for keys 8 warp .. 8 warp + 7.
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    const bf16* krow = ks + (8 * warp + r) * kAdPitch + c2;
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const uint4 w = *reinterpret_cast<const uint4*>(kr + 8 * c);
-          const float4 qa = *reinterpret_cast<const float4*>(qh + 8 * c);
-          const float4 qb = *reinterpret_cast<const float4*>(qh + 8 * c + 4);
-          d = fmaf(qa.x, bf_lo(w.x), d);
-          d = fmaf(qa.y, bf_hi(w.x), d);
-          d = fmaf(qa.z, bf_lo(w.y), d);
-          d = fmaf(qa.w, bf_hi(w.y), d);
-          d = fmaf(qb.x, bf_lo(w.z), d);
-          d = fmaf(qb.y, bf_hi(w.z), d);
-          d = fmaf(qb.z, bf_lo(w.w), d);
-          d = fmaf(qb.w, bf_hi(w.w), d);
-        }
-        sc = d * scale;
-      }
-      ps[h * kAdKeys + kk] = sc;
+    for (int kk = 0; kk < 8; ++kk) {
+      const uint32_t a[4] = {qa[kk][0], 0u, qa[kk][1], 0u};
+      mma16816(sc, a, lds32(krow + 16 * kk), lds32(krow + 16 * kk + 8));
     }
+    const int key = 8 * warp + c2;
+    const float s0 = key < n ? sc[0] * scale : -INFINITY;
+    const float s1 = key + 1 < n ? sc[1] * scale : -INFINITY;
+    float wm = fmaxf(s0, s1);
+    wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, 1));
+    wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, 2));
+    if ((lane & 3) == 0) wred[warp * 8 + r] = wm;
     __syncthreads();
-    // Running max / sum per head: warp h.
-    const int warp = t >> 5, lane = t & 31;
-    if (warp < group) {
-      float* row = ps + warp * kAdKeys;
-      const float s0 = row[lane], s1 = row[lane + 32];
-      float m = fmaxf(s0, s1);
+    float tmax = -INFINITY;
 #pragma unroll
-      for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-      const float m_old = mrun[warp];
-      const float m_new = fmaxf(m_old, m);
-      const float p0 = s0 == -INFINITY ? 0.f : expf(s0 - m_new);
-      const float p1 = s1 == -INFINITY ? 0.f : expf(s1 - m_new);
-      row[lane] = p0;
-      row[lane + 32] = p1;
-      float sum = p0 + p1;
+    for (int w = 0; w < 8; ++w) tmax = fmaxf(tmax, wred[w * 8 + r]);
+    const float m_new = fmaxf(m_run, tmax);
+    const float alpha = m_run == -INFINITY ? 0.f : expf(m_run - m_new);
+    const float p0 = s0 == -INFINITY ? 0.f : expf(s0 - m_new);
+    const float p1 = s1 == -INFINITY ? 0.f : expf(s1 - m_new);
+    const __nv_bfloat162 p2 = __floats2bfloat162_rn(p0, p1);
+    if (qrow) *reinterpret_cast<__nv_bfloat162*>(ps + r * kAdPPitch + key) = p2;
+    float psum = __low2float(p2) + __high2float(p2);  // the BF16 weights the MMA multiplies
+    psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+    psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+    if ((lane & 3) == 0) wred[64 + warp * 8 + r] = psum;
+    __syncthreads();  // P and the partial sums complete
+    float tsum = 0.f;
 #pragma unroll
-      for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-      __syncwarp();
-      if (lane == 0) {
-        const float a = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
-        alpha[warp] = a;
-        lrun[warp] = lrun[warp] * a + sum;
-        mrun[warp] = m_new;
+    for (int w = 0; w < 8; ++w) tsum += wred[64 + w * 8 + r];
+    l_run = l_run * alpha + tsum;
+    m_run = m_new;
+    // O = O * alpha + P V for features 16 warp .. 16 warp + 15.
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      o[j][0] *= alpha;
+      o[j][1] *= alpha;
+    }
+    const bf16* prow = ps + r * kAdPPitch + c2;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const uint32_t a[4] = {lds32(prow + 16 * kk), 0u, lds32(prow + 16 * kk + 8), 0u};
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        uint32_t b0, b1;
+        // Lanes 0..15 address keys 16 kk + lane (rows of the two 8x8 matrices).
+        ldsm_x2_trans(b0, b1, vs + (16 * kk + (lane & 15)) * kAdPitch + 16 * warp + 8 * j);
+        mma16816(o[j], a, b0, b1);
       }
     }
-    __syncthreads();
-    // Output pairs: (head, features 2f, 2f+1).
-#pragma unroll
-    for (int i = 0; i < kMaxPairs; ++i) {
-      const int pair = t + i * kAdThreads;
-      if (pair < group * 64) {
-        const int h = pair / 64, f = (pair % 64) * 2;
-        const float a = alpha[h];
-        float x = acc[i][0] * a, y = acc[i][1] * a;
-        const float* ph = ps + h * kAdKeys;
-        for (int kk = 0; kk < n; ++kk) {
-          const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vs + kk * kAdPitch + f);
-          x = fmaf(ph[kk], bf_lo(v2), x);
-          y = fmaf(ph[kk], bf_hi(v2), y);
-        }
-        acc[i][0] = x;
-        acc[i][1] = y;
-      }
+  }
+  if (qrow) {
+    float* w = ws + ((size_t(b) * query_heads + g * group + r) * splits + s) * kAdWs;
+    if (warp == 0 && (lane & 3) == 0) {
+      w[0] = m_run;
+      w[1] = l_run;
     }
-    __syncthreads();  // the next tile's loads reuse this slot
-  }
-  float* w = ws + ((size_t(b) * query_heads + g * group) * splits + s) * kAdWs;
-  if (t < group) {
-    w[size_t(t) * splits * kAdWs + 0] = mrun[t];
-    w[size_t(t) * splits * kAdWs + 1] = lrun[t];
-  }
 #pragma unroll
-  for (int i = 0; i < kMaxPairs; ++i) {
-    const int pair = t + i * kAdThreads;
-    if (pair < group * 64) {
-      const int h = pair / 64, f = (pair % 64) * 2;
-      w[size_t(h) * splits * kAdWs + 2 + f] = acc[i][0];
-      w[size_t(h) * splits * kAdWs + 3 + f] = acc[i][1];
+    for (int j = 0; j < 2; ++j) {
+      w[2 + 16 * warp + 8 * j + c2] = o[j][0];
+      w[3 + 16 * warp + 8 * j + c2] = o[j][1];
     }
   }
 }
@@ -269,9 +286,11 @@ size_t attention_decode_ws_floats(int batch, int query_heads, int splits) {
 }
 
 int attention_decode_splits(int batch, int kv_heads, int capacity, int sms) {
+  // About eight waves of two resident CTAs per SM, and at least 8 tiles of
+  // keys per split at full capacity.
   const int units = std::max(1, batch * kv_heads);
-  const int want = (4 * sms + units - 1) / units;
-  return std::clamp(want, 1, std::clamp((capacity + kAdKeys - 1) / kAdKeys, 1, 64));
+  const int want = (16 * sms + units - 1) / units;
+  return std::clamp(want, 1, std::clamp(capacity / (8 * kAdKeys), 1, 64));
 }
 
 cudaError_t launch_attention_decode_batched(const bf16* q, KvPlanes planes, const long long* position, int batch,
@@ -282,7 +301,7 @@ cudaError_t launch_attention_decode_batched(const bf16* q, KvPlanes planes, cons
   cudaError_t e = cudaFuncSetAttribute(attention_decode_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        int(kAdSmem));
   if (e != cudaSuccess) return e;
-  attention_decode_split_kernel<<<dim3(splits, kv_heads, batch), kAdThreads, kAdSmem, stream>>>(
+  attention_decode_split_kernel<<<dim3(kv_heads, splits, batch), kAdThreads, kAdSmem, stream>>>(
       q, planes, position, query_heads, kv_heads, splits, scale, ws);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
