@@ -627,7 +627,7 @@ DL_API dl_status dl_gemm_bf16_parts(const void* x, size_t ldx, const void* w, vo
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int p = parts ? int(parts) : dl::gemm_splitk_parts(int(M), int(N), int(K), sms);
-  if (p < 1 || p > 16 || (K / 64) % size_t(p)) return fail(DL_INVALID_ARGUMENT, "gemm parts: parts must divide K/64");
+  if (p < 1 || p > 16 || K / 64 < size_t(p)) return fail(DL_INVALID_ARGUMENT, "gemm parts: 1..16 parts, at most K/64");
   dl::GemmProblem g = {};
   g.x = static_cast<const bf16*>(x);
   g.ldx = int(ldx);

@@ -135,7 +135,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
   const int mt = (a.M + kBM - 1) / kBM;
   const int tiles = mt * (a.N / BN);
   const int units = tiles * a.split;  // unit u: tile u % tiles, K half u / tiles
-  const int kt_per = (a.K / kBK) / a.split;
+  // K part h of a tile covers k-steps [h kt / split, (h + 1) kt / split).
+  const int kt_all = a.K / kBK;
   const int S = a.stages;
 
   if (threadIdx.x == 0) {
@@ -165,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
       for (int u = blockIdx.x; u < units && !*reinterpret_cast<volatile int*>(&abort_flag); u += gridDim.x) {
         const int tile = u % tiles, half = u / tiles;
         const int m0 = (tile % mt) * kBM, n0 = (tile / mt) * BN;
-        for (int kt = half * kt_per; kt < (half + 1) * kt_per; ++kt, ++g) {
+        for (int kt = half * kt_all / a.split; kt < (half + 1) * kt_all / a.split; ++kt, ++g) {
           const int s = g % S;
           if (g >= S && !mbar_wait(&empty[s], ((g / S) - 1) & 1)) {
             record_error(a.err, kErrWaitEmpty);
@@ -194,7 +195,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
         fence_after_sync();
         const uint32_t acc = tmem + uint32_t(buf * BN);
         bool ok = true;
-        for (int kt = 0; kt < kt_per; ++kt, ++g) {
+        const int part = u / tiles;
+        const int kt_n = (part + 1) * kt_all / a.split - part * kt_all / a.split;
+        for (int kt = 0; kt < kt_n; ++kt, ++g) {
           const int s = g % S;
           if (!mbar_wait(&full[s], (g / S) & 1)) {
             record_error(a.err, kErrWaitFull);
@@ -380,15 +383,25 @@ __global__ void splitk_epilogue_kernel(const float* __restrict__ parts, int spli
 }  // namespace
 
 int gemm_splitk_parts(int M, int N, int K, int sms) {
+  // Parts (uneven when K/64 is not a multiple) that fill whole waves of the
+  // SMs best, with at least 8 k-steps each; ties go to fewer parts.
   const int mt = (M + kBM - 1) / kBM, tiles = mt * (N / 128), kt = K / kBK;
   int best = 1;
-  for (int s = 1; s <= 16; ++s)
-    if (kt % s == 0 && kt / s >= 4 && tiles * s <= sms) best = s;
+  double best_fill = 0.0;
+  for (int s = 1; s <= 16 && kt / s >= 8; ++s) {
+    const long long units = (long long)tiles * s;
+    const long long waves = (units + sms - 1) / sms;
+    const double fill = double(units) / double(waves * sms);
+    if (fill > best_fill + 0.02) {
+      best = s;
+      best_fill = fill;
+    }
+  }
   return best;
 }
 
 cudaError_t launch_gemm_tcgen05_parts(const GemmProblem& p, int splits, float* parts, cudaStream_t stream) {
-  if (!gemm_tcgen05_supported(p.M, p.N, p.K) || splits < 1 || splits > 16 || (p.K / kBK) % splits || !parts)
+  if (!gemm_tcgen05_supported(p.M, p.N, p.K) || splits < 1 || splits > 16 || p.K / kBK < splits || !parts)
     return cudaErrorInvalidValue;
   GemmArgs a = {};
   constexpr int BN = 128;

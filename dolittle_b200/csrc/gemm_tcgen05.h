@@ -35,7 +35,8 @@ struct GemmProblem {
 bool gemm_tcgen05_supported(int M, int N, int K);
 cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool pdl);
 
-// Split-K for few rows (batched decode): the K extent in `splits` equal parts,
+// Split-K for few rows (batched decode): the K extent in `splits` parts
+// (k-steps [h kt / splits, (h + 1) kt / splits) for part h),
 // each (tile, part) unit storing its FP32 partial into parts[splits][M][N];
 // then the epilogue kernel adds the parts in part order and applies
 // `epilogue` into out (row stride ld), or writes the FP32 sum to sum_out.
