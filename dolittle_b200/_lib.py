@@ -13,7 +13,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libdolittle_b200.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "dolittle_b200.h")
 
-DL_OK, DL_INVALID_ARGUMENT, DL_UNSUPPORTED, DL_CUDA_ERROR, DL_OUT_OF_MEMORY, DL_DEVICE_FAULT = range(6)
+DL_OK, DL_INVALID_ARGUMENT, DL_UNSUPPORTED, DL_CUDA_ERROR, DL_OUT_OF_MEMORY, DL_DEVICE_FAULT, DL_NOT_READY = range(7)
+DL_EVENT_NONE, DL_EVENT_CONSUMED, DL_EVENT_SELECTED, DL_EVENT_TERMINAL = range(4)
+DL_REASON_LIMIT, DL_REASON_EOS, DL_REASON_CANCELLED, DL_REASON_FAILURE = range(4)
 DL_BF16, DL_F32 = 0, 1
 DL_PREFILL_PARITY, DL_PREFILL_FAST = 0, 1
 DL_DECODE_PERSISTENT, DL_DECODE_KERNELS = 0, 1
@@ -40,6 +42,11 @@ class GenerationStats(C.Structure):
     _fields_ = [("prefill_ms", C.c_double), ("decode_ms", C.c_double), ("decode_steps", C.c_uint64),
                 ("kernels_per_decode_step", C.c_uint64), ("kernels_total", C.c_uint64),
                 ("status", C.c_uint32), ("fault", C.c_uint32)]
+
+
+class SequenceEvent(C.Structure):
+    _fields_ = [("kind", C.c_uint8), ("reason", C.c_uint8), ("reserved", C.c_uint16), ("status", C.c_uint32),
+                ("position", C.c_uint64), ("count", C.c_uint64), ("token", C.c_uint32), ("norm", C.c_float)]
 
 
 class ServeStats(C.Structure):
@@ -103,6 +110,10 @@ SIGNATURES = {
     "dl_engine_read_kv": (C.c_int, [vp, sz, C.c_int, sz, sz, u16p]),
     "dl_engine_generate": (C.c_int, [vp, u32p, sz, sz, C.POINTER(Sampling), C.c_uint64, u32p, sz, C.c_int,
                                      u32p, C.POINTER(sz), u16p, C.POINTER(GenerationStats)]),
+    "dl_engine_start": (C.c_int, [vp, u32p, sz, sz, C.POINTER(Sampling), C.c_uint64, u32p, sz, C.c_int]),
+    "dl_engine_collect": (C.c_int, [vp, sz, C.c_int64, C.POINTER(SequenceEvent)]),
+    "dl_engine_request_stop": (C.c_int, [vp]),
+    "dl_engine_drain": (C.c_int, [vp, u32p, C.POINTER(sz), C.POINTER(GenerationStats)]),
     "dl_serve_create": (C.c_int, [C.POINTER(ModelConfig), C.c_int, sz, sz, sz, C.c_int, C.c_int, C.POINTER(vp)]),
     "dl_serve_destroy": (None, [vp]),
     "dl_serve_nccl_id": (C.c_int, [vp]),

@@ -536,6 +536,31 @@ DL_API dl_status dl_engine_generate(dl_engine* e, const uint32_t* prompt, size_t
 }
 
 
+// ---- device-side sequence loop ----
+DL_API dl_status dl_engine_start(dl_engine* e, const uint32_t* prompt, size_t n_prompt, size_t max_new,
+                                 const dl_sampling* settings, uint64_t seed, const uint32_t* stop_ids,
+                                 size_t n_stop, int prefill_mode) {
+  if (!prompt || !settings || (n_stop && !stop_ids)) return fail(DL_INVALID_ARGUMENT, "engine_start: arguments");
+  DL_ENGINE_CALL(e->impl->start(prompt, n_prompt, max_new, *settings, seed, stop_ids, n_stop, prefill_mode));
+}
+
+DL_API dl_status dl_engine_collect(dl_engine* e, size_t index, int64_t timeout_ms, dl_sequence_event* out) {
+  if (!e || !e->impl || !out) return fail(DL_INVALID_ARGUMENT, "engine_collect: arguments");
+  bool got = false;
+  const dl_status st = guarded([&] {
+    got = e->impl->collect(index, timeout_ms, out);
+    return DL_OK;
+  });
+  if (st != DL_OK) return st;
+  return got ? DL_OK : fail(DL_NOT_READY, "journal event not available");
+}
+
+DL_API dl_status dl_engine_request_stop(dl_engine* e) { DL_ENGINE_CALL(e->impl->request_stop()); }
+
+DL_API dl_status dl_engine_drain(dl_engine* e, uint32_t* tokens_out, size_t* n_out, dl_generation_stats* stats) {
+  DL_ENGINE_CALL(e->impl->drain(tokens_out, n_out, stats));
+}
+
 // ---- batched serving ----
 DL_API dl_status dl_serve_create(const dl_model_config* config, int device, size_t batch, size_t capacity,
                                  size_t chunk_rows, int tp_rank, int tp_size, dl_serve** out) {

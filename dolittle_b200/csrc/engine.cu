@@ -6,10 +6,15 @@
 #include <stdexcept>
 #include <string>
 
+#include <atomic>
+#include <chrono>
+#include <thread>
+
 #include "attention_decode.h"
 #include "attention_prefill_tc.h"
 #include "engine.h"
 #include "gemm_tcgen05.h"
+#include "sequence.h"
 #include "steering.h"
 
 namespace dl {
@@ -169,11 +174,26 @@ Engine::Engine(const dl_model_config& cfg, int device, size_t capacity, size_t m
   attn_tc_ = attention_prefill_tc_maps(q_rot_, int(R), int(cfg.query_heads), static_cast<const bf16*>(kv_arena_),
                                        kv_block, int(capacity), int(L), int(cfg.kv_heads), int(d), vt_, vt_stride_);
   check(launch_inv_freq(inv_freq_, int(d), cfg.theta, stream_), "inv_freq");
+  // Journal of the device-side loop (prompt event, a selection per token, a
+  // terminal event) and its cancel flag, in mapped host memory.
+  journal_cap_ = capacity + 2;
+  check(cudaHostAlloc(reinterpret_cast<void**>(&journal_host_), journal_cap_ * sizeof(dl_sequence_event),
+                      cudaHostAllocMapped),
+        "journal");
+  check(cudaHostGetDevicePointer(reinterpret_cast<void**>(&journal_dev_), journal_host_, 0), "journal map");
+  check(cudaHostAlloc(reinterpret_cast<void**>(&cancel_host_), 64, cudaHostAllocMapped), "cancel flag");
+  check(cudaHostGetDevicePointer(reinterpret_cast<void**>(&cancel_dev_), cancel_host_, 0), "cancel map");
+  std::memset(journal_host_, 0, journal_cap_ * sizeof(dl_sequence_event));
+  *cancel_host_ = 0;
   check(cudaStreamSynchronize(stream_), "init sync");
 }
 
 Engine::~Engine() {
+  if (stream_) cudaStreamSynchronize(stream_);
   if (decode_exec_) cudaGraphExecDestroy(decode_exec_);
+  if (loop_exec_) cudaGraphExecDestroy(loop_exec_);
+  if (journal_host_) cudaFreeHost(journal_host_);
+  if (cancel_host_) cudaFreeHost(cancel_host_);
   attention_prefill_tc_free(attn_tc_);
   cudaFree(recon_head_);
   cudaFree(persist_layers_);
@@ -819,10 +839,10 @@ void Engine::capture_decode_graph() {
   graph_path_ = decode_path_;
 }
 
-void Engine::generate(const uint32_t* prompt, size_t n_prompt, size_t max_new, const dl_sampling& s,
-                      uint64_t seed, const uint32_t* stop_ids, size_t n_stop, int prefill_mode,
-                      uint32_t* tokens_out, size_t* n_out, uint16_t* logits_out, dl_generation_stats* stats) {
+void Engine::begin_sequence(const uint32_t* prompt, size_t n_prompt, size_t max_new, const dl_sampling& s,
+                            uint64_t seed, const uint32_t* stop_ids, size_t n_stop, int prefill_mode) {
   check(cudaSetDevice(device_), "cudaSetDevice");
+  if (seq_running_) throw std::logic_error("a device sequence is running: drain it first");
   if (!n_prompt || !max_new) throw std::invalid_argument("empty prompt or budget");
   if (n_prompt + max_new > capacity_) throw std::length_error("sequence exceeds KV capacity");
   validate_sampling(s, cfg_.vocabulary);
@@ -835,6 +855,12 @@ void Engine::generate(const uint32_t* prompt, size_t n_prompt, size_t max_new, c
   if (!sampler_.arena) check(sampler_init(sampler_, cfg_.vocabulary, true), "sampler init");
   check(sampler_start(sampler_, s, seed, stop_ids, n_stop, stream_), "sampler start");
   stop_mask_ = sampler_.stop_mask;  // the greedy finisher latches on the same mask
+}
+
+void Engine::generate(const uint32_t* prompt, size_t n_prompt, size_t max_new, const dl_sampling& s,
+                      uint64_t seed, const uint32_t* stop_ids, size_t n_stop, int prefill_mode,
+                      uint32_t* tokens_out, size_t* n_out, uint16_t* logits_out, dl_generation_stats* stats) {
+  begin_sequence(prompt, n_prompt, max_new, s, seed, stop_ids, n_stop, prefill_mode);
   capture_decode_graph();
   const size_t V = cfg_.vocabulary;
   check(cudaEventRecord(ev_[0], stream_), "event");
@@ -890,6 +916,139 @@ void Engine::generate(const uint32_t* prompt, size_t n_prompt, size_t max_new, c
     stats->decode_steps = max_new - 1;
     stats->kernels_per_decode_step = kernels_per_step_;
     stats->kernels_total = launches_ + kernels_per_step_ * (max_new - 1);
+    stats->status = st.result[1];
+    stats->fault = st.err;
+  }
+  if (st.err) throw std::runtime_error("device fault word " + std::to_string(st.err));
+}
+
+// ---------------------------------------------------------------------------
+// Device-side generation loop (DeviceSequence): one graph = journal the
+// first selection and set the loop condition, then a WHILE node whose body
+// is the decode step plus the journal/condition kernel.
+// ---------------------------------------------------------------------------
+void Engine::build_loop_graph() {
+  if (loop_exec_ && loop_capture_layer_ == capture_layer_ && loop_edit_layer_ == edit_layer_ && loop_mode_ == mode_ &&
+      loop_path_ == decode_path_)
+    return;
+  if (decode_path_ == DL_DECODE_PERSISTENT) persistent_decode_ready();  // plans outside the capture
+  if (loop_exec_) {
+    cudaGraphExecDestroy(loop_exec_);
+    loop_exec_ = nullptr;
+  }
+  const unsigned* result = mode_ == 0 ? state_->result : sampler_.result;
+  cudaGraph_t g = nullptr;
+  check(cudaGraphCreate(&g, 0), "loop graph");
+  try {
+    cudaGraphConditionalHandle loop;
+    check(cudaGraphConditionalHandleCreate(&loop, g, 0, 0), "loop handle");
+    cudaGraph_t captured = nullptr;
+    check(cudaStreamBeginCaptureToGraph(stream_, g, nullptr, nullptr, 0, cudaStreamCaptureModeThreadLocal),
+          "capture first selection");
+    const cudaError_t e1 = launch_journal_selection(&state_->step, result, &state_->position, stop_mask_,
+                                                    &state_->limit, cancel_dev_, journal_dev_, loop, true, stream_);
+    check(cudaStreamEndCapture(stream_, &captured), "end capture");
+    check(e1, "journal kernel");
+    cudaGraphNode_t first = nullptr;
+    size_t nodes = 1;
+    check(cudaGraphGetNodes(g, &first, &nodes), "loop graph nodes");
+    cudaGraphNodeParams cp = {};
+    cp.type = cudaGraphNodeTypeConditional;
+    cp.conditional.handle = loop;
+    cp.conditional.type = cudaGraphCondTypeWhile;
+    cp.conditional.size = 1;
+    cudaGraphNode_t node = nullptr;
+    check(cudaGraphAddNode(&node, g, &first, 1, &cp), "while node");
+    cudaGraph_t body = cp.conditional.phGraph_out[0];
+    check(cudaStreamBeginCaptureToGraph(stream_, body, nullptr, nullptr, 0, cudaStreamCaptureModeThreadLocal),
+          "capture loop body");
+    launches_ = 0;
+    try {
+      decode_step(false);
+      check(launch_journal_selection(&state_->step, result, &state_->position, stop_mask_, &state_->limit,
+                                     cancel_dev_, journal_dev_, loop, true, stream_),
+            "journal kernel");
+    } catch (...) {
+      cudaStreamEndCapture(stream_, &captured);
+      throw;
+    }
+    check(cudaStreamEndCapture(stream_, &captured), "end capture");
+    kernels_per_step_ = launches_ + 1;
+    check(cudaGraphInstantiate(&loop_exec_, g, 0), "loop graph instantiate");
+  } catch (...) {
+    cudaGraphDestroy(g);
+    throw;
+  }
+  cudaGraphDestroy(g);
+  loop_capture_layer_ = capture_layer_;
+  loop_edit_layer_ = edit_layer_;
+  loop_mode_ = mode_;
+  loop_path_ = decode_path_;
+}
+
+void Engine::start(const uint32_t* prompt, size_t n_prompt, size_t max_new, const dl_sampling& s, uint64_t seed,
+                   const uint32_t* stop_ids, size_t n_stop, int prefill_mode) {
+  begin_sequence(prompt, n_prompt, max_new, s, seed, stop_ids, n_stop, prefill_mode);
+  build_loop_graph();
+  std::memset(journal_host_, 0, (max_new + 2) * sizeof(dl_sequence_event));
+  *reinterpret_cast<volatile unsigned*>(cancel_host_) = 0;
+  const unsigned limit = unsigned(max_new);
+  check(cudaMemcpyAsync(&state_->limit, &limit, 4, cudaMemcpyHostToDevice, stream_), "limit");
+  check(cudaEventRecord(ev_[0], stream_), "event");
+  launches_ = 0;
+  consume_rows(prompt, n_prompt, true, prefill_mode, 0);
+  check(launch_journal_consumed(journal_dev_, n_prompt, stream_), "journal");
+  select(residual_ + size_t(last_rows_ - 1) * cfg_.hidden, false, true);
+  check(cudaEventRecord(ev_[1], stream_), "event");
+  check(cudaGraphLaunch(loop_exec_, stream_), "loop launch");
+  check(cudaEventRecord(ev_[2], stream_), "event");
+  seq_running_ = true;
+  seq_max_new_ = max_new;
+  seq_launches_ = launches_ + 1;
+}
+
+bool Engine::collect(size_t index, long long timeout_ms, dl_sequence_event* out) {
+  if (!seq_running_ && index >= seq_max_new_ + 2) throw std::invalid_argument("no such journal event");
+  if (index >= journal_cap_) throw std::invalid_argument("journal index beyond capacity + 2");
+  const volatile uint8_t* kind = &journal_host_[index].kind;
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    if (*kind) {
+      std::atomic_thread_fence(std::memory_order_acquire);
+      std::memcpy(out, const_cast<const dl_sequence_event*>(&journal_host_[index]), sizeof(*out));
+      return true;
+    }
+    const cudaError_t q = cudaStreamQuery(stream_);
+    if (q != cudaSuccess && q != cudaErrorNotReady) check(q, "sequence");
+    if (q == cudaSuccess && !*kind) return false;  // the loop ended without this event
+    if (timeout_ms >= 0 &&
+        std::chrono::steady_clock::now() - t0 >= std::chrono::milliseconds(timeout_ms))
+      return false;
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
+void Engine::request_stop() { *reinterpret_cast<volatile unsigned*>(cancel_host_) = 1; }
+
+void Engine::drain(uint32_t* tokens_out, size_t* n_out, dl_generation_stats* stats) {
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  if (!seq_running_) throw std::logic_error("no device sequence is running");
+  seq_running_ = false;
+  check(cudaStreamSynchronize(stream_), "drain");
+  DeviceState st;
+  check(cudaMemcpy(&st, state_, sizeof(st), cudaMemcpyDeviceToHost), "state");
+  const size_t n = std::min(size_t(std::max(st.step, 0)), seq_max_new_);
+  if (tokens_out && n) check(cudaMemcpy(tokens_out, history_, n * 4, cudaMemcpyDeviceToHost), "history");
+  if (n_out) *n_out = n;
+  float pre = 0, dec = 0;
+  check(cudaEventElapsedTime(&pre, ev_[0], ev_[1]), "elapsed");
+  check(cudaEventElapsedTime(&dec, ev_[1], ev_[2]), "elapsed");
+  if (stats) {
+    stats->prefill_ms = pre;
+    stats->decode_ms = dec;
+    stats->decode_steps = n ? n - 1 : 0;
+    stats->kernels_per_decode_step = kernels_per_step_;
+    stats->kernels_total = seq_launches_ + kernels_per_step_ * (n ? n - 1 : 0);
     stats->status = st.result[1];
     stats->fault = st.err;
   }

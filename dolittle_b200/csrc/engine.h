@@ -37,7 +37,8 @@ struct DeviceState {
   unsigned ticket;     // argmax completion counter
   unsigned barrier;    // persistent decode: grid barrier arrivals
   unsigned exit_ticket;
-  unsigned pad[7];
+  unsigned limit;      // device sequence loop: selections to make
+  unsigned pad[6];
 };
 
 class Engine {
@@ -72,6 +73,13 @@ class Engine {
                 uint64_t seed, const uint32_t* stop_ids, size_t n_stop, int prefill_mode,
                 uint32_t* tokens_out, size_t* n_out, uint16_t* logits_out,
                 dl_generation_stats* stats);
+  // Device-side generation loop (role of the reference's DeviceSequence):
+  // start returns at once; the journal reports each selection.
+  void start(const uint32_t* prompt, size_t n_prompt, size_t max_new, const dl_sampling& s, uint64_t seed,
+             const uint32_t* stop_ids, size_t n_stop, int prefill_mode);
+  bool collect(size_t index, long long timeout_ms, dl_sequence_event* out);
+  void request_stop();
+  void drain(uint32_t* tokens_out, size_t* n_out, dl_generation_stats* stats);
 
  private:
   TensorView view(size_t index);
@@ -86,6 +94,9 @@ class Engine {
   void project(const bf16* x, int x_stride, int rows, int in_width, int prologue, const bf16* norm_w,
                int epilogue, GemvSegment* segs, int nseg, bool pdl);
   void capture_decode_graph();
+  void build_loop_graph();
+  void begin_sequence(const uint32_t* prompt, size_t n_prompt, size_t max_new, const dl_sampling& s,
+                      uint64_t seed, const uint32_t* stop_ids, size_t n_stop, int prefill_mode);
   bool persistent_decode_ready();
   void launch_persistent_step(bool greedy);
   void check(cudaError_t e, const char* what);
@@ -133,6 +144,16 @@ class Engine {
   int mode_ = 0, graph_mode_ = -1;
   Sampler sampler_;
   cudaEvent_t ev_[4] = {};
+  // device-side sequence loop: journal and cancel flag in mapped host memory
+  dl_sequence_event* journal_host_ = nullptr;
+  dl_sequence_event* journal_dev_ = nullptr;
+  size_t journal_cap_ = 0;
+  unsigned* cancel_host_ = nullptr;
+  unsigned* cancel_dev_ = nullptr;
+  cudaGraphExec_t loop_exec_ = nullptr;
+  int loop_capture_layer_ = -2, loop_edit_layer_ = -2, loop_mode_ = -1, loop_path_ = -1;
+  bool seq_running_ = false;
+  size_t seq_max_new_ = 0, seq_launches_ = 0;
   // persistent decode step (one cooperative launch per token)
   int decode_path_ = DL_DECODE_PERSISTENT, graph_path_ = -1;
   int persist_state_ = -1;  // -1 not planned, 0 unsupported, 1 ready

@@ -192,6 +192,42 @@ class Engine:
         check(lib().dl_engine_read_kv(self._h, layer, int(values), first, count, out.ctypes.data_as(_lib.u16p)))
         return out
 
+    # ---- device-side sequence loop (DeviceSequence) ---------------------
+    def start(self, prompt, max_new: int, settings: Settings | None = None, seed: int = 0, stop_ids=(),
+              prefill: int = _lib.DL_PREFILL_PARITY) -> None:
+        """Enqueue the prompt pass, the first selection and the device loop
+        of up to max_new selections; returns at once (see collect/drain)."""
+        settings = settings or Settings()
+        p = _u32(prompt)
+        stops = _u32(list(stop_ids) or [0])
+        s = settings.c()
+        check(lib().dl_engine_start(self._h, p.ctypes.data_as(_lib.u32p), p.size, max_new, C.byref(s), seed,
+                                    stops.ctypes.data_as(_lib.u32p), len(stop_ids), prefill))
+        self._max_new = max_new  # the running sequence's budget (drain's buffer size)
+
+    def collect(self, index: int, timeout_ms: int = -1):
+        """Journal event `index` (0: prompt consumed, k: k-th selection, then
+        a terminal event), or None if it did not arrive in time."""
+        ev = _lib.SequenceEvent()
+        st = lib().dl_engine_collect(self._h, index, timeout_ms, C.byref(ev))
+        if st == _lib.DL_NOT_READY:
+            return None
+        check(st)
+        return ev
+
+    def request_stop(self) -> None:
+        check(lib().dl_engine_request_stop(self._h))
+
+    def drain(self) -> Generation:
+        out = np.zeros(max(1, getattr(self, "_max_new", 0)), np.uint32)
+        n = C.c_size_t()
+        stats = _lib.GenerationStats()
+        check(lib().dl_engine_drain(self._h, out.ctypes.data_as(_lib.u32p), C.byref(n), C.byref(stats)))
+        return Generation(tokens=out[:n.value].tolist(), prefill_ms=stats.prefill_ms, decode_ms=stats.decode_ms,
+                          decode_steps=int(stats.decode_steps),
+                          kernels_per_decode_step=int(stats.kernels_per_decode_step),
+                          kernels_total=int(stats.kernels_total), status=int(stats.status))
+
     def generate(self, prompt, max_new: int, settings: Settings | None = None, seed: int = 0,
                  stop_ids=(), prefill: int = _lib.DL_PREFILL_PARITY, want_logits: bool = False) -> Generation:
         settings = settings or Settings()

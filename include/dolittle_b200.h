@@ -52,7 +52,8 @@ typedef enum {
   DL_UNSUPPORTED = 2,       /* unsupported dtype/shape (reference: invalid_argument) */
   DL_CUDA_ERROR = 3,        /* launch or runtime error (reference: runtime_error) */
   DL_OUT_OF_MEMORY = 4,     /* reference: length_error on budget */
-  DL_DEVICE_FAULT = 5       /* a kernel recorded a bounded-wait timeout */
+  DL_DEVICE_FAULT = 5,      /* a kernel recorded a bounded-wait timeout */
+  DL_NOT_READY = 6          /* dl_engine_collect: the event did not arrive in time */
 } dl_status;
 
 typedef enum { DL_BF16 = 0, DL_F32 = 1 } dl_dtype;
@@ -361,6 +362,43 @@ DL_API dl_status dl_attention_decode_batched(const void* query, const void* kv, 
                                              size_t k_offset, size_t v_offset, const int64_t* position,
                                              size_t batch, size_t query_heads, size_t kv_heads, size_t capacity,
                                              void* output, void* workspace, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Device-side generation loop (DeviceSequence, src/inference/decoding/     */
+/* device.h:84-139): dl_engine_start enqueues the prompt pass, the first    */
+/* selection and ONE graph launch whose conditional WHILE node replays the  */
+/* decode step on the device until a stop ID, a failed selection, a cancel  */
+/* request or max_new selections; the host follows a journal of 32-byte     */
+/* events in mapped host memory: event 0 = prompt consumed, event k = the   */
+/* k-th selection, then one terminal event.                                 */
+/* ------------------------------------------------------------------------ */
+enum { DL_EVENT_NONE = 0, DL_EVENT_CONSUMED = 1, DL_EVENT_SELECTED = 2, DL_EVENT_TERMINAL = 3 };
+enum { DL_REASON_LIMIT = 0, DL_REASON_EOS = 1, DL_REASON_CANCELLED = 2, DL_REASON_FAILURE = 3 };
+
+typedef struct {
+  uint8_t kind;      /* DL_EVENT_*; written last (0 until the event is complete) */
+  uint8_t reason;    /* terminal events: DL_REASON_* */
+  uint16_t reserved;
+  uint32_t status;   /* selection status (0 ok) */
+  uint64_t position; /* absolute position after the event */
+  uint64_t count;    /* prompt tokens (consumed) or selections so far */
+  uint32_t token;    /* selected token */
+  float norm;        /* reserved (injection events) */
+} dl_sequence_event;
+
+/* Same arguments and validation as dl_engine_generate; returns at once. */
+DL_API dl_status dl_engine_start(dl_engine* e, const uint32_t* prompt, size_t n_prompt, size_t max_new,
+                                 const dl_sampling* settings, uint64_t seed, const uint32_t* stop_ids,
+                                 size_t n_stop, int prefill_mode);
+/* Waits up to timeout_ms (< 0: no limit) for journal event `index`;
+ * DL_NOT_READY if it did not arrive. */
+DL_API dl_status dl_engine_collect(dl_engine* e, size_t index, int64_t timeout_ms, dl_sequence_event* out);
+/* Asks the running loop to stop after its current step (terminal reason
+ * DL_REASON_CANCELLED). */
+DL_API dl_status dl_engine_request_stop(dl_engine* e);
+/* Waits for the loop to finish; tokens_out (capacity max_new) receives the
+ * selections, *n_out their count (a stop ID is included). */
+DL_API dl_status dl_engine_drain(dl_engine* e, uint32_t* tokens_out, size_t* n_out, dl_generation_stats* stats);
 
 #ifdef __cplusplus
 }
