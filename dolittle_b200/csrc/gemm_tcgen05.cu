@@ -118,7 +118,11 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, bf16* out, int ld
 // the ring, warp 1 issues the MMAs into one of two TMEM accumulators, and
 // warps 2-5 (TMEM lane groups 2, 3, 0, 1) drain the other accumulator, so a
 // tile's epilogue overlaps the next tile's main loop.
-template <int BN>
+// SWAP (a few rows, split-K partials only): the weights are the 128-row A
+// operand and the M <= BN input rows the N side, D = W X^T lands in TMEM as
+// [128 output features][BN rows]; a stage then carries 16 KB of weights and
+// BN x 128 bytes of inputs instead of a mostly zero-filled 128-row input tile.
+template <int BN, bool SWAP = false>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_constant__ GemmArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ uint64_t full[8], empty[8], acc_full[2], acc_empty[2];
@@ -132,8 +136,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
   const uint32_t base_s = (smem_addr(smem_raw) + 1023u) & ~1023u;
   unsigned char* ring = smem_raw + (base_s - smem_addr(smem_raw));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mt = (a.M + kBM - 1) / kBM;
-  const int tiles = mt * (a.N / BN);
+  const int mt = SWAP ? 1 : (a.M + kBM - 1) / kBM;
+  const int tiles = SWAP ? a.N / kBM : mt * (a.N / BN);
   const int units = tiles * a.split;  // unit u: tile u % tiles, K half u / tiles
   // K part h of a tile covers k-steps [h kt / split, (h + 1) kt / split).
   const int kt_all = a.K / kBK;
@@ -165,7 +169,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
       int g = 0;
       for (int u = blockIdx.x; u < units && !*reinterpret_cast<volatile int*>(&abort_flag); u += gridDim.x) {
         const int tile = u % tiles, half = u / tiles;
-        const int m0 = (tile % mt) * kBM, n0 = (tile / mt) * BN;
+        // A rows m0.. (inputs; SWAP: weights), B rows n0.. (weights; SWAP: inputs).
+        const int m0 = SWAP ? tile * kBM : (tile % mt) * kBM, n0 = SWAP ? 0 : (tile / mt) * BN;
         for (int kt = half * kt_all / a.split; kt < (half + 1) * kt_all / a.split; ++kt, ++g) {
           const int s = g % S;
           if (g >= S && !mbar_wait(&empty[s], ((g / S) - 1) & 1)) {
@@ -232,8 +237,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
         break;
       }
       fence_after_sync();
-      const int m0 = (tile % mt) * kBM, n0 = (tile / mt) * BN;
-      const int row = m0 + q * 32 + lane;
+      const int m0 = SWAP ? tile * kBM : (tile % mt) * kBM, n0 = SWAP ? 0 : (tile / mt) * BN;
+      const int row = m0 + q * 32 + lane;  // SWAP: the output feature
       int si = 0;
       for (int i = 1; i < a.nseg; ++i)
         if (n0 >= a.seg_n0[i]) si = i;
@@ -241,7 +246,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
       const int ld = a.seg_ld[si];
       const int c0 = n0 - a.seg_n0[si];
       const uint32_t acc = tmem + uint32_t(buf * BN) + (uint32_t(q * 32) << 16);
-      if (a.partial_only) {
+      if (SWAP) {
+        // D[feature row][input m]: part `half`, FP32, [part][M][N] as below;
+        // for each m the warp's 32 features are 128 contiguous bytes.
+        float* mine = a.partial + size_t(half) * a.M * a.N + row;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(acc + uint32_t(c * 32), r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i < a.M) mine[size_t(c * 32 + i) * a.N] = __uint_as_float(r[i]);
+        }
+      } else if (a.partial_only) {
         // K part `half` of the tile as FP32; the split-K epilogue kernel adds
         // the parts in order.
         float* mine = a.partial + (size_t(half) * a.M + row) * a.N + n0;
@@ -404,9 +421,18 @@ cudaError_t launch_gemm_tcgen05_parts(const GemmProblem& p, int splits, float* p
   if (!gemm_tcgen05_supported(p.M, p.N, p.K) || splits < 1 || splits > 16 || p.K / kBK < splits || !parts)
     return cudaErrorInvalidValue;
   GemmArgs a = {};
-  constexpr int BN = 128;
-  if (!encode_2d(&a.map_a, p.x, uint64_t(p.M), uint64_t(p.K), uint64_t(p.ldx), kBM)) return cudaErrorInvalidValue;
-  if (!encode_2d(&a.map_b, p.w, uint64_t(p.N), uint64_t(p.K), uint64_t(p.K), uint32_t(BN))) return cudaErrorInvalidValue;
+  // Up to 128 rows: the swapped form (weights as the 128-row operand).
+  const bool swap = p.M <= 128;
+  const int BN = swap ? (p.M <= 32 ? 32 : p.M <= 64 ? 64 : 128) : 128;
+  if (swap) {
+    if (!encode_2d(&a.map_a, p.w, uint64_t(p.N), uint64_t(p.K), uint64_t(p.K), kBM)) return cudaErrorInvalidValue;
+    if (!encode_2d(&a.map_b, p.x, uint64_t(p.M), uint64_t(p.K), uint64_t(p.ldx), uint32_t(BN)))
+      return cudaErrorInvalidValue;
+  } else {
+    if (!encode_2d(&a.map_a, p.x, uint64_t(p.M), uint64_t(p.K), uint64_t(p.ldx), kBM)) return cudaErrorInvalidValue;
+    if (!encode_2d(&a.map_b, p.w, uint64_t(p.N), uint64_t(p.K), uint64_t(p.K), uint32_t(BN)))
+      return cudaErrorInvalidValue;
+  }
   a.M = p.M;
   a.N = p.N;
   a.K = p.K;
@@ -421,14 +447,21 @@ cudaError_t launch_gemm_tcgen05_parts(const GemmProblem& p, int splits, float* p
   const size_t smem = size_t(a.stages) * stage_bytes + 1024;
   int sms = 148, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const long long units = (long long)((p.M + kBM - 1) / kBM) * (p.N / BN) * splits;
+  const long long tiles = swap ? p.N / kBM : (long long)((p.M + kBM - 1) / kBM) * (p.N / BN);
+  const long long units = tiles * splits;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(std::min<long long>(units, sms)));
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaFuncSetAttribute(gemm_tcgen05_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  return cudaLaunchKernelEx(&cfg, gemm_tcgen05_kernel<BN>, a);
+  auto go = [&](auto kernel) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    return cudaLaunchKernelEx(&cfg, kernel, a);
+  };
+  if (!swap) return go(gemm_tcgen05_kernel<128>);
+  if (BN == 32) return go(gemm_tcgen05_kernel<32, true>);
+  if (BN == 64) return go(gemm_tcgen05_kernel<64, true>);
+  return go(gemm_tcgen05_kernel<128, true>);
 }
 
 cudaError_t launch_gemm_splitk_epilogue(const float* parts, int splits, int M, int N, int epilogue, bf16* out,
