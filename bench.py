@@ -547,6 +547,124 @@ def run_serve(args):
     return 0
 
 
+def run_branches(args):
+    """Configs 3 and 4 as data-parallel units (replicas: the units split
+    round-robin over the launched ranks, no collective on the data path).
+
+    steer (config 3): prompt of 256 uniform IDs; block 24's output at token
+    200 is captured; the steering direction is a seeded unit Gaussian with
+    strength 4 x that row's norm at block 24, row 200 (the reference's
+    DeviceIntervention law); the steered and unsteered branches then decode
+    512 tokens at temperature 0.7 / top-p 0.9, seed 7.
+    nla (config 4): a 64-token prefix whose marker row carries the captured
+    vector (injection law, scale 150); 16 samples of 128 tokens at
+    temperature 1.0; each sample then passes the reconstructor (last-token
+    block output through a 4096 x 4096 head)."""
+    world, rank, local = dist_setup()
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+    import numpy as np
+    import dolittle_b200 as dl
+    from dolittle_b200 import replicas
+    cfg = dl.QWEN3_8B
+    V = cfg.vocabulary
+    steer = args.workload == "steer"
+    prompt = np.random.Generator(np.random.Philox(SEED + 3)).integers(0, V, 256, dtype=np.uint32)
+    engine = dl.Engine(cfg, device=local, capacity=256 + 512 + 8, max_rows=256)
+    engine.init_random(SEED, 0.02)
+    # The captured row: block 24's output at token 200 of the prompt.
+    engine.set_capture(24)
+    engine.consume_view(prompt, dl.DL_PREFILL_FAST)
+    h_bits = engine.read_capture(200, 1)[0]
+    engine.set_capture(-1)
+    engine.reset()
+    if steer:
+        n_units, new_tokens = 2, 512
+        u = np.random.Generator(np.random.Philox(7)).standard_normal(cfg.hidden).astype(np.float32)
+        u /= np.linalg.norm(u)
+        settings = dl.Settings(dl.SelectionMode.categorical, temperature=0.7, top_p=0.9)
+    else:
+        n_units, new_tokens = 16, 128
+        prefix = prompt[:64].copy()
+        marker = 32
+        settings = dl.Settings(dl.SelectionMode.categorical, temperature=1.0)
+    mine = replicas.shard(n_units, rank, world)
+
+    def run_unit(unit):
+        if steer:
+            if unit == 1:
+                engine.set_intervention(24, 200, 4.0, u)
+            else:
+                engine.set_intervention(-1)
+            g = engine.generate(prompt, new_tokens, settings=settings, seed=7, prefill=dl.DL_PREFILL_FAST)
+            return g, None
+        engine.set_injection(marker, h_bits, 150.0)
+        g = engine.generate(prefix, new_tokens, settings=settings, seed=unit, prefill=dl.DL_PREFILL_FAST)
+        engine.set_injection(-1)
+        return g, g.tokens
+
+    for _ in range(args.warmup):
+        run_unit(mine[0] if mine else 0)
+    if not steer:
+        # Reconstructor head: seeded BF16 weights ~N(0, 0.02).
+        from dolittle_b200.checkpoint import _bf16_bits
+        w = np.random.Generator(np.random.Philox(SEED + 9)).standard_normal((cfg.hidden, cfg.hidden),
+                                                                             dtype=np.float32) * np.float32(0.02)
+        engine.set_reconstruction_head(_bf16_bits(w))
+    clocks = Clocks(local)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    t0 = time.perf_counter()
+    decode_s = prefill_s = 0.0
+    recon_s = 0.0
+    for _ in range(args.steps):
+        for unit in mine:
+            g, toks = run_unit(unit)
+            decode_s += g.decode_ms / 1000.0
+            prefill_s += g.prefill_ms / 1000.0
+            if toks is not None:
+                t1 = time.perf_counter()
+                engine.reconstruct(toks)
+                recon_s += time.perf_counter() - t1
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    clk = clocks.stop()
+    decode_s, prefill_s, wall = replicas.max_over_ranks(dist, [decode_s, prefill_s, wall])
+    if rank == 0:
+        tokens = args.steps * n_units * new_tokens
+        line = {
+            "metric": ("Qwen3-8B steering comparison decode tok/s (config 3)" if steer
+                       else "Qwen3-8B NLA verbalizer sample tok/s (config 4)"),
+            "value": tokens / decode_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000 * wall / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init BF16 weights ~N(0,0.02), uniform prompt IDs)",
+            "config": {"workload": ("config 3: 256-token prompt, capture block 24 at token 200, steered and "
+                                    "unsteered branches, 512 tokens each at T 0.7 / top-p 0.9, seed 7") if steer
+                       else ("config 4: 64-token prefix with the injected marker row, 16 samples x 128 tokens "
+                             "at T 1.0, then the reconstructor on each sample"),
+                       "parallelism": f"replicas x{world} over the {n_units} independent units"},
+            "e2e": {"value": tokens / wall, "unit": "tok/s (host loop, prompt passes"
+                    + (")" if steer else " and reconstructions)"),
+                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "prefill_s": prefill_s,
+            "clocks": clk,
+        }
+        if not steer:
+            line["reconstruct_s"] = recon_s
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_profile_case(args):
     """Small standalone cases for ncu captures (a few hundred MB on device).
 
@@ -602,14 +720,17 @@ def main():
                     help="prompt pass on the tcgen05 GEMMs (fast) or in the reference order (parity)")
     ap.add_argument("--profile", choices=["gemv", "decode", "prefill", "persist"], default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
-    ap.add_argument("--workload", choices=["decode", "serve"], default="decode",
-                    help="decode: config 2 (headline); serve: config 5 batched serving, TP over the ranks")
+    ap.add_argument("--workload", choices=["decode", "serve", "steer", "nla"], default="decode",
+                    help="decode: config 2 (headline); serve: config 5 batched serving, TP over the ranks; "
+                         "steer / nla: configs 3 / 4, units split over the ranks")
     ap.add_argument("--serve-batch", type=int, default=32)
     ap.add_argument("--serve-prompt", type=int, default=8192)
     ap.add_argument("--serve-steps", type=int, default=32, help="decode steps per timed call (config 5)")
     args = ap.parse_args()
     if args.workload == "serve" and args.impl == "ours":
         return run_serve(args)
+    if args.workload in ("steer", "nla") and args.impl == "ours":
+        return run_branches(args)
     if args.profile:
         return run_profile_case(args)
     if args.impl == "reference":
