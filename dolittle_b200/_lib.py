@@ -118,6 +118,8 @@ SIGNATURES = {
     "dl_serve_destroy": (None, [vp]),
     "dl_serve_nccl_id": (C.c_int, [vp]),
     "dl_serve_connect": (C.c_int, [vp, vp]),
+    "dl_serve_ipc_handle": (C.c_int, [vp, vp]),
+    "dl_serve_connect_peers": (C.c_int, [vp, vp]),
     "dl_serve_init_random": (C.c_int, [vp, C.c_uint64, C.c_float]),
     "dl_serve_set_tensor": (C.c_int, [vp, sz, vp, sz]),
     "dl_serve_get_tensor": (C.c_int, [vp, sz, vp, sz]),

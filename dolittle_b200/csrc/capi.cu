@@ -596,6 +596,14 @@ DL_API dl_status dl_serve_connect(dl_serve* s, const unsigned char* id128) {
   if (!id128) return fail(DL_INVALID_ARGUMENT, "serve_connect: null id");
   DL_SERVE_CALL(s->impl->connect(id128));
 }
+DL_API dl_status dl_serve_ipc_handle(dl_serve* s, unsigned char* handle64) {
+  if (!handle64) return fail(DL_INVALID_ARGUMENT, "serve_ipc_handle: null");
+  DL_SERVE_CALL(s->impl->ipc_handle(handle64));
+}
+DL_API dl_status dl_serve_connect_peers(dl_serve* s, const unsigned char* handles) {
+  if (!handles) return fail(DL_INVALID_ARGUMENT, "serve_connect_peers: null");
+  DL_SERVE_CALL(s->impl->connect_peers(handles));
+}
 DL_API dl_status dl_serve_init_random(dl_serve* s, uint64_t seed, float sigma) {
   DL_SERVE_CALL(s->impl->init_random(seed, sigma));
 }

@@ -1,6 +1,7 @@
 // Server implementation (see serve.h).
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <stdexcept>
 #include <string>
@@ -185,6 +186,10 @@ Server::~Server() {
   if (stream_) cudaStreamSynchronize(stream_);
   if (step_exec_) cudaGraphExecDestroy(step_exec_);
   if (comm_) nccl().comm_destroy(comm_);
+  for (auto* p : peer_open_)
+    if (p) cudaIpcCloseMemHandle(p);
+  cudaFree(peer_mem_);
+  cudaFree(peer_epoch_);
   for (auto* m : attn_maps_) attention_prefill_tc_free(m);
   sampler_free(sampler_);
   for (auto& ev : ev_)
@@ -209,6 +214,53 @@ void Server::connect(const unsigned char* id128) {
   ncclUniqueId id;
   std::memcpy(&id, id128, sizeof(id));
   check_nccl(nccl().comm_init_rank(&comm_, tp_, id, rank_), "ncclCommInitRank");
+}
+
+void Server::ipc_handle(unsigned char* out64) {
+  if (tp_ == 1) throw std::logic_error("no tensor-parallel group");
+  if (tp_ > kPeerMaxRanks) throw std::invalid_argument("peer all-reduce supports up to 8 ranks");
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  if (!peer_mem_) {
+    const size_t bytes = peer_buffer_bytes(tp_, batch_ * D_);
+    check(cudaMalloc(&peer_mem_, bytes), "peer buffer");
+    check(cudaMemset(peer_mem_, 0, bytes), "peer buffer clear");
+    check(cudaMalloc(reinterpret_cast<void**>(&peer_epoch_), kPeerChunks * 4), "peer epochs");
+    check(cudaMemset(peer_epoch_, 0, kPeerChunks * 4), "peer epochs clear");
+  }
+  cudaIpcMemHandle_t h;
+  check(cudaIpcGetMemHandle(&h, peer_mem_), "ipc handle");
+  static_assert(sizeof(h) == 64, "CUDA IPC handle size");
+  std::memcpy(out64, &h, 64);
+}
+
+void Server::connect_peers(const unsigned char* handles) {
+  if (!peer_mem_) throw std::logic_error("ipc_handle first");
+  if (peers_) throw std::logic_error("peers already connected");
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  const size_t cap = batch_ * D_;
+  const size_t data_bytes = size_t(2) * tp_ * cap * 4;
+  pb_ = PeerBuffers{};
+  for (int r = 0; r < tp_; ++r) {
+    void* base = peer_mem_;
+    if (r != rank_) {
+      cudaIpcMemHandle_t h;
+      std::memcpy(&h, handles + size_t(r) * 64, 64);
+      check(cudaIpcOpenMemHandle(&peer_open_[r], h, cudaIpcMemLazyEnablePeerAccess), "ipc open");
+      base = peer_open_[r];
+    }
+    pb_.data[r] = static_cast<float*>(base);
+    pb_.flags[r] = reinterpret_cast<unsigned*>(static_cast<unsigned char*>(base) + data_bytes);
+  }
+  pb_.epoch = peer_epoch_;
+  pb_.err = err_;
+  pb_.ranks = tp_;
+  pb_.rank = rank_;
+  pb_.capacity = cap;
+  peers_ = true;
+  if (step_exec_) {  // the decode graph picks the peer path at capture
+    cudaGraphExecDestroy(step_exec_);
+    step_exec_ = nullptr;
+  }
 }
 
 // Slice of tensor `index` held by this rank.  q/k/v and gate/up: row ranges
@@ -367,6 +419,18 @@ void Server::row_projection_out(const bf16* x, int ldx, const bf16* w, int M, in
   if (tp_ == 1) {
     check(launch_gemm_splitk_epilogue(parts_, parts, M, N, kGemmResidual, residual_, N, nullptr, stream_),
           "splitk epilogue");
+    ++launches_;
+    return;
+  }
+  // Decode rows: one kernel sums the K parts, exchanges them over NVLink peer
+  // memory and adds the residual (NCCL when DOLITTLE_TP_ALLREDUCE=nccl, and
+  // for the prompt pass's large messages).
+  static const bool use_nccl = [] {
+    const char* v = std::getenv("DOLITTLE_TP_ALLREDUCE");
+    return v && std::string(v) == "nccl";
+  }();
+  if (decode && peers_ && !use_nccl && size_t(M) * N <= pb_.capacity) {
+    check(launch_peer_allreduce_residual(pb_, parts_, parts, residual_, size_t(M) * N, stream_), "peer all-reduce");
     ++launches_;
     return;
   }

@@ -37,6 +37,10 @@ class Server {
 
   static void nccl_id(unsigned char* out128);
   void connect(const unsigned char* id128);
+  // NVLink peer all-reduce of the decode step: this rank's buffer handle,
+  // then every rank's handles [tp][64] (CUDA IPC).
+  void ipc_handle(unsigned char* out64);
+  void connect_peers(const unsigned char* handles);
   void init_random(uint64_t seed, float sigma);
   // Full tensor `index` (engine order) from the host; this rank keeps its slice.
   void set_tensor(size_t index, const void* host, size_t bytes);
@@ -74,6 +78,12 @@ class Server {
   size_t D_, Ql_, Gl_, Fl_, V_, d_, L_;
   cudaStream_t stream_ = nullptr;
   ncclComm_t comm_ = nullptr;
+  // peer all-reduce: this rank's slots + flags, the peers' mapped copies
+  void* peer_mem_ = nullptr;
+  unsigned* peer_epoch_ = nullptr;
+  void* peer_open_[kPeerMaxRanks] = {};
+  PeerBuffers pb_ = {};
+  bool peers_ = false;
   // weights (local slices)
   void* weight_arena_ = nullptr;
   bf16 *embed_ = nullptr, *final_norm_ = nullptr, *lm_head_ = nullptr;

@@ -259,6 +259,90 @@ __global__ void add_fp32_residual_kernel(const float* __restrict__ sum, bf16* __
 
 unsigned grid_for(size_t n) { return unsigned(std::min<size_t>((n + 255) / 256, 148 * 32)); }
 
+__device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+constexpr long long kPeerSpin = 1ll << 31;  // ~1 s of SM cycles
+
+__global__ void __launch_bounds__(256) peer_allreduce_residual_kernel(PeerBuffers pb, const float* __restrict__ parts,
+                                                                      int splits, bf16* __restrict__ residual,
+                                                                      size_t n) {
+  __shared__ unsigned epoch_s;
+  __shared__ int ok_s;
+  const int i = blockIdx.x, R = pb.ranks;
+  // CTA i counts its own calls: every rank runs the same calls, so chunk i's
+  // epochs agree across ranks without any ordering between CTAs.
+  if (threadIdx.x == 0) epoch_s = pb.epoch[i] + 1;
+  __syncthreads();
+  const unsigned epoch = epoch_s, par = epoch & 1u;
+  const size_t per = ((n + kPeerChunks - 1) / kPeerChunks + 3) / 4 * 4;
+  const size_t c0 = min(n, size_t(i) * per), c1 = min(n, c0 + per);
+  // 1. This rank's chunk i (its split-K parts summed in part order, the
+  // split-K epilogue's law) into slot `rank` of every rank's buffer (16-byte
+  // stores; n and the chunk bounds are multiples of 4 floats).
+  const float4* src = reinterpret_cast<const float4*>(parts);
+  for (size_t j = c0 / 4 + threadIdx.x; j < c1 / 4; j += blockDim.x) {
+    float4 acc = src[j];
+    for (int s = 1; s < splits; ++s) {
+      const float4 v = src[size_t(s) * (n / 4) + j];
+      acc.x = __fadd_rn(acc.x, v.x);
+      acc.y = __fadd_rn(acc.y, v.y);
+      acc.z = __fadd_rn(acc.z, v.z);
+      acc.w = __fadd_rn(acc.w, v.w);
+    }
+    for (int p = 0; p < R; ++p)
+      reinterpret_cast<float4*>(pb.data[p] + (size_t(par) * R + pb.rank) * pb.capacity)[j] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int p = 0; p < R; ++p) st_release_sys(pb.flags[p] + (size_t(par) * R + pb.rank) * kPeerChunks + i, epoch);
+  }
+  // 2. Every rank's chunk i has arrived here (bounded wait).
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const unsigned* mine = pb.flags[pb.rank] + size_t(par) * R * kPeerChunks;
+    for (int src = 0; src < R && ok; ++src) {
+      const long long start = clock64();
+      while (ld_relaxed_sys(mine + src * kPeerChunks + i) != epoch) {
+        if (clock64() - start > kPeerSpin) {
+          ok = 0;
+          atomicOr(pb.err, kErrWaitFull);
+          break;
+        }
+      }
+    }
+    asm volatile("fence.acq_rel.sys;" ::: "memory");  // the acquire of the flags seen
+    ok_s = ok;
+  }
+  __syncthreads();
+  // 3. Sum in rank order, residual add (the residual epilogue law).
+  if (ok_s) {
+    const float* slots = pb.data[pb.rank] + size_t(par) * R * pb.capacity;
+    for (size_t j = c0 / 4 + threadIdx.x; j < c1 / 4; j += blockDim.x) {
+      float4 sum = __ldcv(reinterpret_cast<const float4*>(slots) + j);
+      for (int src = 1; src < R; ++src) {
+        const float4 v = __ldcv(reinterpret_cast<const float4*>(slots + size_t(src) * pb.capacity) + j);
+        sum.x = __fadd_rn(sum.x, v.x);
+        sum.y = __fadd_rn(sum.y, v.y);
+        sum.z = __fadd_rn(sum.z, v.z);
+        sum.w = __fadd_rn(sum.w, v.w);
+      }
+      __nv_bfloat162* r2 = reinterpret_cast<__nv_bfloat162*>(residual) + 2 * j;
+      const float2 a = __bfloat1622float2(r2[0]), b = __bfloat1622float2(r2[1]);
+      r2[0] = __floats2bfloat162_rn(__fadd_rn(a.x, round_bf16(sum.x)), __fadd_rn(a.y, round_bf16(sum.y)));
+      r2[1] = __floats2bfloat162_rn(__fadd_rn(b.x, round_bf16(sum.z)), __fadd_rn(b.y, round_bf16(sum.w)));
+    }
+  }
+  if (threadIdx.x == 0) pb.epoch[i] = epoch;
+}
+
 }  // namespace
 
 cudaError_t launch_fill_normal_slice(bf16* out, size_t rows, size_t cols, size_t out_stride, size_t full_cols,
@@ -306,6 +390,18 @@ cudaError_t launch_attention_decode_batched(const bf16* q, KvPlanes planes, cons
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   attention_decode_combine_kernel<<<dim3(query_heads, batch), 128, 0, stream>>>(ws, query_heads, splits, out);
+  return cudaGetLastError();
+}
+
+size_t peer_buffer_bytes(int ranks, size_t capacity) {
+  return size_t(2) * ranks * capacity * 4 + size_t(2) * ranks * kPeerChunks * 4;
+}
+
+cudaError_t launch_peer_allreduce_residual(const PeerBuffers& pb, const float* parts, int splits, bf16* residual,
+                                           size_t n, cudaStream_t stream) {
+  if (n > pb.capacity || n % 4 || splits < 1 || pb.ranks < 1 || pb.ranks > kPeerMaxRanks)
+    return cudaErrorInvalidValue;
+  peer_allreduce_residual_kernel<<<kPeerChunks, 256, 0, stream>>>(pb, parts, splits, residual, n);
   return cudaGetLastError();
 }
 

@@ -45,4 +45,27 @@ cudaError_t launch_attention_decode_batched(const bf16* q, KvPlanes planes, cons
 // applied to an FP32 sum (after the tensor-parallel all-reduce).
 cudaError_t launch_add_fp32_residual(const float* sum, bf16* residual, size_t n, cudaStream_t stream);
 
+// Tensor-parallel all-reduce of the row-parallel projections over NVLink peer
+// memory, fused with the split-K sum and the residual add: every rank sums
+// its split-K parts [splits][n] in part order and writes the FP32 partial sum
+// [n] (chunk i per CTA) into slot `rank` of every rank's buffer (peer
+// pointers from CUDA IPC), raises flag (rank, i) on each with the call's
+// epoch, waits (bounded) for every rank's flag i on its own buffer, then adds
+// the slots in rank order (the same sum on every rank) and applies
+// residual = round(residual + round(sum)).  Buffers alternate by epoch parity
+// so a rank running one call ahead never overwrites a slot still being read.
+constexpr int kPeerMaxRanks = 8;
+constexpr int kPeerChunks = 128;  // CTAs per call
+struct PeerBuffers {
+  float* data[kPeerMaxRanks];       // [2][ranks][capacity] FP32 on each rank
+  unsigned* flags[kPeerMaxRanks];   // [2][ranks][kPeerChunks] on each rank
+  unsigned* epoch;                  // this rank: calls so far, per CTA [kPeerChunks]
+  unsigned* err;
+  int ranks, rank;
+  size_t capacity;                  // floats per slot
+};
+size_t peer_buffer_bytes(int ranks, size_t capacity);  // data + flags, one rank
+cudaError_t launch_peer_allreduce_residual(const PeerBuffers& pb, const float* parts, int splits, bf16* residual,
+                                           size_t n, cudaStream_t stream);
+
 }  // namespace dl

@@ -61,6 +61,15 @@ class Server:
         buf = (C.c_ubyte * 128).from_buffer_copy(nccl_id)
         check(lib().dl_serve_connect(self._h, buf))
 
+    def ipc_handle(self) -> bytes:
+        buf = (C.c_ubyte * 64)()
+        check(lib().dl_serve_ipc_handle(self._h, buf))
+        return bytes(buf)
+
+    def connect_peers(self, handles: bytes) -> None:
+        buf = (C.c_ubyte * len(handles)).from_buffer_copy(handles)
+        check(lib().dl_serve_connect_peers(self._h, buf))
+
     def init_random(self, seed: int, sigma: float = 0.02) -> None:
         check(lib().dl_serve_init_random(self._h, seed, sigma))
 
@@ -140,11 +149,16 @@ def tp_slices(config: Qwen3Config, rank: int, size: int) -> list:
     return out
 
 
-def connect_group(server, dist, make_id=Server.nccl_id) -> bytes:
-    """NCCL communicator of a tensor-parallel group: rank 0's id reaches every
-    rank over the torch.distributed process group (any backend), and every
-    rank connects with it."""
+def connect_group(server, dist, make_id=Server.nccl_id, peers: bool = True) -> bytes:
+    """Connect a tensor-parallel group over the torch.distributed process
+    group (any backend): rank 0's NCCL id reaches every rank and every rank
+    connects with it; then (peers) the ranks swap CUDA IPC handles of their
+    peer all-reduce buffers, in rank order."""
     obj = [make_id() if dist.get_rank() == 0 else None]
     dist.broadcast_object_list(obj, src=0)
     server.connect(obj[0])
+    if peers:
+        handles = [None] * dist.get_world_size()
+        dist.all_gather_object(handles, server.ipc_handle())
+        server.connect_peers(b"".join(handles))
     return obj[0]

@@ -324,6 +324,12 @@ DL_API void dl_serve_destroy(dl_serve* s);
  * same id to dl_serve_connect (all ranks concurrently). */
 DL_API dl_status dl_serve_nccl_id(unsigned char* id128);
 DL_API dl_status dl_serve_connect(dl_serve* s, const unsigned char* id128);
+/* Fused NVLink all-reduce of the decode step (peer memory instead of NCCL
+ * for o_proj / down_proj): each rank publishes a 64-byte CUDA IPC handle of
+ * its buffer, then every rank passes all handles [tp_size][64] in rank order
+ * (after dl_serve_connect; ranks must be separate processes). */
+DL_API dl_status dl_serve_ipc_handle(dl_serve* s, unsigned char* handle64);
+DL_API dl_status dl_serve_connect_peers(dl_serve* s, const unsigned char* handles);
 /* Seeded weights as dl_engine_init_random; each rank generates only its
  * slice of the same tensors. */
 DL_API dl_status dl_serve_init_random(dl_serve* s, uint64_t seed, float sigma);

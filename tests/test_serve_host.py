@@ -50,11 +50,19 @@ def test_slices_follow_kv_head_groups():
 
 
 class _FakeServer:
-    def __init__(self):
+    def __init__(self, rank):
         self.got = None
+        self.rank = rank
+        self.peers = None
 
     def connect(self, nccl_id):
         self.got = nccl_id
+
+    def ipc_handle(self):
+        return bytes([self.rank]) * 64
+
+    def connect_peers(self, handles):
+        self.peers = handles
 
 
 def _rank_main(rank, world, port):
@@ -62,10 +70,11 @@ def _rank_main(rank, world, port):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        srv = _FakeServer()
+        srv = _FakeServer(rank)
         made = []
         got = serve.connect_group(srv, dist, make_id=lambda: made.append(1) or bytes(range(128)))
         assert srv.got == got == bytes(range(128))
+        assert srv.peers == b"".join(bytes([r]) * 64 for r in range(world))  # every rank's handle, rank order
         assert made == ([1] if rank == 0 else [])  # only rank 0 makes the id
         dist.barrier()
     finally:
