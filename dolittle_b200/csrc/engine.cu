@@ -141,8 +141,9 @@ Engine::Engine(const dl_model_config& cfg, int device, size_t capacity, size_t m
                o_inv = stake(d * 2), o_dir = stake(D * 4), o_edit = stake(64),
                o_cap = stake(capacity * D * 2), o_xn = stake(R * D * 2),
                o_vt = stake(size_t(cfg.kv_heads) * d * align_up(capacity, 64) * 2),
-               o_split = stake(2 * std::min<size_t>(R, 1024) * std::max<size_t>(D, Q + 2 * G) * 4),
-               o_tickets = stake(1024 * 4), o_inject = stake(2 * D * 2), o_inject_misc = stake(64);
+               o_split = stake(gemm_split_floats(int(std::min<size_t>(R, 1024)), int(std::max<size_t>(D, Q + 2 * G)),
+                                                 kGemmMaxSplit) * 4),
+               o_tickets = stake(size_t(kGemmTickets) * 4), o_inject = stake(2 * D * 2), o_inject_misc = stake(64);
   check(cudaMalloc(&scratch_, s), "scratch");
   check(cudaMemsetAsync(scratch_, 0, s, stream_), "scratch clear");
   auto* sb = static_cast<unsigned char*>(scratch_);
@@ -165,7 +166,8 @@ Engine::Engine(const dl_model_config& cfg, int device, size_t capacity, size_t m
   xn_ = reinterpret_cast<bf16*>(sb + o_xn);
   vt_ = reinterpret_cast<bf16*>(sb + o_vt);
   gemm_partial_ = reinterpret_cast<float*>(sb + o_split);
-  gemm_partial_rows_ = int(std::min<size_t>(R, 1024));
+  gemm_partial_floats_ =
+      gemm_split_floats(int(std::min<size_t>(R, 1024)), int(std::max<size_t>(D, Q + 2 * G)), kGemmMaxSplit);
   gemm_tickets_ = reinterpret_cast<unsigned*>(sb + o_tickets);
   inject_row_ = reinterpret_cast<bf16*>(sb + o_inject);
   inject_norm_ = reinterpret_cast<float*>(sb + o_inject_misc);
@@ -424,10 +426,6 @@ bool Engine::fast_prefill_supported() const {
 // rows appended to the cache by the epilogue), o (+residual), gate|up
 // (+SwiGLU) and down (+residual); QK-norm/RoPE and causal attention use the
 // same kernels as the parity path.  `first` is the absolute position of row 0.
-namespace {
-// Tiles of a 128 x 256 tiling (the split-K ticket count).
-long long mt_tickets(int rows, int N) { return (long long)((rows + 127) / 128) * (N / 256); }
-}  // namespace
 
 void Engine::run_layers_fast(int rows, long long first) {
   const int D = int(cfg_.hidden), Q = int(cfg_.query_heads * cfg_.head_width),
@@ -454,13 +452,11 @@ void Engine::run_layers_fast(int rows, long long first) {
     }
     p.wide_tiles = true;
     p.err = &state_->err;
-    // Split-K only for shapes no wider than the workspace (not gate|up).
-    if (N <= int(std::max(cfg_.hidden, cfg_.query_heads * cfg_.head_width + 2 * cfg_.kv_heads * cfg_.head_width)) &&
-        rows <= gemm_partial_rows_ && size_t(mt_tickets(rows, N)) <= 1024) {
-      p.partial = gemm_partial_;
-      p.partial_rows = gemm_partial_rows_;
-      p.tickets = gemm_tickets_;
-    }
+    // Split-K where the parts fit the workspace (the launcher checks).
+    p.partial = gemm_partial_;
+    p.partial_floats = gemm_partial_floats_;
+    p.tickets = gemm_tickets_;
+    p.n_tickets = kGemmTickets;
     check(launch_gemm_tcgen05(p, stream_, false), "gemm");
     ++launches_;
   };

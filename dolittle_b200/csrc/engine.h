@@ -165,7 +165,8 @@ class Engine {
   bf16* vt_ = nullptr;
   int vt_stride_ = 0;
   float* gemm_partial_ = nullptr;  // split-K partials of the prompt-pass GEMMs
-  int gemm_partial_rows_ = 0;
+  size_t gemm_partial_floats_ = 0;
+  static constexpr int kGemmTickets = 4096;
   unsigned* gemm_tickets_ = nullptr;
   // verbalizer injection (marker row) and reconstruction head
   long long inject_position_ = -1;

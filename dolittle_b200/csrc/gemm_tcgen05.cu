@@ -32,6 +32,15 @@ using namespace tc;
 constexpr int kBM = 128;
 constexpr int kBK = 64;   // one 128-byte swizzle atom of BF16
 constexpr int kThreads = 192;  // producer warp, MMA warp, 4 epilogue warps
+// Tile choice, in units of one 256-wide k-step (~0.5 us on a B200): a
+// 128-wide k-step takes nearly as long (the narrow MMA is bound by shared
+// memory reads), and split-K costs a fixed ~8 us plus its FP32 partials'
+// traffic at ~3 TB/s.  Fitted to a sweep of M = 512 / 2048 x the Qwen3-8B
+// projections (qkv, o, gate|up, down) over tile widths 128 / 256 and 1-4
+// parts: the estimate ranks the measured times in the same order.
+constexpr double kStep128 = 0.95;
+constexpr double kSplitFixed = 16.0;
+constexpr double kSplitPerByte = 1.0 / 1.5e6;
 
 struct alignas(64) GemmArgs {
   CUtensorMap map_a;
@@ -46,7 +55,7 @@ struct alignas(64) GemmArgs {
   unsigned* err;
   int split;           // K parts per tile
   float* partial;      // [split][M][N] FP32
-  unsigned* tickets;   // per tile (split 2 with the epilogue in the kernel)
+  unsigned* tickets;   // per tile (split >= 2 with the epilogue in the kernel)
   int partial_only;    // every part stores its FP32 partial; no epilogue
 };
 
@@ -66,8 +75,16 @@ __device__ __forceinline__ float swiglu_law(float a, float b) {
 
 // Epilogue of one accumulator row chunk: 32 FP32 columns of output row `row`
 // starting at column `col` (of the output segment).
+// The residual epilogue's 32 old values of the chunk (four 16-byte words),
+// loaded one chunk ahead so the round trip overlaps the previous chunk.
+__device__ __forceinline__ void load_residual(const bf16* out, int ld, int row, int col, uint4 (&old)[4]) {
+  const uint4* src = reinterpret_cast<const uint4*>(out + size_t(row) * ld + col);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) old[q] = src[q];
+}
+
 __device__ __forceinline__ void store_chunk(const GemmArgs& a, bf16* out, int ld, int row, int col,
-                                            const uint32_t (&r)[32]) {
+                                            const uint32_t (&r)[32], const uint4 (&res)[4]) {
   if (a.epilogue == kGemmSwiGLU) {
     // Columns (2o, 2o+1) = (gate o, up o).
     uint32_t packed[8];
@@ -87,10 +104,9 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, bf16* out, int ld
   uint32_t packed[16];
   bf16* dst = out + size_t(row) * ld + col;
   if (a.epilogue == kGemmResidual) {
-    const uint4* src = reinterpret_cast<const uint4*>(dst);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const uint4 old = src[q];
+      const uint4 old = res[q];
       const uint32_t ow[4] = {old.x, old.y, old.z, old.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -273,49 +289,76 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
           }
         }
       } else if (a.split == 1) {
+        const bool resid = a.epilogue == kGemmResidual && row < a.M;
+        uint4 res[4] = {};
+        if (resid) load_residual(out, ld, row, c0, res);
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
           tmem_ld32(acc + uint32_t(c * 32), r);
-          if (row < a.M) store_chunk(a, out, ld, row, c0 + c * 32, r);
+          uint4 next[4] = {};
+          if (resid && c + 1 < BN / 32) load_residual(out, ld, row, c0 + (c + 1) * 32, next);
+          if (row < a.M) store_chunk(a, out, ld, row, c0 + c * 32, r, res);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) res[q] = next[q];
         }
       } else {
-        // Both K halves publish their FP32 partial; the second to finish
-        // adds the other half (FP32 addition commutes, so the result does
-        // not depend on which half finishes last) and stores.
-        float* mine = a.partial + (size_t(half) * a.M + row) * a.N + n0;
-        const float* other = a.partial + (size_t(1 - half) * a.M + row) * a.N + n0;
+        // Every K part publishes its FP32 partial; the last part to finish
+        // adds all parts in part order (p0 + p1 + ... whichever finished
+        // last, so the result is deterministic) and applies the epilogue.
+        // Partial block of (part, tile): [BN columns][128 rows], so each warp
+        // store covers one 128-byte line (lanes = consecutive rows).
+        const size_t blk = size_t(BN) * kBM;
+        float* mine = a.partial + (size_t(half) * tiles + tile) * blk + q * 32 + lane;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
           tmem_ld32(acc + uint32_t(c * 32), r);
-          if (row < a.M) {
-            uint4* d = reinterpret_cast<uint4*>(mine + c * 32);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) d[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
-          }
+          for (int i = 0; i < 32; ++i) mine[size_t(c * 32 + i) * kBM] = __uint_as_float(r[i]);
         }
         __threadfence();
         named_sync(1, 128);
-        if (threadIdx.x == 64) last_half = atomicAdd(&a.tickets[tile], 1u) == 1u;
+        if (threadIdx.x == 64) last_half = atomicAdd(&a.tickets[tile], 1u) == unsigned(a.split - 1);
         named_sync(1, 128);
         if (last_half) {
           __threadfence();
+          const float* first = a.partial + size_t(tile) * blk + q * 32 + lane;
+          const size_t part_stride = size_t(tiles) * blk;
+          const bool resid = a.epilogue == kGemmResidual && row < a.M;
 #pragma unroll 1
           for (int c = 0; c < BN / 32; ++c) {
+            // One round trip per chunk: the other parts' values and the
+            // residual words are all loaded before the sums.
+            float pv[kGemmMaxSplit][32];
+#pragma unroll
+            for (int h = 0; h < kGemmMaxSplit; ++h)
+              if (h < a.split && h != half) {
+                const float* ph = first + size_t(h) * part_stride + size_t(c * 32) * kBM;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) pv[h][i] = __ldcg(ph + size_t(i) * kBM);
+              }
+            uint4 res[4] = {};
+            if (resid) load_residual(out, ld, row, c0 + c * 32, res);
             uint32_t r[32];
             tmem_ld32(acc + uint32_t(c * 32), r);
-            if (row < a.M) {
-              const uint4* o4 = reinterpret_cast<const uint4*>(other + c * 32);
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const uint4 v = __ldcg(o4 + i);
-                r[4 * i] = __float_as_uint(__uint_as_float(r[4 * i]) + __uint_as_float(v.x));
-                r[4 * i + 1] = __float_as_uint(__uint_as_float(r[4 * i + 1]) + __uint_as_float(v.y));
-                r[4 * i + 2] = __float_as_uint(__uint_as_float(r[4 * i + 2]) + __uint_as_float(v.z));
-                r[4 * i + 3] = __float_as_uint(__uint_as_float(r[4 * i + 3]) + __uint_as_float(v.w));
+            for (int h = 0; h < kGemmMaxSplit; ++h)
+              if (h == half) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) pv[h][i] = __uint_as_float(r[i]);
               }
-              store_chunk(a, out, ld, row, c0 + c * 32, r);
+            // Sum in part order.
+#pragma unroll
+            for (int h = 1; h < kGemmMaxSplit; ++h)
+              if (h < a.split) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) pv[0][i] = __fadd_rn(pv[0][i], pv[h][i]);
+              }
+            if (row < a.M) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(pv[0][i]);
+              store_chunk(a, out, ld, row, c0 + c * 32, r, res);
             }
           }
           if (threadIdx.x == 64) a.tickets[tile] = 0;
@@ -363,6 +406,8 @@ bool encode_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
 }  // namespace
 
 bool gemm_tcgen05_supported(int M, int N, int K) { return M > 0 && K % kBK == 0 && N % 128 == 0; }
+
+size_t gemm_split_floats(int M, int N, int parts) { return size_t(parts) * size_t((M + kBM - 1) / kBM) * kBM * N; }
 
 namespace {
 
@@ -476,22 +521,40 @@ cudaError_t launch_gemm_splitk_epilogue(const float* parts, int splits, int M, i
 cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool pdl) {
   if (!gemm_tcgen05_supported(p.M, p.N, p.K) || p.nseg < 1 || p.nseg > 3) return cudaErrorInvalidValue;
   GemmArgs a = {};
-  // Tile width by waves over the SMs: a 256-wide tile costs about two
-  // 128-wide ones, so 256 only when it needs no more than half the waves.
+  // Tile width and K parts by estimated time: waves over the SMs x k-steps
+  // per unit x the cost of one k-step, plus the partial sums' traffic.  A
+  // 128-wide k-step moves 2/3 of a 256-wide one's bytes for half the MMA work.
   int sms = 148, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const long long mt = (p.M + kBM - 1) / kBM;
-  const long long waves256 = (mt * (p.N / 256) + sms - 1) / sms, waves128 = (mt * (p.N / 128) + sms - 1) / sms;
+  const int kt = p.K / kBK;
   bool aligned256 = p.N % 256 == 0;
   for (int i = 0; i < p.nseg; ++i) aligned256 = aligned256 && p.seg_n0[i] % 256 == 0;
-  int BN = (aligned256 && p.wide_tiles && 2 * waves256 <= waves128) ? 256 : 128;
-  // Split K in two when even 128-wide tiles would leave half the SMs idle.
-  int split = 1;
-  if (p.partial && p.tickets && p.M <= p.partial_rows && (p.K / kBK) % 2 == 0 && aligned256 && p.wide_tiles &&
-      2 * mt * (p.N / 256) <= sms) {
-    BN = 256;
-    split = 2;
+  const bool workspace = p.partial && p.tickets;
+  int BN = 0, split = 0;
+  double best = 1e30;
+  for (int bn : {256, 128}) {
+    if (bn == 256 && !(aligned256 && p.wide_tiles)) continue;
+    if (p.force_bn && bn != p.force_bn) continue;
+    const long long tiles = mt * (p.N / bn);
+    for (int sp = 1; sp <= kGemmMaxSplit; ++sp) {
+      if (p.force_split && sp != p.force_split) continue;
+      if (sp > 1 && (!workspace || kt / sp < 4 || gemm_split_floats(p.M, p.N, sp) > p.partial_floats ||
+                     tiles > p.n_tickets))
+        continue;
+      const long long waves = (tiles * sp + sms - 1) / sms;
+      const double step = bn == 256 ? 1.0 : kStep128;
+      const double split_cost =
+          sp > 1 ? kSplitFixed + kSplitPerByte * 4.0 * double(gemm_split_floats(p.M, p.N, sp)) : 0.0;
+      const double cost = double(waves) * double((kt + sp - 1) / sp) * step + split_cost;
+      if (cost < best * 0.98) {
+        best = cost;
+        BN = bn;
+        split = sp;
+      }
+    }
   }
+  if (!BN) return cudaErrorInvalidValue;
   for (int i = 0; i < p.nseg; ++i)
     if (p.seg_n0[i] % BN) return cudaErrorInvalidValue;  // tiles never straddle outputs
   if (!encode_2d(&a.map_a, p.x, uint64_t(p.M), uint64_t(p.K), uint64_t(p.ldx), kBM)) return cudaErrorInvalidValue;
@@ -508,7 +571,7 @@ cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool 
   }
   a.err = p.err;
   const int stage_bytes = (kBM + BN) * kBK * 2;
-  a.stages = std::min(8, (200 * 1024) / stage_bytes);
+  a.stages = std::min(8, (225 * 1024) / stage_bytes);
   const size_t smem = size_t(a.stages) * stage_bytes + 1024;
   cudaLaunchConfig_t cfg = {};
   a.split = split;

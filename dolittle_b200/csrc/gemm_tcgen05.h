@@ -23,16 +23,25 @@ struct GemmProblem {
   int seg_ld[3];      // output row stride (elements)
   bool wide_tiles;    // allow 128 x 256 tiles
   unsigned* err;
-  // Optional split-K workspace (both or neither): FP32 partials
-  // [2][partial_rows][N] and per-tile tickets (zeroed, left zeroed).  With
-  // them, shapes that would leave most SMs idle run as two K halves whose
-  // second finisher adds the halves and applies the epilogue.
+  // Optional split-K workspace (both or neither): room for FP32 partials
+  // (partial_floats >= gemm_split_floats(M, N, parts)) and n_tickets per-tile tickets (zeroed,
+  // left zeroed).  With them, shapes that would leave SMs idle run as up to
+  // kGemmMaxSplit K parts whose last finisher adds the parts in part order
+  // and applies the epilogue.
   float* partial;
-  int partial_rows;
+  size_t partial_floats;
   unsigned* tickets;
+  int n_tickets;
+  // Tuning overrides (0 = chosen by the launcher): tile width 128 / 256 and
+  // the number of K parts.
+  int force_bn, force_split;
 };
 
+constexpr int kGemmMaxSplit = 4;
+
 bool gemm_tcgen05_supported(int M, int N, int K);
+// FP32 workspace of `parts` K parts: one [128 rows x N] plane per part.
+size_t gemm_split_floats(int M, int N, int parts);
 cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool pdl);
 
 // Split-K for few rows (batched decode): the K extent in `splits` parts

@@ -154,13 +154,21 @@ DL_API dl_status dl_qk_norm_rope_append(const void* q_raw, const void* k_raw,
  * N % 128 == 0, 16-byte aligned rows. */
 DL_API dl_status dl_gemm_bf16(const void* x, size_t ldx, const void* w, void* y, size_t ldy, size_t M,
                               size_t N, size_t K, int epilogue, void* stream);
-/* dl_gemm_bf16 that may split K in two when the tile count leaves most SMs
- * idle: workspace of dl_gemm_bf16_split_workspace_bytes(M, N) bytes (FP32
- * partials) and n_tickets >= ceil(M/128) * (N/256) zeroed words (left zeroed). */
+/* dl_gemm_bf16 that may split K into up to 4 parts when the tile count
+ * leaves SMs idle (the last part to finish adds the parts in part order):
+ * workspace of dl_gemm_bf16_split_workspace_bytes(M, N) bytes (FP32
+ * partials) and n_tickets >= ceil(M/128) * (N/128) zeroed words (left
+ * zeroed).  Repeated calls give bit-identical results. */
 DL_API size_t dl_gemm_bf16_split_workspace_bytes(size_t M, size_t N);
 DL_API dl_status dl_gemm_bf16_split(const void* x, size_t ldx, const void* w, void* y, size_t ldy, size_t M,
                                     size_t N, size_t K, int epilogue, void* stream, void* workspace,
                                     unsigned* tickets, size_t n_tickets);
+/* dl_gemm_bf16_split with the tiling chosen by the caller: tile_n 128 or 256
+ * output columns per tile and `parts` K parts (1..4; 0 = chosen by the
+ * library for either).  workspace / tickets may be NULL when parts <= 1. */
+DL_API dl_status dl_gemm_bf16_config(const void* x, size_t ldx, const void* w, void* y, size_t ldy, size_t M,
+                                     size_t N, size_t K, int epilogue, void* stream, void* workspace,
+                                     unsigned* tickets, size_t n_tickets, int tile_n, int parts);
 /* residual = round(residual + round(X W^T)) in place. */
 DL_API dl_status dl_projection_residual(const void* input, const void* weight, void* residual,
                                         size_t rows, size_t input_width, size_t output_width,

@@ -71,30 +71,42 @@ def test_gemm_residual_and_swiglu_epilogues():
     assert r2["passed"], r2
 
 
-@pytest.mark.parametrize("M,N,K,epi", [(512, 4096, 4096, 0), (512, 4096, 12288, 1), (200, 6144, 4096, 0)])
-def test_gemm_split_k_matches_fp32_reference_and_unsplit(M, N, K, epi):
-    """Split-K (two K halves summed in FP32 by the second finisher) against
-    the FP32 reference and against the unsplit kernel: same tolerance, and
-    repeated runs are bit-identical (the order of the halves is fixed)."""
+@pytest.mark.parametrize("M,N,K,epi,tile_n,parts", [(512, 4096, 4096, 0, 0, 0), (512, 4096, 12288, 1, 0, 0),
+                                                    (200, 6144, 4096, 0, 0, 0), (512, 4096, 4096, 1, 256, 3),
+                                                    (300, 4096, 4096, 0, 128, 4), (512, 4096, 12288, 1, 128, 2),
+                                                    (129, 2048, 1024, 0, 256, 4), (512, 2048, 4096, 3, 128, 3)])
+def test_gemm_split_k_matches_fp32_reference_and_unsplit(M, N, K, epi, tile_n, parts):
+    """Split-K (up to 4 K parts summed in FP32 in part order by the last
+    finisher; tile width and parts chosen by the library or pinned) against
+    the FP32 reference: same tolerance as the unsplit kernel, and repeated
+    runs are bit-identical (the order of the parts is fixed)."""
     torch = _torch()
     x, w = _case(M, N, K, seed=M + K + epi)
+    ncols = N // 2 if epi == 3 else N
     res = torch.randn(M, N, device="cuda").to(torch.bfloat16) if epi == 1 else None
     L = dl.lib()
     ws = torch.empty(L.dl_gemm_bf16_split_workspace_bytes(M, N), device="cuda", dtype=torch.uint8)
-    n_t = ((M + 127) // 128) * (N // 256)
+    n_t = ((M + 127) // 128) * (N // 128)
     tickets = torch.zeros(n_t, device="cuda", dtype=torch.int32)
     outs = []
     for _ in range(2):
-        y = res.clone() if epi == 1 else torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-        assert L.dl_gemm_bf16_split(x.data_ptr(), K, w.data_ptr(), y.data_ptr(), N, M, N, K, epi, None,
-                                    ws.data_ptr(), tickets.data_ptr(), n_t) == 0, L.dl_last_error()
+        y = res.clone() if epi == 1 else torch.empty(M, ncols, device="cuda", dtype=torch.bfloat16)
+        assert L.dl_gemm_bf16_config(x.data_ptr(), K, w.data_ptr(), y.data_ptr(), ncols, M, N, K, epi, None,
+                                     ws.data_ptr(), tickets.data_ptr(), n_t, tile_n, parts) == 0, L.dl_last_error()
         torch.cuda.synchronize()
         outs.append(y)
     assert torch.equal(outs[0], outs[1])
     assert int(tickets.abs().sum()) == 0
     proj = x.float() @ w.float().T
-    ref = (res.float() + proj.to(torch.bfloat16).float()).to(torch.bfloat16).float() if epi == 1 else proj
     got = outs[0].float()
+    if epi == 3:
+        yy = proj.to(torch.bfloat16).float()
+        g, u = yy[:, 0::2], yy[:, 1::2]
+        ref = ((g * torch.sigmoid(g)).to(torch.bfloat16).float() * u).to(torch.bfloat16).float()
+        r = nm.compare_elementwise(ref.cpu().numpy(), got.cpu().numpy(), 1e-2, 3e-2)
+        assert r["passed"], r
+        return
+    ref = (res.float() + proj.to(torch.bfloat16).float()).to(torch.bfloat16).float() if epi == 1 else proj
     if epi == 1:
         # Residual epilogue: round(res + round(acc)) rounds twice, so a
         # different (tensor-core) accumulation can move round(acc) by one
