@@ -118,6 +118,10 @@ __global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const
   fence_after_sync();
   const uint32_t tmem = tmem_base;
   auto t_s = [&](int st) { return tmem + uint32_t(st * 128); };
+  // Programmatic dependent launch: the prologue above overlaps the previous
+  // kernel; nothing it wrote is read before this point.
+  allow_next();
+  wait_prior();
   const uint32_t t_o = tmem + 256;
   const uint32_t lane_base = uint32_t(warp * 32) << 16;
 
@@ -257,6 +261,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const
 __global__ void vt_transpose_kernel(const bf16* __restrict__ v, bf16* __restrict__ vt, int keys, int kv_heads,
                                     int width, int vt_stride) {
   __shared__ bf16 tile[32][33];
+  allow_next();
+  wait_prior();
   const int g = blockIdx.z;
   const int j0 = blockIdx.x * 32, f0 = blockIdx.y * 32;
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
@@ -328,17 +334,33 @@ AttnTcMaps* attention_prefill_tc_maps(const bf16* q, int max_rows, int query_hea
 
 void attention_prefill_tc_free(AttnTcMaps* m) { delete m; }
 
+namespace {
+cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t stream, cudaLaunchAttribute* attr,
+                              bool pdl) {
+  cudaLaunchConfig_t c = {};
+  c.gridDim = grid;
+  c.blockDim = block;
+  c.dynamicSmemBytes = smem;
+  c.stream = stream;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  c.attrs = attr;
+  c.numAttrs = pdl ? 1 : 0;
+  return c;
+}
+}  // namespace
+
 cudaError_t launch_vt_transpose(const bf16* v_cache, bf16* vt, int keys, int kv_heads, int width, int vt_stride,
-                                cudaStream_t stream) {
+                                cudaStream_t stream, bool pdl) {
   if (keys <= 0) return cudaSuccess;
-  dim3 grid((keys + 31) / 32, (width + 31) / 32, kv_heads);
-  vt_transpose_kernel<<<grid, dim3(32, 8), 0, stream>>>(v_cache, vt, keys, kv_heads, width, vt_stride);
-  return cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  auto cfg = pdl_config(dim3((keys + 31) / 32, (width + 31) / 32, kv_heads), dim3(32, 8), 0, stream, attr, pdl);
+  return cudaLaunchKernelEx(&cfg, vt_transpose_kernel, v_cache, vt, keys, kv_heads, width, vt_stride);
 }
 
 cudaError_t launch_attention_prefill_tc(const AttnTcMaps* maps, bf16* out, int rows, long long first, int layer,
                                         int query_heads, int kv_heads, float scale, unsigned* err,
-                                        cudaStream_t stream) {
+                                        cudaStream_t stream, bool pdl) {
   if (!maps || rows <= 0) return cudaErrorInvalidValue;
   AttnArgs a = {};
   a.map_q = maps->q;
@@ -356,8 +378,9 @@ cudaError_t launch_attention_prefill_tc(const AttnTcMaps* maps, bf16* out, int r
   std::call_once(once, [] {
     cudaFuncSetAttribute(attention_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   });
-  attention_prefill_tc_kernel<<<dim3((rows + kTile - 1) / kTile, query_heads), kThreads, kSmem, stream>>>(a);
-  return cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  auto cfg = pdl_config(dim3((rows + kTile - 1) / kTile, query_heads), dim3(kThreads), kSmem, stream, attr, pdl);
+  return cudaLaunchKernelEx(&cfg, attention_prefill_tc_kernel, a);
 }
 
 }  // namespace dl

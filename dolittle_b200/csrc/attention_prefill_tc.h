@@ -16,12 +16,14 @@ AttnTcMaps* attention_prefill_tc_maps(const bf16* q, int max_rows, int query_hea
                                       size_t kv_block_bytes, int capacity, int layers, int kv_heads, int width,
                                       const bf16* vt, int vt_stride);
 void attention_prefill_tc_free(AttnTcMaps* maps);
+// pdl: programmatic dependent launch (both kernels wait for the previous
+// kernel's completion before reading its results).
 cudaError_t launch_vt_transpose(const bf16* v_cache, bf16* vt, int keys, int kv_heads, int width, int vt_stride,
-                                cudaStream_t stream);
+                                cudaStream_t stream, bool pdl = false);
 // out[rows][Hq * d] for query rows at absolute positions first .. first+rows-1
 // of block `layer`; keys 0 .. first+rows-1 (the cache already holds them).
 cudaError_t launch_attention_prefill_tc(const AttnTcMaps* maps, bf16* out, int rows, long long first, int layer,
                                         int query_heads, int kv_heads, float scale, unsigned* err,
-                                        cudaStream_t stream);
+                                        cudaStream_t stream, bool pdl = false);
 
 }  // namespace dl

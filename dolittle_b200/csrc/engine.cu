@@ -426,6 +426,9 @@ bool Engine::fast_prefill_supported() const {
 // rows appended to the cache by the epilogue), o (+residual), gate|up
 // (+SwiGLU) and down (+residual); QK-norm/RoPE and causal attention use the
 // same kernels as the parity path.  `first` is the absolute position of row 0.
+// Every kernel of the chain is a programmatic dependent launch: each waits
+// (griddepcontrol.wait) for its predecessor before reading, so its launch and
+// prologue overlap the predecessor's tail.
 
 void Engine::run_layers_fast(int rows, long long first) {
   const int D = int(cfg_.hidden), Q = int(cfg_.query_heads * cfg_.head_width),
@@ -457,12 +460,12 @@ void Engine::run_layers_fast(int rows, long long first) {
     p.partial_floats = gemm_partial_floats_;
     p.tickets = gemm_tickets_;
     p.n_tickets = kGemmTickets;
-    check(launch_gemm_tcgen05(p, stream_, false), "gemm");
+    check(launch_gemm_tcgen05(p, stream_, true), "gemm");
     ++launches_;
   };
   for (size_t l = 0; l < layers_.size(); ++l) {
     const Layer& y = layers_[l];
-    check(launch_rms_norm(residual_, y.in_norm, xn_, size_t(rows), D, cfg_.epsilon, stream_), "rms_norm");
+    check(launch_rms_norm(residual_, y.in_norm, xn_, size_t(rows), D, cfg_.epsilon, stream_, true), "rms_norm");
     {
       const int n0s[3] = {0, Q, Q + G};
       bf16* outs[3] = {q_raw_, k_raw_, vcache_[l] + size_t(first) * G};
@@ -470,13 +473,13 @@ void Engine::run_layers_fast(int rows, long long first) {
       gemm(xn_, D, y.wqkv, Q + 2 * G, D, kGemmStore, 3, n0s, outs, lds);
     }
     check(launch_qk_norm_rope(q_raw_, k_raw_, y.q_norm, y.k_norm, inv_freq_, q_rot_, kcache_[l], pos, rows, H, Hk,
-                              d, cfg_.epsilon, stream_, false),
+                              d, cfg_.epsilon, stream_, true),
           "qk_norm_rope");
     if (attn_tc_) {
       // Tensor-core causal attention over keys 0 .. first+rows-1.
-      check(launch_vt_transpose(vcache_[l], vt_, int(first) + rows, Hk, d, vt_stride_, stream_), "v transpose");
+      check(launch_vt_transpose(vcache_[l], vt_, int(first) + rows, Hk, d, vt_stride_, stream_, true), "v transpose");
       check(launch_attention_prefill_tc(attn_tc_, att_, rows, first, int(l), H, Hk, attention_scale(d), &state_->err,
-                                        stream_),
+                                        stream_, true),
             "attention prefill");
     } else {
       check(launch_attention_scores(q_rot_, kcache_[l], scores_, pos, rows, H, Hk, d, cap, attention_scale(d),
@@ -491,7 +494,7 @@ void Engine::run_layers_fast(int rows, long long first) {
       const int lds[1] = {D};
       gemm(att_, Q, y.wo, D, Q, kGemmResidual, 1, n0s, outs, lds);
     }
-    check(launch_rms_norm(residual_, y.post_norm, xn_, size_t(rows), D, cfg_.epsilon, stream_), "rms_norm");
+    check(launch_rms_norm(residual_, y.post_norm, xn_, size_t(rows), D, cfg_.epsilon, stream_, true), "rms_norm");
     ++launches_;
     {
       const int n0s[1] = {0};

@@ -46,7 +46,7 @@ cudaError_t launch_add(const bf16* a, const bf16* b, bf16* out, size_t n, cudaSt
 cudaError_t launch_silu_multiply(const bf16* g, const bf16* u, bf16* out, size_t n,
                                  cudaStream_t stream);
 cudaError_t launch_rms_norm(const bf16* x, const bf16* w, bf16* out, size_t rows, int width,
-                            float eps, cudaStream_t stream);
+                            float eps, cudaStream_t stream, bool pdl = false);
 cudaError_t launch_rotary(const bf16* x, bf16* out, size_t positions, int heads, int width,
                           RowPositions pos, double theta, bool positioned_output,
                           cudaStream_t stream);

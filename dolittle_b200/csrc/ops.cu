@@ -44,19 +44,24 @@ __global__ void qk_norm_rope_kernel(const bf16* __restrict__ q_raw, const bf16* 
                                     bf16* __restrict__ k_cache, RowPositions pos, int query_heads,
                                     int kv_heads, int width, float eps) {
   __shared__ float vals[kNormWarps][128];
+  __shared__ float co[64], si[64];
   allow_next();
   wait_prior();
   const int warp = threadIdx.x >> 5;
   const int r = blockIdx.x;
-  const int head = blockIdx.y * kNormWarps + warp;
-  if (head >= query_heads + kv_heads) return;
-  const bool is_q = head < query_heads;
-  const bf16* src = is_q ? q_raw + (size_t(r) * query_heads + head) * width
-                         : k_raw + (size_t(r) * kv_heads + (head - query_heads)) * width;
   const int p = row_position(pos, r);
-  bf16* dst = is_q ? q_out + (size_t(r) * query_heads + head) * width
-                   : k_cache + (size_t(p) * kv_heads + (head - query_heads)) * width;
-  qk_norm_rope_warp(src, is_q ? qw : kw, inv_freq, p, dst, width, eps, vals[warp]);
+  // One block per row: the row's RoPE factors once, then the warps walk the
+  // heads.
+  rope_factors(inv_freq, p, width, co, si);
+  __syncthreads();
+  for (int head = warp; head < query_heads + kv_heads; head += kNormWarps) {
+    const bool is_q = head < query_heads;
+    const bf16* src = is_q ? q_raw + (size_t(r) * query_heads + head) * width
+                           : k_raw + (size_t(r) * kv_heads + (head - query_heads)) * width;
+    bf16* dst = is_q ? q_out + (size_t(r) * query_heads + head) * width
+                     : k_cache + (size_t(p) * kv_heads + (head - query_heads)) * width;
+    qk_norm_rope_warp_table(src, is_q ? qw : kw, co, si, dst, width, eps, vals[warp]);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -281,7 +286,10 @@ __global__ void rms_norm_kernel(const bf16* x, const bf16* w, bf16* out, size_t 
 __global__ void rms_norm_rows_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w, bf16* __restrict__ out,
                                      int width, float eps) {
   extern __shared__ float xs[];  // [width]
+  __shared__ float chains[128];
   __shared__ float inv_s;
+  allow_next();
+  wait_prior();
   const size_t r = blockIdx.x;
   const int n8 = width / 8;
   const uint4* src = reinterpret_cast<const uint4*>(x + r * width);
@@ -295,7 +303,22 @@ __global__ void rms_norm_rows_kernel(const bf16* __restrict__ x, const bf16* __r
     }
   }
   __syncthreads();
-  if (threadIdx.x < 32) {
+  if (width > 128) {
+    // The staged law's component sums run as 128 independent chains, one
+    // per thread (chain t = 4 * lane + c sums columns t, t + 128, ...); warp
+    // 0 then adds each lane's four in order and runs the shuffle tree.
+    float chain = 0.f;
+    for (int col = threadIdx.x; col < width; col += 128) chain = __fadd_rn(chain, __fmul_rn(xs[col], xs[col]));
+    chains[threadIdx.x] = chain;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      const float* c4 = chains + 4 * threadIdx.x;
+      float sum = __fadd_rn(__fadd_rn(__fadd_rn(c4[0], c4[1]), c4[2]), c4[3]);
+      sum = shuffle_down_tree32(sum);
+      const float total = __shfl_sync(0xffffffffu, sum, 0);
+      if (threadIdx.x == 0) inv_s = rsqrtf(__fadd_rn(__fmul_rn(total, 1.0f / static_cast<float>(width)), eps));
+    }
+  } else if (threadIdx.x < 32) {
     const float inv = rms_inverse_warp(xs, width, eps);
     if (threadIdx.x == 0) inv_s = inv;
   }
@@ -390,9 +413,7 @@ cudaError_t launch_qk_norm_rope(const bf16* q_raw, const bf16* k_raw, const bf16
                                 int kv_heads, int width, float eps, cudaStream_t stream, bool pdl) {
   if (width > 128 || width % 2) return cudaErrorInvalidValue;
   cudaLaunchAttribute attr[1];
-  const int heads = query_heads + kv_heads;
-  auto cfg = make_config(dim3(rows, (heads + kNormWarps - 1) / kNormWarps), dim3(32 * kNormWarps), 0,
-                         stream, attr, pdl);
+  auto cfg = make_config(dim3(rows), dim3(32 * kNormWarps), 0, stream, attr, pdl);
   return cudaLaunchKernelEx(&cfg, qk_norm_rope_kernel, q_raw, k_raw, q_norm_w, k_norm_w, inv_freq, q_out,
                             k_cache, pos, query_heads, kv_heads, width, eps);
 }
@@ -439,13 +460,14 @@ cudaError_t launch_silu_multiply(const bf16* g, const bf16* u, bf16* out, size_t
 }
 
 cudaError_t launch_rms_norm(const bf16* x, const bf16* w, bf16* out, size_t rows, int width, float eps,
-                            cudaStream_t stream) {
+                            cudaStream_t stream, bool pdl) {
   if (width > 32768) return cudaErrorInvalidValue;
   if (width % 8 == 0 && width <= 8192 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
       reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0) {
     const size_t smem = size_t(width) * sizeof(float);
-    rms_norm_rows_kernel<<<unsigned(rows), 128, smem, stream>>>(x, w, out, width, eps);
-    return cudaGetLastError();
+    cudaLaunchAttribute attr[1];
+    auto cfg = make_config(dim3(unsigned(rows)), dim3(128), smem, stream, attr, pdl);
+    return cudaLaunchKernelEx(&cfg, rms_norm_rows_kernel, x, w, out, width, eps);
   }
   const int warps = width > 8192 ? 1 : (width > 2048 ? 2 : 4);
   const size_t smem = size_t(warps) * width * sizeof(float);

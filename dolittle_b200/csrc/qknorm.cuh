@@ -76,4 +76,50 @@ __device__ __forceinline__ void qk_norm_rope_warp(const bf16* src, const bf16* w
   }
 }
 
+// qk_norm_rope_warp with the row's rounded cosine / sine factors already in
+// co[f] / si[f] (f < width / 2): every head of a row shares them, so a block
+// serving all heads of one row computes them once.  Same arithmetic.
+__device__ __forceinline__ void qk_norm_rope_warp_table(const bf16* src, const bf16* w, const float* co,
+                                                        const float* si, bf16* dst, int width, float eps,
+                                                        float* vals) {
+  const int lane = threadIdx.x & 31;
+  float x[4];
+  float part[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int col = lane + 32 * c;
+    x[c] = col < width ? widen(src[col]) : 0.f;
+    if (col < width) part[c] = __fmul_rn(x[c], x[c]);
+  }
+  float sum = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), part[2]), part[3]);
+  sum = shuffle_down_tree32(sum);
+  const float total = __shfl_sync(0xffffffffu, sum, 0);
+  const float inv = rsqrtf(__fadd_rn(__fmul_rn(total, 1.0f / static_cast<float>(width)), eps));
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int col = lane + 32 * c;
+    if (col < width) vals[col] = round_bf16(__fmul_rn(round_bf16(__fmul_rn(x[c], inv)), widen(w[col])));
+  }
+  __syncwarp();
+  const int half = width / 2;
+  for (int f = lane; f < half; f += 32) {
+    const float a = vals[f], b = vals[f + half];
+    const float ac = round_bf16(__fmul_rn(a, co[f])), bs = round_bf16(__fmul_rn(b, si[f]));
+    const float bc = round_bf16(__fmul_rn(b, co[f])), as = round_bf16(__fmul_rn(a, si[f]));
+    dst[f] = narrow(__fsub_rn(ac, bs));
+    dst[f + half] = narrow(__fadd_rn(bc, as));
+  }
+  __syncwarp();
+}
+
+// The rounded RoPE factors of position p for f < width / 2 (threads of the
+// block stride over f).
+__device__ __forceinline__ void rope_factors(const float* inv_freq, int p, int width, float* co, float* si) {
+  for (int f = threadIdx.x; f < width / 2; f += blockDim.x) {
+    const float angle = __fmul_rn(static_cast<float>(p), inv_freq[f]);
+    co[f] = round_bf16(cosf(angle));
+    si[f] = round_bf16(sinf(angle));
+  }
+}
+
 }  // namespace dl
