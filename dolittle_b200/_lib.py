@@ -81,7 +81,8 @@ SIGNATURES = {
     "dl_gemm_bf16": (C.c_int, [vp, sz, vp, vp, sz, sz, sz, sz, C.c_int, vp]),
     "dl_gemm_bf16_split_workspace_bytes": (sz, [sz, sz]),
     "dl_gemm_bf16_split": (C.c_int, [vp, sz, vp, vp, sz, sz, sz, sz, C.c_int, vp, vp, vp, sz]),
-    "dl_gemm_bf16_config": (C.c_int, [vp, sz, vp, vp, sz, sz, sz, sz, C.c_int, vp, vp, vp, sz, C.c_int, C.c_int]),
+    "dl_gemm_bf16_config": (C.c_int, [vp, sz, vp, vp, sz, sz, sz, sz, C.c_int, vp, vp, vp, sz, C.c_int, C.c_int,
+                                      C.c_int]),
     "dl_sampler_required_bytes": (sz, [sz]),
     "dl_sampler_create": (C.c_int, [sz, C.c_int, C.POINTER(vp)]),
     "dl_sampler_destroy": (None, [vp]),

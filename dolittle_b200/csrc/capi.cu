@@ -308,21 +308,23 @@ DL_API size_t dl_gemm_bf16_split_workspace_bytes(size_t M, size_t N) {
 
 DL_API dl_status dl_gemm_bf16_config(const void* x, size_t ldx, const void* w, void* y, size_t ldy, size_t M,
                                      size_t N, size_t K, int epilogue, void* stream, void* workspace,
-                                     unsigned* tickets, size_t n_tickets, int tile_n, int parts) {
+                                     unsigned* tickets, size_t n_tickets, int tile_m, int tile_n, int parts) {
   if ((workspace == nullptr) != (tickets == nullptr))
     return fail(DL_INVALID_ARGUMENT, "gemm: workspace and tickets go together");
   if (workspace && n_tickets < ((M + 127) / 128) * (N / 128))
     return fail(DL_INVALID_ARGUMENT, "gemm split: one ticket per 128 x 128 tile required");
-  if ((tile_n != 0 && tile_n != 128 && tile_n != 256) || parts < 0 || parts > dl::kGemmMaxSplit ||
-      (parts > 1 && !workspace))
-    return fail(DL_INVALID_ARGUMENT, "gemm: tile_n 0/128/256, parts 0..4 (more than 1 needs the workspace)");
+  if ((tile_m != 0 && tile_m != 128 && tile_m != 256) || (tile_n != 0 && tile_n != 128 && tile_n != 256) ||
+      (tile_m == 256 && tile_n == 128) || parts < 0 || parts > dl::kGemmMaxSplit || (parts > 1 && !workspace))
+    return fail(DL_INVALID_ARGUMENT,
+                "gemm: tile_m 0/128/256, tile_n 0/128/256 (256 x 128 does not exist), parts 0..4 (more than 1 needs "
+                "the workspace)");
   if (!x || !w || !y || !M) return fail(DL_INVALID_ARGUMENT, "gemm: null pointer or empty shape");
   if (epilogue != dl::kGemmStore && epilogue != dl::kGemmResidual && epilogue != dl::kGemmSwiGLU)
     return fail(DL_INVALID_ARGUMENT, "gemm: epilogue must be 0, 1 or 3");
   if (!dl::gemm_tcgen05_supported(int(M), int(N), int(K)) || ldx % 8 || ldy % 8 || ldx < K ||
       (reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y)) % 16)
     return fail(DL_UNSUPPORTED, "gemm: K % 64, N % 128, 8-element row strides and 16-byte alignment required");
-  if ((tile_n == 256 && N % 256) || (parts > 1 && size_t(K / 64) < size_t(4 * parts)))
+  if (((tile_n == 256 || tile_m == 256) && N % 256) || (parts > 1 && size_t(K / 64) < size_t(4 * parts)))
     return fail(DL_UNSUPPORTED, "gemm: 256-wide tiles need N % 256; each K part needs 4 k-steps of 64");
   dl::GemmProblem p = {};
   p.x = static_cast<const bf16*>(x);
@@ -342,6 +344,7 @@ DL_API dl_status dl_gemm_bf16_config(const void* x, size_t ldx, const void* w, v
     p.tickets = tickets;
     p.n_tickets = int(std::min<size_t>(n_tickets, 1u << 30));
   }
+  p.force_bm = tile_m;
   p.force_bn = tile_n;
   p.force_split = parts;
   return cuda_status(dl::launch_gemm_tcgen05(p, st(stream), false), "gemm");
@@ -351,7 +354,7 @@ DL_API dl_status dl_gemm_bf16_split(const void* x, size_t ldx, const void* w, vo
                                     size_t N, size_t K, int epilogue, void* stream, void* workspace,
                                     unsigned* tickets, size_t n_tickets) {
   if (!workspace || !tickets) return fail(DL_INVALID_ARGUMENT, "gemm split: workspace and tickets required");
-  return dl_gemm_bf16_config(x, ldx, w, y, ldy, M, N, K, epilogue, stream, workspace, tickets, n_tickets, 0, 0);
+  return dl_gemm_bf16_config(x, ldx, w, y, ldy, M, N, K, epilogue, stream, workspace, tickets, n_tickets, 0, 0, 0);
 }
 
 DL_API dl_status dl_projection_residual(const void* input, const void* weight, void* residual, size_t rows,

@@ -39,6 +39,10 @@ constexpr int kThreads = 192;  // producer warp, MMA warp, 4 epilogue warps
 // projections (qkv, o, gate|up, down) over tile widths 128 / 256 and 1-4
 // parts: the estimate ranks the measured times in the same order.
 constexpr double kStep128 = 0.95;
+// 256 x 256 on two SMs (32 KB of loads per SM and k-step, against 48 KB) measured
+// 1.13-1.4x the single-SM step: one accumulator, so the epilogue does not
+// overlap the next tile, and each step waits for both SMs' loads.
+constexpr double kStepPair = 1.25;
 constexpr double kSplitFixed = 16.0;
 constexpr double kSplitPerByte = 1.0 / 1.5e6;
 
@@ -126,6 +130,93 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, bf16* out, int ld
   uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
   for (int q = 0; q < 4; ++q) d4[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+}
+
+// Epilogue of one 128-row x BN tile held in TMEM at `acc` (this warp's lane
+// group): the store / residual / SwiGLU epilogue of output row `row`, columns
+// c0.. of `out`; or, with K split in parts, this part's FP32 partial
+// (block `tile` of `tiles`) and, for the last part to finish, the sum in
+// part order followed by the epilogue.  Run by the 4 epilogue warps (threads
+// 64-191, named barrier 1).
+template <int BN>
+__device__ __forceinline__ void tile_epilogue(const GemmArgs& a, uint32_t acc, bf16* out, int ld, int row, int c0,
+                                              int tile, int tiles, int half, int q, int lane, bool& last_half) {
+  if (a.split == 1) {
+    const bool resid = a.epilogue == kGemmResidual && row < a.M;
+    uint4 res[4] = {};
+    if (resid) load_residual(out, ld, row, c0, res);
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(acc + uint32_t(c * 32), r);
+      uint4 next[4] = {};
+      if (resid && c + 1 < BN / 32) load_residual(out, ld, row, c0 + (c + 1) * 32, next);
+      if (row < a.M) store_chunk(a, out, ld, row, c0 + c * 32, r, res);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) res[q] = next[q];
+    }
+  } else {
+    // Every K part publishes its FP32 partial; the last part to finish
+    // adds all parts in part order (p0 + p1 + ... whichever finished
+    // last, so the result is deterministic) and applies the epilogue.
+    // Partial block of (part, tile): [BN columns][128 rows], so each warp
+    // store covers one 128-byte line (lanes = consecutive rows).
+    const size_t blk = size_t(BN) * kBM;
+    float* mine = a.partial + (size_t(half) * tiles + tile) * blk + q * 32 + lane;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(acc + uint32_t(c * 32), r);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) mine[size_t(c * 32 + i) * kBM] = __uint_as_float(r[i]);
+    }
+    __threadfence();
+    named_sync(1, 128);
+    if (threadIdx.x == 64) last_half = atomicAdd(&a.tickets[tile], 1u) == unsigned(a.split - 1);
+    named_sync(1, 128);
+    if (last_half) {
+      __threadfence();
+      const float* first = a.partial + size_t(tile) * blk + q * 32 + lane;
+      const size_t part_stride = size_t(tiles) * blk;
+      const bool resid = a.epilogue == kGemmResidual && row < a.M;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        // One round trip per chunk: the other parts' values and the
+        // residual words are all loaded before the sums.
+        float pv[kGemmMaxSplit][32];
+#pragma unroll
+        for (int h = 0; h < kGemmMaxSplit; ++h)
+          if (h < a.split && h != half) {
+            const float* ph = first + size_t(h) * part_stride + size_t(c * 32) * kBM;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) pv[h][i] = __ldcg(ph + size_t(i) * kBM);
+          }
+        uint4 res[4] = {};
+        if (resid) load_residual(out, ld, row, c0 + c * 32, res);
+        uint32_t r[32];
+        tmem_ld32(acc + uint32_t(c * 32), r);
+#pragma unroll
+        for (int h = 0; h < kGemmMaxSplit; ++h)
+          if (h == half) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) pv[h][i] = __uint_as_float(r[i]);
+          }
+        // Sum in part order.
+#pragma unroll
+        for (int h = 1; h < kGemmMaxSplit; ++h)
+          if (h < a.split) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) pv[0][i] = __fadd_rn(pv[0][i], pv[h][i]);
+          }
+        if (row < a.M) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(pv[0][i]);
+          store_chunk(a, out, ld, row, c0 + c * 32, r, res);
+        }
+      }
+      if (threadIdx.x == 64) a.tickets[tile] = 0;
+    }
+  }
 }
 
 // Persistent, warp-specialized: CTA b processes tiles b, b + grid, ... with
@@ -288,81 +379,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
             for (int i = 0; i < 8; ++i) d[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
           }
         }
-      } else if (a.split == 1) {
-        const bool resid = a.epilogue == kGemmResidual && row < a.M;
-        uint4 res[4] = {};
-        if (resid) load_residual(out, ld, row, c0, res);
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(acc + uint32_t(c * 32), r);
-          uint4 next[4] = {};
-          if (resid && c + 1 < BN / 32) load_residual(out, ld, row, c0 + (c + 1) * 32, next);
-          if (row < a.M) store_chunk(a, out, ld, row, c0 + c * 32, r, res);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) res[q] = next[q];
-        }
       } else {
-        // Every K part publishes its FP32 partial; the last part to finish
-        // adds all parts in part order (p0 + p1 + ... whichever finished
-        // last, so the result is deterministic) and applies the epilogue.
-        // Partial block of (part, tile): [BN columns][128 rows], so each warp
-        // store covers one 128-byte line (lanes = consecutive rows).
-        const size_t blk = size_t(BN) * kBM;
-        float* mine = a.partial + (size_t(half) * tiles + tile) * blk + q * 32 + lane;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(acc + uint32_t(c * 32), r);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) mine[size_t(c * 32 + i) * kBM] = __uint_as_float(r[i]);
-        }
-        __threadfence();
-        named_sync(1, 128);
-        if (threadIdx.x == 64) last_half = atomicAdd(&a.tickets[tile], 1u) == unsigned(a.split - 1);
-        named_sync(1, 128);
-        if (last_half) {
-          __threadfence();
-          const float* first = a.partial + size_t(tile) * blk + q * 32 + lane;
-          const size_t part_stride = size_t(tiles) * blk;
-          const bool resid = a.epilogue == kGemmResidual && row < a.M;
-#pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            // One round trip per chunk: the other parts' values and the
-            // residual words are all loaded before the sums.
-            float pv[kGemmMaxSplit][32];
-#pragma unroll
-            for (int h = 0; h < kGemmMaxSplit; ++h)
-              if (h < a.split && h != half) {
-                const float* ph = first + size_t(h) * part_stride + size_t(c * 32) * kBM;
-#pragma unroll
-                for (int i = 0; i < 32; ++i) pv[h][i] = __ldcg(ph + size_t(i) * kBM);
-              }
-            uint4 res[4] = {};
-            if (resid) load_residual(out, ld, row, c0 + c * 32, res);
-            uint32_t r[32];
-            tmem_ld32(acc + uint32_t(c * 32), r);
-#pragma unroll
-            for (int h = 0; h < kGemmMaxSplit; ++h)
-              if (h == half) {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) pv[h][i] = __uint_as_float(r[i]);
-              }
-            // Sum in part order.
-#pragma unroll
-            for (int h = 1; h < kGemmMaxSplit; ++h)
-              if (h < a.split) {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) pv[0][i] = __fadd_rn(pv[0][i], pv[h][i]);
-              }
-            if (row < a.M) {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(pv[0][i]);
-              store_chunk(a, out, ld, row, c0 + c * 32, r, res);
-            }
-          }
-          if (threadIdx.x == 64) a.tickets[tile] = 0;
-        }
+        tile_epilogue<BN>(a, acc, out, ld, row, c0, tile, tiles, half, q, lane, last_half);
       }
       fence_before_sync();
       __syncwarp();
@@ -372,6 +390,175 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
   fence_before_sync();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, kCols);
+}
+
+// TMA load into this CTA's shared memory whose completion is counted on the
+// pair's even-CTA barrier (`bar`, a cluster address).
+__device__ __forceinline__ void tma_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// CTA-pair GEMM: 256 x 256 output tiles on two SMs (tcgen05 cta_group::2).
+// Per k-step each CTA loads its 128 input rows and 128 of the tile's 256
+// weight rows (32 KB, against 48 KB for a 128 x 256 tile on one SM), and
+// the even CTA's MMA thread issues one M = 256, N = 256 MMA per 16 features
+// over both CTAs' shared memory.  Both CTAs' loads complete on the even
+// CTA's stage barrier; each MMA batch is committed to both CTAs' stage-free
+// barriers, each finished tile to both CTAs' accumulator barriers; the
+// epilogue warps of both CTAs drain their 128 TMEM rows and report to the
+// even CTA.  One 256-column accumulator per CTA.  Units are (tile, K part)
+// as in the single-CTA kernel; pair p takes units p, p + pairs, ...
+constexpr int kPairN = 256;
+constexpr uint32_t kPairCols = 256;
+
+__global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_constant__ GemmArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ uint64_t full[8], empty[8], acc_full, acc_empty;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  __shared__ bool last_half;
+  constexpr int kABytes = kBM * kBK * 2;
+  constexpr int kBBytes = (kPairN / 2) * kBK * 2;
+  constexpr int kStageBytes = kABytes + kBBytes;
+  const uint32_t base_s = (smem_addr(smem_raw) + 1023u) & ~1023u;
+  unsigned char* ring = smem_raw + (base_s - smem_addr(smem_raw));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  const int mt = (a.M + 2 * kBM - 1) / (2 * kBM);
+  const int tiles = mt * (a.N / kPairN);
+  const int units = tiles * a.split;
+  const int kt_all = a.K / kBK;
+  const int S = a.stages;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&acc_full, 1);
+    mbar_init(&acc_empty, 8);  // 4 epilogue warps in each CTA
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc_pair(&tmem_base, kPairCols);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  // Both CTAs' barriers exist before either signals the other's.
+  cluster_sync();
+  const uint32_t tmem = tmem_base;
+  allow_next();
+  wait_prior();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // Producer (both CTAs): this CTA's A rows and B rows of each k-step,
+      // completing on the even CTA's stage barrier.
+      int g = 0;
+      for (int u = pair; u < units && !*reinterpret_cast<volatile int*>(&abort_flag); u += pairs) {
+        const int tile = u % tiles, part = u / tiles;
+        const int m0 = (tile % mt) * 2 * kBM + int(rank) * kBM;
+        const int nb = (tile / mt) * kPairN + int(rank) * (kPairN / 2);
+        for (int kt = part * kt_all / a.split; kt < (part + 1) * kt_all / a.split; ++kt, ++g) {
+          const int s = g % S;
+          if (g >= S && !mbar_wait_cluster(&empty[s], ((g / S) - 1) & 1)) {
+            record_error(a.err, kErrWaitEmpty);
+            atomicExch(&abort_flag, 1);
+            break;
+          }
+          unsigned char* st = ring + s * kStageBytes;
+          const uint32_t bar = mapa_shared(smem_addr(&full[s]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * kStageBytes);
+          tma_2d_pair(st, &a.map_a, kt * kBK, m0, bar);
+          tma_2d_pair(st + kABytes, &a.map_b, kt * kBK, nb, bar);
+        }
+      }
+      // Drain: the last commits onto this CTA's stage barriers have landed
+      // before the CTA can leave.
+      if (!*reinterpret_cast<volatile int*>(&abort_flag))
+        for (int h = g - S < 0 ? 0 : g - S; h < g; ++h)
+          if (!mbar_wait_cluster(&empty[h % S], (h / S) & 1)) {
+            record_error(a.err, kErrWaitEmpty);
+            break;
+          }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // MMA issuer (even CTA).
+      constexpr uint32_t idesc = instr_desc_bf16(2 * kBM, kPairN);
+      const uint32_t acc_full0 = mapa_shared(smem_addr(&acc_full), 0);
+      const uint32_t acc_full1 = mapa_shared(smem_addr(&acc_full), 1);
+      int g = 0, t = 0;
+      for (int u = pair; u < units && !*reinterpret_cast<volatile int*>(&abort_flag); u += pairs, ++t) {
+        if (t >= 1 && !mbar_wait_cluster(&acc_empty, (t - 1) & 1)) {
+          record_error(a.err, kErrWaitEmpty);
+          atomicExch(&abort_flag, 1);
+          break;
+        }
+        fence_after_sync();
+        bool ok = true;
+        const int part = u / tiles;
+        const int kt_n = (part + 1) * kt_all / a.split - part * kt_all / a.split;
+        for (int kt = 0; kt < kt_n; ++kt, ++g) {
+          const int s = g % S;
+          if (!mbar_wait_cluster(&full[s], (g / S) & 1)) {
+            record_error(a.err, kErrWaitFull);
+            atomicExch(&abort_flag, 1);
+            ok = false;
+            break;
+          }
+          fence_after_sync();
+          const uint32_t sa = smem_addr(ring + s * kStageBytes);
+          const uint64_t adesc = smem_desc_sw128(sa);
+          const uint64_t bdesc = smem_desc_sw128(sa + kABytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            mma_bf16_pair(tmem, adesc + uint64_t(kk * 2), bdesc + uint64_t(kk * 2), idesc, (kt | kk) != 0);
+          mma_commit_pair(mapa_shared(smem_addr(&empty[s]), 0));
+          mma_commit_pair(mapa_shared(smem_addr(&empty[s]), 1));
+        }
+        if (!ok) break;
+        mma_commit_pair(acc_full0);
+        mma_commit_pair(acc_full1);
+      }
+    }
+  } else {
+    // Epilogue warps (both CTAs): TMEM lane group q = warp % 4 holds rows
+    // 32q .. 32q+31 of this CTA's 128 rows of the tile.
+    const int q = warp & 3;
+    const uint32_t acc_empty0 = mapa_shared(smem_addr(&acc_empty), 0);
+    int t = 0;
+    for (int u = pair; u < units; u += pairs, ++t) {
+      const int tile = u % tiles, half = u / tiles;
+      if (!mbar_wait_cluster(&acc_full, t & 1)) {
+        record_error(a.err, kErrWaitFull);
+        atomicExch(&abort_flag, 1);
+        break;
+      }
+      fence_after_sync();
+      const int m0 = (tile % mt) * 2 * kBM + int(rank) * kBM, n0 = (tile / mt) * kPairN;
+      const int row = m0 + q * 32 + lane;
+      int si = 0;
+      for (int i = 1; i < a.nseg; ++i)
+        if (n0 >= a.seg_n0[i]) si = i;
+      // Split-K blocks and tickets per 128-row half tile.
+      tile_epilogue<kPairN>(a, tmem + (uint32_t(q * 32) << 16), a.seg_out[si], a.seg_ld[si], row,
+                            n0 - a.seg_n0[si], tile * 2 + int(rank), tiles * 2, half, q, lane, last_half);
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(acc_empty0);
+    }
+  }
+  fence_before_sync();
+  __syncthreads();
+  // Neither CTA leaves while the pair may still touch its shared memory or TMEM.
+  cluster_sync();
+  if (warp == 0) tmem_dealloc_pair(tmem, kPairCols);
 }
 
 }  // namespace
@@ -407,7 +594,9 @@ bool encode_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
 
 bool gemm_tcgen05_supported(int M, int N, int K) { return M > 0 && K % kBK == 0 && N % 128 == 0; }
 
-size_t gemm_split_floats(int M, int N, int parts) { return size_t(parts) * size_t((M + kBM - 1) / kBM) * kBM * N; }
+size_t gemm_split_floats(int M, int N, int parts) {
+  return size_t(parts) * size_t((M + 2 * kBM - 1) / (2 * kBM)) * 2 * kBM * N;  // 256-row tiles (CTA pairs) included
+}
 
 namespace {
 
@@ -518,6 +707,32 @@ cudaError_t launch_gemm_splitk_epilogue(const float* parts, int splits, int M, i
   return cudaGetLastError();
 }
 
+// CTA pairs that fit on the device at once (clusters of 2 at one CTA per SM).
+int gemm_pair_clusters(int sms) {
+  static int cached = -1;
+  static std::once_flag once;
+  std::call_once(once, [sms] {
+    const size_t smem = size_t(std::min(8, (225 * 1024) / ((kBM + kPairN / 2) * kBK * 2))) *
+                            ((kBM + kPairN / 2) * kBK * 2) + 1024;
+    cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * unsigned(sms / 2));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    cached = cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel, &cfg) == cudaSuccess ? n : 0;
+    cudaGetLastError();
+  });
+  return cached;
+}
+
 cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool pdl) {
   if (!gemm_tcgen05_supported(p.M, p.N, p.K) || p.nseg < 1 || p.nseg > 3) return cudaErrorInvalidValue;
   GemmArgs a = {};
@@ -532,25 +747,38 @@ cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool 
   for (int i = 0; i < p.nseg; ++i) aligned256 = aligned256 && p.seg_n0[i] % 256 == 0;
   const bool workspace = p.partial && p.tickets;
   int BN = 0, split = 0;
+  bool pair = false;
   double best = 1e30;
-  for (int bn : {256, 128}) {
-    if (bn == 256 && !(aligned256 && p.wide_tiles)) continue;
-    if (p.force_bn && bn != p.force_bn) continue;
-    const long long tiles = mt * (p.N / bn);
+  // Single-CTA tiles 128 x 256 / 128 x 128, and 256 x 256 tiles on CTA pairs.
+  struct Shape {
+    int bm, bn;
+  };
+  const Shape shapes[3] = {{128, 256}, {128, 128}, {256, 256}};
+  const int pair_slots = gemm_pair_clusters(sms);
+  for (const Shape& sh : shapes) {
+    const bool is_pair = sh.bm == 256;
+    if (sh.bn == 256 && !(aligned256 && p.wide_tiles)) continue;
+    if (p.force_bn && sh.bn != p.force_bn) continue;
+    if (p.force_bm && sh.bm != p.force_bm) continue;
+    if (is_pair && pair_slots < 1) continue;
+    const long long mtiles = (p.M + sh.bm - 1) / sh.bm;
+    const long long tiles = mtiles * (p.N / sh.bn);
+    const long long slots = is_pair ? pair_slots : sms;
     for (int sp = 1; sp <= kGemmMaxSplit; ++sp) {
       if (p.force_split && sp != p.force_split) continue;
-      if (sp > 1 && (!workspace || kt / sp < 4 || gemm_split_floats(p.M, p.N, sp) > p.partial_floats ||
-                     tiles > p.n_tickets))
+      const size_t split_floats = size_t(sp) * size_t(mtiles) * sh.bm * size_t(p.N);
+      if (sp > 1 && (!workspace || kt / sp < 4 || split_floats > p.partial_floats ||
+                     tiles * (sh.bm / kBM) > p.n_tickets))
         continue;
-      const long long waves = (tiles * sp + sms - 1) / sms;
-      const double step = bn == 256 ? 1.0 : kStep128;
-      const double split_cost =
-          sp > 1 ? kSplitFixed + kSplitPerByte * 4.0 * double(gemm_split_floats(p.M, p.N, sp)) : 0.0;
+      const long long waves = (tiles * sp + slots - 1) / slots;
+      const double step = is_pair ? kStepPair : sh.bn == 256 ? 1.0 : kStep128;
+      const double split_cost = sp > 1 ? kSplitFixed + kSplitPerByte * 4.0 * double(split_floats) : 0.0;
       const double cost = double(waves) * double((kt + sp - 1) / sp) * step + split_cost;
       if (cost < best * 0.98) {
         best = cost;
-        BN = bn;
+        BN = sh.bn;
         split = sp;
+        pair = is_pair;
       }
     }
   }
@@ -558,7 +786,8 @@ cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool 
   for (int i = 0; i < p.nseg; ++i)
     if (p.seg_n0[i] % BN) return cudaErrorInvalidValue;  // tiles never straddle outputs
   if (!encode_2d(&a.map_a, p.x, uint64_t(p.M), uint64_t(p.K), uint64_t(p.ldx), kBM)) return cudaErrorInvalidValue;
-  if (!encode_2d(&a.map_b, p.w, uint64_t(p.N), uint64_t(p.K), uint64_t(p.K), uint32_t(BN))) return cudaErrorInvalidValue;
+  if (!encode_2d(&a.map_b, p.w, uint64_t(p.N), uint64_t(p.K), uint64_t(p.K), uint32_t(pair ? BN / 2 : BN)))
+    return cudaErrorInvalidValue;
   a.M = p.M;
   a.N = p.N;
   a.K = p.K;
@@ -570,13 +799,31 @@ cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool 
     a.seg_ld[i] = p.seg_ld[i];
   }
   a.err = p.err;
-  const int stage_bytes = (kBM + BN) * kBK * 2;
+  const int stage_bytes = (kBM + (pair ? BN / 2 : BN)) * kBK * 2;
   a.stages = std::min(8, (225 * 1024) / stage_bytes);
   const size_t smem = size_t(a.stages) * stage_bytes + 1024;
   cudaLaunchConfig_t cfg = {};
   a.split = split;
   a.partial = p.partial;
   a.tickets = p.tickets;
+  if (pair) {
+    const long long units = (long long)((p.M + 2 * kBM - 1) / (2 * kBM)) * (p.N / kPairN) * split;
+    cfg.gridDim = dim3(unsigned(2 * std::min<long long>(units, pair_slots)));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    return cudaLaunchKernelEx(&cfg, gemm_pair_kernel, a);
+  }
   const long long units = mt * (p.N / BN) * split;
   cfg.gridDim = dim3(unsigned(std::min<long long>(units, sms)));
   cfg.blockDim = dim3(kThreads);

@@ -32,15 +32,16 @@ struct GemmProblem {
   size_t partial_floats;
   unsigned* tickets;
   int n_tickets;
-  // Tuning overrides (0 = chosen by the launcher): tile width 128 / 256 and
-  // the number of K parts.
-  int force_bn, force_split;
+  // Tuning overrides (0 = chosen by the launcher): tile height 128 (one SM)
+  // or 256 (a CTA pair, 256 wide), tile width 128 / 256, the number of K parts.
+  int force_bm, force_bn, force_split;
 };
 
 constexpr int kGemmMaxSplit = 4;
 
 bool gemm_tcgen05_supported(int M, int N, int K);
-// FP32 workspace of `parts` K parts: one [128 rows x N] plane per part.
+// FP32 workspace of `parts` K parts: one plane of N columns x M rows rounded
+// up to 256 per part.
 size_t gemm_split_floats(int M, int N, int parts);
 cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool pdl);
 

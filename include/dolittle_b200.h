@@ -163,12 +163,13 @@ DL_API size_t dl_gemm_bf16_split_workspace_bytes(size_t M, size_t N);
 DL_API dl_status dl_gemm_bf16_split(const void* x, size_t ldx, const void* w, void* y, size_t ldy, size_t M,
                                     size_t N, size_t K, int epilogue, void* stream, void* workspace,
                                     unsigned* tickets, size_t n_tickets);
-/* dl_gemm_bf16_split with the tiling chosen by the caller: tile_n 128 or 256
- * output columns per tile and `parts` K parts (1..4; 0 = chosen by the
- * library for either).  workspace / tickets may be NULL when parts <= 1. */
+/* dl_gemm_bf16_split with the tiling chosen by the caller: tile_m 128 rows
+ * per tile on one SM or 256 on a pair of SMs (then 256 columns), tile_n 128
+ * or 256 output columns, and `parts` K parts (1..4); 0 = chosen by the
+ * library for any of them.  workspace / tickets may be NULL when parts <= 1. */
 DL_API dl_status dl_gemm_bf16_config(const void* x, size_t ldx, const void* w, void* y, size_t ldy, size_t M,
                                      size_t N, size_t K, int epilogue, void* stream, void* workspace,
-                                     unsigned* tickets, size_t n_tickets, int tile_n, int parts);
+                                     unsigned* tickets, size_t n_tickets, int tile_m, int tile_n, int parts);
 /* residual = round(residual + round(X W^T)) in place. */
 DL_API dl_status dl_projection_residual(const void* input, const void* weight, void* residual,
                                         size_t rows, size_t input_width, size_t output_width,

@@ -71,15 +71,19 @@ def test_gemm_residual_and_swiglu_epilogues():
     assert r2["passed"], r2
 
 
-@pytest.mark.parametrize("M,N,K,epi,tile_n,parts", [(512, 4096, 4096, 0, 0, 0), (512, 4096, 12288, 1, 0, 0),
-                                                    (200, 6144, 4096, 0, 0, 0), (512, 4096, 4096, 1, 256, 3),
-                                                    (300, 4096, 4096, 0, 128, 4), (512, 4096, 12288, 1, 128, 2),
-                                                    (129, 2048, 1024, 0, 256, 4), (512, 2048, 4096, 3, 128, 3)])
-def test_gemm_split_k_matches_fp32_reference_and_unsplit(M, N, K, epi, tile_n, parts):
+@pytest.mark.parametrize("M,N,K,epi,tile_m,tile_n,parts", [
+    (512, 4096, 4096, 0, 0, 0, 0), (512, 4096, 12288, 1, 0, 0, 0), (200, 6144, 4096, 0, 0, 0, 0),
+    (512, 4096, 4096, 1, 128, 256, 3), (300, 4096, 4096, 0, 128, 128, 4), (512, 4096, 12288, 1, 128, 128, 2),
+    (129, 2048, 1024, 0, 128, 256, 4), (512, 2048, 4096, 3, 128, 128, 3),
+    # 256 x 256 tiles on CTA pairs (tcgen05 cta_group::2)
+    (512, 4096, 4096, 0, 256, 256, 1), (300, 2048, 4096, 1, 256, 256, 1), (512, 4096, 12288, 1, 256, 256, 2),
+    (700, 4096, 2048, 3, 256, 256, 3), (2048, 6144, 4096, 0, 256, 0, 1)])
+def test_gemm_split_k_matches_fp32_reference_and_unsplit(M, N, K, epi, tile_m, tile_n, parts):
     """Split-K (up to 4 K parts summed in FP32 in part order by the last
-    finisher; tile width and parts chosen by the library or pinned) against
-    the FP32 reference: same tolerance as the unsplit kernel, and repeated
-    runs are bit-identical (the order of the parts is fixed)."""
+    finisher) and single-SM or CTA-pair tiles, chosen by the library or
+    pinned, against the FP32 reference: same tolerance as the unsplit
+    kernel, and repeated runs are bit-identical (the order of the parts is
+    fixed)."""
     torch = _torch()
     x, w = _case(M, N, K, seed=M + K + epi)
     ncols = N // 2 if epi == 3 else N
@@ -92,7 +96,8 @@ def test_gemm_split_k_matches_fp32_reference_and_unsplit(M, N, K, epi, tile_n, p
     for _ in range(2):
         y = res.clone() if epi == 1 else torch.empty(M, ncols, device="cuda", dtype=torch.bfloat16)
         assert L.dl_gemm_bf16_config(x.data_ptr(), K, w.data_ptr(), y.data_ptr(), ncols, M, N, K, epi, None,
-                                     ws.data_ptr(), tickets.data_ptr(), n_t, tile_n, parts) == 0, L.dl_last_error()
+                                     ws.data_ptr(), tickets.data_ptr(), n_t, tile_m, tile_n, parts) == 0, \
+            L.dl_last_error()
         torch.cuda.synchronize()
         outs.append(y)
     assert torch.equal(outs[0], outs[1])
