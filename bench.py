@@ -670,7 +670,11 @@ def run_profile_case(args):
 
     gemv: the decode GEMV on one gate|up-shaped matrix (24576 x 4096, 201 MB,
     larger than L2), launched 4 times.  decode: a 36-block engine with a
-    16-token prompt and 3 decode passes (one prefill chunk, then graphs)."""
+    16-token prompt and 3 decode passes (one prefill chunk, then graphs).
+    gemm: the four prompt-pass projections at M = 512 (qkv, o +residual,
+    gate|up +SwiGLU, down +residual; library-chosen tiling), 3 launches each.
+    serve-attention: config 5's batched flash decoding (32 sequences x 8192
+    keys, 8 KV heads; 1.07 GB of cache), 4 launches."""
     import torch
     import dolittle_b200 as dl
     torch.cuda.set_device(0)
@@ -692,6 +696,37 @@ def run_profile_case(args):
         e.init_random(SEED, 0.02)
         g = e.generate(prompt_ids(cfg.vocabulary)[:16], 3)
         print("profile persist ok", g.tokens, g.kernels_per_decode_step)
+    elif args.profile == "gemm":
+        L = dl.lib()
+        M = PROMPT
+        for N, K, epi in ((6144, 4096, 0), (4096, 4096, 1), (24576, 4096, 3), (4096, 12288, 1)):
+            x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+            w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+            cols = N // 2 if epi == 3 else N
+            y = torch.zeros(M, cols, device="cuda", dtype=torch.bfloat16)
+            ws = torch.empty(L.dl_gemm_bf16_split_workspace_bytes(M, N), device="cuda", dtype=torch.uint8)
+            n_t = ((M + 127) // 128) * (N // 128)
+            tickets = torch.zeros(n_t, device="cuda", dtype=torch.int32)
+            for _ in range(3):
+                assert L.dl_gemm_bf16_split(x.data_ptr(), K, w.data_ptr(), y.data_ptr(), cols, M, N, K, epi, None,
+                                            ws.data_ptr(), tickets.data_ptr(), n_t) == 0, L.dl_last_error()
+            torch.cuda.synchronize()
+        print("profile gemm ok")
+    elif args.profile == "serve-attention":
+        L = dl.lib()
+        B, Hq, Hkv, cap = 32, 32, 8, 8192
+        G = Hkv * 128
+        kv = torch.randn(B, 2, cap, G, device="cuda").to(torch.bfloat16)
+        q = torch.randn(B, Hq, 128, device="cuda").to(torch.bfloat16)
+        pos = torch.tensor([cap - 1], device="cuda", dtype=torch.int64)
+        out = torch.empty(B, Hq * 128, device="cuda", dtype=torch.bfloat16)
+        ws = torch.empty(L.dl_attention_decode_batched_workspace_bytes(B, Hq, Hkv, cap), device="cuda",
+                         dtype=torch.uint8)
+        for _ in range(4):
+            assert L.dl_attention_decode_batched(q.data_ptr(), kv.data_ptr(), 2 * cap * G, 0, cap * G, pos.data_ptr(),
+                                                 B, Hq, Hkv, cap, out.data_ptr(), ws.data_ptr(), None) == 0
+        torch.cuda.synchronize()
+        print("profile serve-attention ok")
     elif args.profile == "prefill":
         cfg = dl.QWEN3_8B
         e = dl.Engine(cfg, capacity=PROMPT + 8, max_rows=PROMPT)
@@ -718,7 +753,8 @@ def main():
                     help="reference arm: skip timing the reference's CUDA kernels on the GPU")
     ap.add_argument("--prefill", choices=["fast", "parity"], default="fast",
                     help="prompt pass on the tcgen05 GEMMs (fast) or in the reference order (parity)")
-    ap.add_argument("--profile", choices=["gemv", "decode", "prefill", "persist"], default=None,
+    ap.add_argument("--profile", choices=["gemv", "decode", "prefill", "persist", "gemm", "serve-attention"],
+                    default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
     ap.add_argument("--workload", choices=["decode", "serve", "steer", "nla"], default="decode",
                     help="decode: config 2 (headline); serve: config 5 batched serving, TP over the ranks; "

@@ -268,24 +268,49 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
   fence_after_sync();
   const uint32_t tmem = tmem_base;
   allow_next();
-  wait_prior();
+  const bool producer = warp == 0 && lane == 0;
+  if (!producer) wait_prior();
 
   if (warp == 0) {
     if (lane == 0) {
-      // Producer.
+      // Producer.  A rows m0.. (inputs; SWAP: weights), B rows n0.. (weights;
+      // SWAP: inputs).  The weight halves of the first S stages are requested
+      // before waiting for the previous kernel (programmatic dependent launch):
+      // no kernel writes the weights, so they stream in during its tail.
+      int pre = 0;
+      for (int u = blockIdx.x; u < units && pre < S; u += gridDim.x) {
+        const int tile = u % tiles, half = u / tiles;
+        const int m0 = SWAP ? tile * kBM : (tile % mt) * kBM, n0 = SWAP ? 0 : (tile / mt) * BN;
+        for (int kt = half * kt_all / a.split; kt < (half + 1) * kt_all / a.split && pre < S; ++kt, ++pre) {
+          unsigned char* st = ring + pre * kStageBytes;
+          mbar_arrive_expect_tx(&full[pre], kStageBytes);
+          if (SWAP)
+            tma_2d(st, &a.map_a, kt * kBK, m0, &full[pre]);
+          else
+            tma_2d(st + kABytes, &a.map_b, kt * kBK, n0, &full[pre]);
+        }
+      }
+      wait_prior();
       int g = 0;
       for (int u = blockIdx.x; u < units && !*reinterpret_cast<volatile int*>(&abort_flag); u += gridDim.x) {
         const int tile = u % tiles, half = u / tiles;
-        // A rows m0.. (inputs; SWAP: weights), B rows n0.. (weights; SWAP: inputs).
         const int m0 = SWAP ? tile * kBM : (tile % mt) * kBM, n0 = SWAP ? 0 : (tile / mt) * BN;
         for (int kt = half * kt_all / a.split; kt < (half + 1) * kt_all / a.split; ++kt, ++g) {
           const int s = g % S;
+          unsigned char* st = ring + s * kStageBytes;
+          if (g < pre) {
+            // Weights already requested: the input half completes the stage.
+            if (SWAP)
+              tma_2d(st + kABytes, &a.map_b, kt * kBK, n0, &full[s]);
+            else
+              tma_2d(st, &a.map_a, kt * kBK, m0, &full[s]);
+            continue;
+          }
           if (g >= S && !mbar_wait(&empty[s], ((g / S) - 1) & 1)) {
             record_error(a.err, kErrWaitEmpty);
             atomicExch(&abort_flag, 1);
             break;
           }
-          unsigned char* st = ring + s * kStageBytes;
           mbar_arrive_expect_tx(&full[s], kStageBytes);
           tma_2d(st, &a.map_a, kt * kBK, m0, &full[s]);
           tma_2d(st + kABytes, &a.map_b, kt * kBK, n0, &full[s]);
@@ -605,6 +630,7 @@ namespace {
 // of columns.
 __global__ void splitk_epilogue_kernel(const float* __restrict__ parts, int splits, int M, int N, int epilogue,
                                        bf16* out, int ld, float* sum_out) {
+  allow_next();  // a dependent GEMM may request its weights meanwhile
   const size_t pairs = size_t(M) * (N / 2);
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < pairs; i += size_t(gridDim.x) * blockDim.x) {
     const int m = int(i / (N / 2)), n = int(i % (N / 2)) * 2;
@@ -651,7 +677,8 @@ int gemm_splitk_parts(int M, int N, int K, int sms) {
   return best;
 }
 
-cudaError_t launch_gemm_tcgen05_parts(const GemmProblem& p, int splits, float* parts, cudaStream_t stream) {
+cudaError_t launch_gemm_tcgen05_parts(const GemmProblem& p, int splits, float* parts, cudaStream_t stream,
+                                      bool pdl) {
   if (!gemm_tcgen05_supported(p.M, p.N, p.K) || splits < 1 || splits > 16 || p.K / kBK < splits || !parts)
     return cudaErrorInvalidValue;
   GemmArgs a = {};
@@ -688,6 +715,11 @@ cudaError_t launch_gemm_tcgen05_parts(const GemmProblem& p, int splits, float* p
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
   auto go = [&](auto kernel) {
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     return cudaLaunchKernelEx(&cfg, kernel, a);

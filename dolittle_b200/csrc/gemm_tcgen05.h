@@ -52,7 +52,10 @@ cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool 
 // `epilogue` into out (row stride ld), or writes the FP32 sum to sum_out.
 // Only p.x, p.ldx, p.w, M, N, K and err are read from p.
 int gemm_splitk_parts(int M, int N, int K, int sms);  // parts that fill the SMs
-cudaError_t launch_gemm_tcgen05_parts(const GemmProblem& p, int splits, float* parts, cudaStream_t stream);
+// pdl: programmatic dependent launch (weights stream in before the kernel
+// waits for its predecessor).
+cudaError_t launch_gemm_tcgen05_parts(const GemmProblem& p, int splits, float* parts, cudaStream_t stream,
+                                      bool pdl = false);
 cudaError_t launch_gemm_splitk_epilogue(const float* parts, int splits, int M, int N, int epilogue, bf16* out,
                                         int ld, float* sum_out, cudaStream_t stream);
 

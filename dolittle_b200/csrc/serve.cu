@@ -414,7 +414,7 @@ void Server::row_projection_out(const bf16* x, int ldx, const bf16* w, int M, in
     return;
   }
   const int parts = decode ? gemm_splitk_parts(M, N, K, sms_) : 1;
-  check(launch_gemm_tcgen05_parts(p, parts, parts_, stream_), "gemm parts");
+  check(launch_gemm_tcgen05_parts(p, parts, parts_, stream_, decode), "gemm parts");
   ++launches_;
   if (tp_ == 1) {
     check(launch_gemm_splitk_epilogue(parts_, parts, M, N, kGemmResidual, residual_, N, nullptr, stream_),
@@ -544,7 +544,9 @@ void Server::decode_body() {
     p.N = Q + 2 * G;
     p.K = D;
     int parts = gemm_splitk_parts(B, p.N, p.K, sms_);
-    check(launch_gemm_tcgen05_parts(p, parts, parts_, stream_), "qkv parts");
+    // The split-K projections are programmatic dependent launches: their
+    // weights stream in while the previous kernel finishes.
+    check(launch_gemm_tcgen05_parts(p, parts, parts_, stream_, true), "qkv parts");
     check(launch_gemm_splitk_epilogue(parts_, parts, B, p.N, kGemmStore, qkv_, p.N, nullptr, stream_), "qkv sum");
     check(launch_norm_rope_append_rows(qkv_, Q + 2 * G, y.q_norm, y.k_norm, inv_freq_, q_rot_, planes(l), position_,
                                        B, hq_, hkv_, d, cfg_.epsilon, stream_),
@@ -559,7 +561,7 @@ void Server::decode_body() {
     p.N = 2 * F;
     p.K = D;
     parts = gemm_splitk_parts(B, p.N, p.K, sms_);
-    check(launch_gemm_tcgen05_parts(p, parts, parts_, stream_), "gate/up parts");
+    check(launch_gemm_tcgen05_parts(p, parts, parts_, stream_, true), "gate/up parts");
     check(launch_gemm_splitk_epilogue(parts_, parts, B, p.N, kGemmSwiGLU, act_, F, nullptr, stream_), "swiglu");
     launches_ += 3;
     row_projection_out(act_, F, y.wd, B, F, true);

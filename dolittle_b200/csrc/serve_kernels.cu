@@ -237,6 +237,7 @@ __global__ void __launch_bounds__(kAdThreads) attention_decode_split_kernel(
 
 __global__ void attention_decode_combine_kernel(const float* __restrict__ ws, int query_heads, int splits,
                                                 bf16* __restrict__ out) {
+  allow_next();  // the o projection may request its weights meanwhile
   const int h = blockIdx.x, b = blockIdx.y, f = threadIdx.x;
   const float* w = ws + (size_t(b) * query_heads + h) * splits * kAdWs;
   float M = -INFINITY;
