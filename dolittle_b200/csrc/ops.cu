@@ -50,18 +50,18 @@ __global__ void qk_norm_rope_kernel(const bf16* __restrict__ q_raw, const bf16* 
   const int warp = threadIdx.x >> 5;
   const int r = blockIdx.x;
   const int p = row_position(pos, r);
-  // One block per row: the row's RoPE factors once, then the warps walk the
-  // heads.
+  // One warp per head (kNormWarps heads per block): the block computes its
+  // row's RoPE factors once for its heads.
   rope_factors(inv_freq, p, width, co, si);
   __syncthreads();
-  for (int head = warp; head < query_heads + kv_heads; head += kNormWarps) {
-    const bool is_q = head < query_heads;
-    const bf16* src = is_q ? q_raw + (size_t(r) * query_heads + head) * width
-                           : k_raw + (size_t(r) * kv_heads + (head - query_heads)) * width;
-    bf16* dst = is_q ? q_out + (size_t(r) * query_heads + head) * width
-                     : k_cache + (size_t(p) * kv_heads + (head - query_heads)) * width;
-    qk_norm_rope_warp_table(src, is_q ? qw : kw, co, si, dst, width, eps, vals[warp]);
-  }
+  const int head = blockIdx.y * kNormWarps + warp;
+  if (head >= query_heads + kv_heads) return;
+  const bool is_q = head < query_heads;
+  const bf16* src = is_q ? q_raw + (size_t(r) * query_heads + head) * width
+                         : k_raw + (size_t(r) * kv_heads + (head - query_heads)) * width;
+  bf16* dst = is_q ? q_out + (size_t(r) * query_heads + head) * width
+                   : k_cache + (size_t(p) * kv_heads + (head - query_heads)) * width;
+  qk_norm_rope_warp_table(src, is_q ? qw : kw, co, si, dst, width, eps, vals[warp]);
 }
 
 // ---------------------------------------------------------------------------
@@ -413,7 +413,9 @@ cudaError_t launch_qk_norm_rope(const bf16* q_raw, const bf16* k_raw, const bf16
                                 int kv_heads, int width, float eps, cudaStream_t stream, bool pdl) {
   if (width > 128 || width % 2) return cudaErrorInvalidValue;
   cudaLaunchAttribute attr[1];
-  auto cfg = make_config(dim3(rows), dim3(32 * kNormWarps), 0, stream, attr, pdl);
+  const int heads = query_heads + kv_heads;
+  auto cfg = make_config(dim3(rows, (heads + kNormWarps - 1) / kNormWarps), dim3(32 * kNormWarps), 0, stream, attr,
+                         pdl);
   return cudaLaunchKernelEx(&cfg, qk_norm_rope_kernel, q_raw, k_raw, q_norm_w, k_norm_w, inv_freq, q_out,
                             k_cache, pos, query_heads, kv_heads, width, eps);
 }
