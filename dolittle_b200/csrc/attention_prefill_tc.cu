@@ -2,16 +2,18 @@
 // fast prompt pass (tensor-core accumulation order, online softmax; checked
 // against the reference-order path within tolerance like the tcgen05 GEMMs).
 //
-// One CTA (4 warps) owns 128 query rows of one query head; thread r owns
-// query row r = TMEM lane r.  Key blocks of 128, one pass:
+// One CTA (4 x kRowSplit warps) owns 128 query rows of one query head; query
+// row r = TMEM lane r is shared by kRowSplit threads (warps w, w + 4, ...
+// reach the same TMEM lane group), each owning 128 / kRowSplit columns.  Key blocks of 128, one pass:
 //   S[kb] = Q K[kb]^T (tcgen05.mma, M = N = 128, K = 128 over the head width)
 //           into one of two TMEM score buffers;
-//   each thread reads its row of S, updates its running max m and sum l of
-//   exp2(s - m) (masked beyond the row's position), writes p = exp2(s - m)
-//   as BF16 into a 128-byte-swizzled K-major tile;
+//   each thread reads its part of the row of S; the parts exchange their max
+//   and sum through shared memory to update the row's running max m and sum
+//   l of exp2(s - m) (masked beyond the row's position); each writes its
+//   p = exp2(s - m) as BF16 into a 128-byte-swizzled K-major tile;
 //   O[kb] = P V[kb] (A = P, B = V^T) into TMEM; each thread rescales its
-//   register copy of the output row by exp2(m_old - m_new) and adds its row
-//   of O[kb]; the output is O / l at the end.
+//   register copy of its 64 output columns by exp2(m_old - m_new) and adds
+//   those of O[kb]; the output is O / l at the end.
 // K and V^T blocks stream through two TMA stages, and the next block's score
 // MMA is issued as soon as this block's P is written, so it overlaps the
 // output update.  Scores carry the softmax scale times log2(e).  Q and K come
@@ -32,7 +34,9 @@ namespace {
 using namespace tc;
 
 constexpr int kTile = 128;                    // query rows per CTA, keys per block
-constexpr int kThreads = 128;
+constexpr int kRowSplit = 2;                  // threads per query row
+constexpr int kThreads = kTile * kRowSplit;
+constexpr int kRowChunks = 4 / kRowSplit;     // 32-column chunks of S / O per thread
 constexpr int kAtomBytes = kTile * 64 * 2;    // [128 rows][64 BF16], one swizzle atom column
 constexpr int kTileBytes = 2 * kAtomBytes;    // [128 rows][128 BF16]
 constexpr int kSmem = 6 * kTileBytes + 1024;  // Q, 2 x K, 2 x V^T, P + alignment
@@ -85,6 +89,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const
   __shared__ uint64_t q_bar, kv_bar[2], s_bar[2], o_bar;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
+  __shared__ float red_max[kRowSplit][kTile], red_sum[kRowSplit][kTile];  // the parts of each row
   const uint32_t base_s = (smem_addr(smem_raw) + 1023u) & ~1023u;
   unsigned char* sq = smem_raw + (base_s - smem_addr(smem_raw));
   // Stage st: K at sq + (1 + st) tiles, V^T at sq + (3 + st) tiles.
@@ -95,7 +100,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const
   const int hq = blockIdx.y;
   const int g = hq / (a.query_heads / a.kv_heads);
   const int q0 = blockIdx.x * kTile;
-  const int r = threadIdx.x;  // row within the tile = TMEM lane
+  const int r = threadIdx.x & (kTile - 1);  // row within the tile = TMEM lane
+  const int h = threadIdx.x >> 7;           // columns [128 h / kRowSplit, 128 (h + 1) / kRowSplit)
   const int row = q0 + r;
   const bool live = row < a.rows;
   const long long pos = a.first + row;
@@ -123,7 +129,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const
   allow_next();
   wait_prior();
   const uint32_t t_o = tmem + 256;
-  const uint32_t lane_base = uint32_t(warp * 32) << 16;
+  const uint32_t lane_base = uint32_t((warp & 3) * 32) << 16;
 
   // Thread 0 issues every TMA load and MMA.
   auto load_kv = [&](int kb) {
@@ -154,9 +160,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const
   }
   __syncthreads();
 
-  float o[128];
+  float o[32 * kRowChunks];
 #pragma unroll
-  for (int i = 0; i < 128; ++i) o[i] = 0.f;
+  for (int i = 0; i < 32 * kRowChunks; ++i) o[i] = 0.f;
   float m = -INFINITY, l = 0.f;
   unsigned o_phase = 0;
   for (int kb = 0; kb < nkb && !abort_flag; ++kb) {
@@ -168,19 +174,23 @@ __global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const
     // every lane loads, only the arithmetic is guarded).
     float bm = -INFINITY;
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
+    for (int c = kRowChunks * h; c < kRowChunks * (h + 1); ++c) {
       uint32_t sv[32];
       tmem_ld32(t_s(st) + lane_base + uint32_t(c * 32), sv);
 #pragma unroll
       for (int i = 0; i < 32; ++i)
         if (key0 + c * 32 + i <= pos) bm = fmaxf(bm, __uint_as_float(sv[i]) * a.scale_log2);
     }
+    red_max[h][r] = bm;
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kRowSplit; ++j) bm = fmaxf(bm, red_max[j][r]);
     const float mn = fmaxf(m, bm);
     const bool use = live && mn != -INFINITY;
     const float alpha = (use && m != -INFINITY) ? exp2f(m - mn) : 0.f;
     float sum = 0.f;
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
+    for (int c = kRowChunks * h; c < kRowChunks * (h + 1); ++c) {
       uint32_t sv[32];
       tmem_ld32(t_s(st) + lane_base + uint32_t(c * 32), sv);
       uint32_t packed[16];
@@ -202,13 +212,17 @@ __global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const
             make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
       }
     }
-    if (use) {
-      l = l * alpha + sum;
-      m = mn;
-    }
+    red_sum[h][r] = sum;
     fence_proxy_async_smem();
     fence_before_sync();
     __syncthreads();  // P complete; S[st] consumed
+    if (use) {
+      float total = red_sum[0][r];
+#pragma unroll
+      for (int j = 1; j < kRowSplit; ++j) total += red_sum[j][r];
+      l = l * alpha + total;
+      m = mn;
+    }
     if (threadIdx.x == 0 && !abort_flag) {
       fence_after_sync();
       mma_tile(t_o, sp, svt(st), false);
@@ -228,9 +242,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const
     o_phase ^= 1;
     fence_after_sync();
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < kRowChunks; ++c) {
       uint32_t ov[32];
-      tmem_ld32(t_o + lane_base + uint32_t(c * 32), ov);
+      tmem_ld32(t_o + lane_base + uint32_t((kRowChunks * h + c) * 32), ov);
 #pragma unroll
       for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha, __uint_as_float(ov[i]));
     }
@@ -240,9 +254,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const
   }
   if (!abort_flag && live) {
     const float inv_l = l > 0.f ? 1.0f / l : 0.f;
-    bf16* out = a.out + size_t(row) * (size_t(a.query_heads) * 128) + size_t(hq) * 128;
+    bf16* out = a.out + size_t(row) * (size_t(a.query_heads) * 128) + size_t(hq) * 128 + 32 * kRowChunks * h;
 #pragma unroll
-    for (int c = 0; c < 16; ++c) {
+    for (int c = 0; c < 4 * kRowChunks; ++c) {
       uint32_t packed[4];
 #pragma unroll
       for (int i = 0; i < 8; i += 2) {
