@@ -250,10 +250,9 @@ def test_rotary_law_within_reference_tolerance():
             angle = f32(first + r) * freq
             c = nm.round_bf16(np.cos(angle, dtype=np.float32))
             s = nm.round_bf16(np.sin(angle, dtype=np.float32))
-            for h in range(heads):
-                a, b = x[r, h, i], x[r, h, i + width // 2]
-                expected[r, h, i] = nm.round_bf16(nm.round_bf16(a * c) - nm.round_bf16(b * s))
-                expected[r, h, i + width // 2] = nm.round_bf16(nm.round_bf16(b * c) + nm.round_bf16(a * s))
+            a, b = x[r, :, i], x[r, :, i + width // 2]
+            expected[r, :, i] = nm.round_bf16(nm.round_bf16(a * c) - nm.round_bf16(b * s))
+            expected[r, :, i + width // 2] = nm.round_bf16(nm.round_bf16(b * c) + nm.round_bf16(a * s))
     got = nm.bf16_bits_to_f32(oracle.rotary(nm.f32_to_bf16_bits(x), first, theta))
     assert nm.compare_elementwise(expected, got, *ORDINARY)["passed"]
 
