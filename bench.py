@@ -13,9 +13,12 @@ cache.  One "step" is one such generation (prompt pass + 256 decode passes).
   passes, CUDA events on the engine's stream), summed over ranks.
 * `e2e` = generated tokens/s measured around the public generate() call with
   host prompt IDs in and host token IDs out (copies inside the region).
-* `roofline` = the dominant kernel (the streaming decode GEMV on each block's
-  gate|up matrix, 24576 x 4096 BF16, 201.4 MB per launch) timed with CUDA
-  events on its own stream over 36 distinct matrices (inputs larger than L2).
+* `roofline` = the dominant kernel: the persistent decode kernel (one
+  cooperative launch per token, 15.23 GB of algorithmic bytes at the mean KV
+  length), timed with CUDA events on the engine's stream.  Nested under it,
+  `gemv_gate_up` = the stand-alone streaming GEMV on a gate|up matrix (24576 x
+  4096 BF16, 201.4 MB per launch) over 36 distinct matrices (inputs larger
+  than L2).
 * `cpu_baseline` = the CPU restatement of the reference laws (oracle/) timed
   on this host's cores on a bounded sample (2 decode passes of the full model).
 * `--impl reference` times the reference's host numerical path (the oracle
@@ -672,9 +675,12 @@ def run_profile_case(args):
     larger than L2), launched 4 times.  decode: a 36-block engine with a
     16-token prompt and 3 decode passes (one prefill chunk, then graphs).
     gemm: the four prompt-pass projections at M = 512 (qkv, o +residual,
-    gate|up +SwiGLU, down +residual; library-chosen tiling), 3 launches each.
+    gate|up +SwiGLU, down +residual; library-chosen tiling unless --gemm-tile
+    pins one; --gemm-shape picks one projection), 3 launches each.
     serve-attention: config 5's batched flash decoding (32 sequences x 8192
-    keys, 8 KV heads; 1.07 GB of cache), 4 launches."""
+    keys, 8 KV heads; 1.07 GB of cache), 4 launches.  sampler: batch-1
+    selections of one 151,936-entry BF16 logits row (4 categorical draws at
+    T 0.7 / top-p 0.9, then 2 greedy)."""
     import torch
     import dolittle_b200 as dl
     torch.cuda.set_device(0)
@@ -699,7 +705,12 @@ def run_profile_case(args):
     elif args.profile == "gemm":
         L = dl.lib()
         M = PROMPT
-        for N, K, epi in ((6144, 4096, 0), (4096, 4096, 1), (24576, 4096, 3), (4096, 12288, 1)):
+        shapes = {"qkv": (6144, 4096, 0), "o": (4096, 4096, 1), "gu": (24576, 4096, 3), "down": (4096, 12288, 1)}
+        # --gemm-tile TM,TN,PARTS pins the tiling (dl_gemm_bf16_config); default: the library's choice.
+        tile = [int(v) for v in args.gemm_tile.split(",")] if args.gemm_tile else None
+        for name, (N, K, epi) in shapes.items():
+            if args.gemm_shape not in ("all", name):
+                continue
             x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
             w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
             cols = N // 2 if epi == 3 else N
@@ -708,8 +719,13 @@ def run_profile_case(args):
             n_t = ((M + 127) // 128) * (N // 128)
             tickets = torch.zeros(n_t, device="cuda", dtype=torch.int32)
             for _ in range(3):
-                assert L.dl_gemm_bf16_split(x.data_ptr(), K, w.data_ptr(), y.data_ptr(), cols, M, N, K, epi, None,
-                                            ws.data_ptr(), tickets.data_ptr(), n_t) == 0, L.dl_last_error()
+                if tile:
+                    rc = L.dl_gemm_bf16_config(x.data_ptr(), K, w.data_ptr(), y.data_ptr(), cols, M, N, K, epi, None,
+                                               ws.data_ptr(), tickets.data_ptr(), n_t, tile[0], tile[1], tile[2])
+                else:
+                    rc = L.dl_gemm_bf16_split(x.data_ptr(), K, w.data_ptr(), y.data_ptr(), cols, M, N, K, epi, None,
+                                              ws.data_ptr(), tickets.data_ptr(), n_t)
+                assert rc == 0, L.dl_last_error()
             torch.cuda.synchronize()
         print("profile gemm ok")
     elif args.profile == "serve-attention":
@@ -727,6 +743,27 @@ def run_profile_case(args):
                                                  B, Hq, Hkv, cap, out.data_ptr(), ws.data_ptr(), None) == 0
         torch.cuda.synchronize()
         print("profile serve-attention ok")
+    elif args.profile == "sampler":
+        # Batch-1 selections of one full-vocabulary BF16 logits row: 4
+        # categorical draws with config 3's settings (T 0.7, top-p 0.9,
+        # device MT19937-64 stream seeded 7), then 2 greedy selections.
+        import ctypes as C
+        L = dl.lib()
+        V = dl.QWEN3_8B.vocabulary
+        logits = (torch.randn(V, device="cuda") * 3.0).to(torch.bfloat16)
+        h = C.c_void_p()
+        assert L.dl_sampler_create(V, dl.DL_BF16, C.byref(h)) == 0
+        res = C.c_void_p()
+        cat = dl.Settings(dl.SelectionMode.categorical, 0.7, 0, 0.9).c()
+        assert L.dl_sampler_start(h, C.byref(cat), 7, None, 0, None) == 0
+        for _ in range(4):
+            assert L.dl_sampler_submit_next(h, logits.data_ptr(), None, C.byref(res)) == 0
+        greedy = dl.Settings().c()
+        for _ in range(2):
+            assert L.dl_sampler_submit(h, logits.data_ptr(), C.byref(greedy), 0, None, C.byref(res)) == 0
+        torch.cuda.synchronize()
+        L.dl_sampler_destroy(h)
+        print("profile sampler ok")
     elif args.profile == "prefill":
         cfg = dl.QWEN3_8B
         e = dl.Engine(cfg, capacity=PROMPT + 8, max_rows=PROMPT)
@@ -753,9 +790,12 @@ def main():
                     help="reference arm: skip timing the reference's CUDA kernels on the GPU")
     ap.add_argument("--prefill", choices=["fast", "parity"], default="fast",
                     help="prompt pass on the tcgen05 GEMMs (fast) or in the reference order (parity)")
-    ap.add_argument("--profile", choices=["gemv", "decode", "prefill", "persist", "gemm", "serve-attention"],
+    ap.add_argument("--profile", choices=["gemv", "decode", "prefill", "persist", "gemm", "serve-attention", "sampler"],
                     default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
+    ap.add_argument("--gemm-shape", choices=["all", "qkv", "o", "gu", "down"], default="all",
+                    help="--profile gemm: one prompt-pass projection only")
+    ap.add_argument("--gemm-tile", default="", help="--profile gemm: TM,TN,PARTS tiling (e.g. 256,256,1)")
     ap.add_argument("--workload", choices=["decode", "serve", "steer", "nla"], default="decode",
                     help="decode: config 2 (headline); serve: config 5 batched serving, TP over the ranks; "
                          "steer / nla: configs 3 / 4, units split over the ranks")

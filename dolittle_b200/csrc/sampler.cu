@@ -44,6 +44,7 @@ struct Layout {
   uint2* keys_b;
   double* prefix;
   unsigned* counts;
+  unsigned* digit_totals;
   double* tile_totals;
   uint4* best;
   ScanState* scan;
@@ -63,6 +64,7 @@ Layout layout(void* arena, size_t n) {
   L.keys_b = reinterpret_cast<uint2*>(b + o); o = align_up(o + n * 8, 256);
   L.prefix = reinterpret_cast<double*>(b + o); o = align_up(o + n * 8, 256);
   L.counts = reinterpret_cast<unsigned*>(b + o); o = align_up(o + blocks * kW * 4, 256);
+  L.digit_totals = reinterpret_cast<unsigned*>(b + o); o = align_up(o + kW * 4, 256);
   L.tile_totals = reinterpret_cast<double*>(b + o); o = align_up(o + blocks * 8, 256);
   L.best = reinterpret_cast<uint4*>(b + o); o = align_up(o + blocks * 16, 256);
   L.scan = reinterpret_cast<ScanState*>(b + o); o = align_up(o + sizeof(ScanState), 256);
@@ -232,44 +234,37 @@ __global__ void histogram_kernel(const uint2* keys, unsigned n, unsigned shift, 
   counts[blockIdx.x * kW + threadIdx.x] = total;
 }
 
-// Exclusive offsets in (digit, block) order: offset[b][d] = (sum of all
-// counts of digits < d) + (sum of counts[b' < b][d]).  Integer sums, so any
-// order gives the same offsets; one CTA per row, four block segments per
-// digit, loads batched ahead of the stores.
-constexpr unsigned kSeg = 4;
-__global__ void __launch_bounds__(kW * kSeg) digit_offsets_kernel(unsigned* counts, unsigned blocks, size_t stride) {
-  __shared__ unsigned seg[kSeg][kW];
-  __shared__ unsigned digit_base[kW];
-  __shared__ unsigned warp_sum[kWarps];
+// Radix offsets, in two halves.  This kernel turns each digit column of the
+// per-block counts into its exclusive prefix over the blocks, in place
+// (counts[b][d] = keys with digit d in blocks b' < b), and writes the
+// column's total to totals[d]; the scatter adds the exclusive scan of the
+// totals over the digits.  Offsets are integer sums, so any order gives the
+// same stable sort.  CTA g owns digits 32g .. 32g+31 (lane = digit, so a warp
+// load is one 128-byte line of a block's counts) and warp w owns block segment
+// w of kOffsetWarps, so the column walks run on kW / 32 CTAs side by side.
+constexpr unsigned kOffsetWarps = 32;
+__global__ void __launch_bounds__(32 * kOffsetWarps)
+    digit_offsets_kernel(unsigned* counts, unsigned* totals, unsigned blocks, size_t stride) {
+  __shared__ unsigned seg[kOffsetWarps][32];
   counts = at_row(counts, stride);
-  const unsigned d = threadIdx.x % kW, q = threadIdx.x / kW;
-  const unsigned per = (blocks + kSeg - 1) / kSeg;
-  const unsigned b0 = min(blocks, q * per), b1 = min(blocks, b0 + per);
+  totals = at_row(totals, stride);
+  const unsigned lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const unsigned d = blockIdx.x * 32 + lane;
+  const unsigned per = (blocks + kOffsetWarps - 1) / kOffsetWarps;
+  const unsigned b0 = min(blocks, w * per), b1 = min(blocks, b0 + per);
   unsigned sum = 0;
-#pragma unroll 8
-  for (unsigned b = b0; b < b1; ++b) sum += counts[b * kW + d];
-  seg[q][d] = sum;
-  __syncthreads();
-  unsigned before = 0;
-  for (unsigned k = 0; k < q; ++k) before += seg[k][d];
-  if (q == 0) {
-    // Exclusive scan of the 256 digit totals.
-    unsigned total = 0;
-    for (unsigned k = 0; k < kSeg; ++k) total += seg[k][d];
-    unsigned v = total;
-    const unsigned lane = d & 31, warp = d >> 5;
-    for (unsigned off = 1; off < 32; off <<= 1) {
-      const unsigned o = __shfl_up_sync(0xffffffffu, v, off);
-      if (lane >= off) v += o;
-    }
-    if (lane == 31) warp_sum[warp] = v;
-    __syncwarp();
-    digit_base[d] = v - total;  // exclusive inside the warp; warp bases added below
+  for (unsigned b = b0; b < b1; b += 8) {
+    unsigned c[8];
+#pragma unroll
+    for (unsigned k = 0; k < 8; ++k) c[k] = b + k < b1 ? counts[(b + k) * kW + d] : 0u;
+#pragma unroll
+    for (unsigned k = 0; k < 8; ++k) sum += c[k];
   }
+  seg[w][lane] = sum;
   __syncthreads();
-  unsigned base = digit_base[d];
-  for (unsigned w = 0; w < (d >> 5); ++w) base += warp_sum[w];
-  unsigned run = base + before;
+  unsigned run = 0;
+  for (unsigned k = 0; k < w; ++k) run += seg[k][lane];
+  if (w == kOffsetWarps - 1) totals[d] = run + sum;
   for (unsigned b = b0; b < b1; b += 8) {
     unsigned c[8];
 #pragma unroll
@@ -284,11 +279,30 @@ __global__ void __launch_bounds__(kW * kSeg) digit_offsets_kernel(unsigned* coun
 }
 
 __global__ void scatter_kernel(const uint2* in, uint2* out, unsigned n, unsigned shift, const unsigned* offsets,
-                               size_t stride) {
+                               const unsigned* totals, size_t stride) {
   __shared__ unsigned bins[kWarps][kW];
+  __shared__ unsigned digit_base[kW];
+  __shared__ unsigned warp_sum[kWarps];
   in = at_row(in, stride);
   out = at_row(out, stride);
   offsets = at_row(offsets, stride);
+  totals = at_row(totals, stride);
+  {
+    // digit_base[d] = keys with a digit below d: exclusive scan of the
+    // digit totals (thread = digit; warp scans, then the warp sums).
+    const unsigned t = totals[threadIdx.x], ln = threadIdx.x & 31, wp = threadIdx.x >> 5;
+    unsigned v = t;
+    for (unsigned off = 1; off < 32; off <<= 1) {
+      const unsigned o = __shfl_up_sync(0xffffffffu, v, off);
+      if (ln >= off) v += o;
+    }
+    if (ln == 31) warp_sum[wp] = v;
+    __syncthreads();
+    unsigned before = 0;
+    for (unsigned k = 0; k < wp; ++k) before += warp_sum[k];
+    digit_base[threadIdx.x] = before + v - t;
+  }
+  // (block_digit_ranks starts with a CTA barrier, which publishes digit_base.)
   const unsigned i = blockIdx.x * kW + threadIdx.x;
   const bool live = i < n;
   const uint2 k = live ? in[i] : make_uint2(0, 0);
@@ -299,7 +313,7 @@ __global__ void scatter_kernel(const uint2* in, uint2* out, unsigned n, unsigned
   const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   unsigned rank = __popc(peers & ((1u << lane) - 1u));
   for (unsigned w = 0; w < warp; ++w) rank += bins[w][digit];
-  out[offsets[blockIdx.x * kW + digit] + rank] = k;
+  out[digit_base[digit] + offsets[blockIdx.x * kW + digit] + rank] = k;
 }
 
 __global__ void weights_kernel(const void* row, bool bf16_in, const uint2* sorted, unsigned keep,
@@ -446,6 +460,7 @@ size_t sampler_required_bytes(size_t n) {
   o = align_up(o + n * 8, 256);
   o = align_up(o + n * 8, 256);
   o = align_up(o + blocks * kW * 4, 256);
+  o = align_up(o + kW * 4, 256);
   o = align_up(o + blocks * 8, 256);
   o = align_up(o + blocks * 16, 256);
   o = align_up(o + sizeof(ScanState), 256);
@@ -508,8 +523,8 @@ cudaError_t sampler_submit(Sampler& s, const void* row, const dl_sampling& st, u
     uint2* out = L.keys_b;
     for (unsigned shift = s.bf16_input ? 16 : 0; shift < 32; shift += 8) {
       histogram_kernel<<<dim3(blocks, R), kW, 0, stream>>>(in, n, shift, L.counts, S);
-      digit_offsets_kernel<<<dim3(1, R), kW * kSeg, 0, stream>>>(L.counts, blocks, S);
-      scatter_kernel<<<dim3(blocks, R), kW, 0, stream>>>(in, out, n, shift, L.counts, S);
+      digit_offsets_kernel<<<dim3(kW / 32, R), 32 * kOffsetWarps, 0, stream>>>(L.counts, L.digit_totals, blocks, S);
+      scatter_kernel<<<dim3(blocks, R), kW, 0, stream>>>(in, out, n, shift, L.counts, L.digit_totals, S);
       uint2* t = in;
       in = out;
       out = t;
