@@ -215,7 +215,8 @@ class _Sampler:
 
 
 @needs_ref
-@pytest.mark.parametrize("n", [1, 513, 151936])
+# 8449 keys = 33 radix blocks + 1: uneven block segments in the offset scan.
+@pytest.mark.parametrize("n", [1, 513, 8449, 151936])
 @pytest.mark.parametrize("bf16", [True, False])
 def test_sampler_matches_reference_device_sampler(n, bf16):
     logits = _device_cases(n)
