@@ -45,6 +45,17 @@ sys.path.insert(0, ROOT)
 
 PROMPT, DECODE, SEED = 512, 256, 1
 METRIC = "Qwen3-8B bf16 decode tok/s (batch 1, % HBM roofline); prefill tok/s"
+WORKLOAD = ("Qwen3-8B config 2: 36 blocks, V=151936, prompt 512, 256 greedy decode steps, batch 1, "
+            "fresh KV cache per step")
+# Config-5-shaped tensor-parallel record added under --gpus N > 1.
+TP_BATCH, TP_PROMPT, TP_STEPS = 32, 2048, 32
+REFERENCE_TOKENS = os.path.join(ROOT, "tests", "golden", "config2_reference_tokens.json")
+
+
+def config_record(world):
+    """The workload description both arms print (the driver compares them)."""
+    return {"workload": WORKLOAD, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "l2": "weights (16.4 GB) exceed L2; streamed once per decode pass"}
 
 
 def peaks():
@@ -279,8 +290,7 @@ def run_reference(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random-init weights, uniform prompt IDs)",
-            "config": {"workload": "Qwen3-8B config 2 decode (batch 1), one decode pass per step on host cores",
-                       "prompt": PROMPT, "decode_steps": DECODE},
+            "config": config_record(world),
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": oracle.lib().or_max_threads(),
                              "kind": "port",
                              "sample": f"{args.steps} timed decode passes (after {args.warmup} warm-up) of full "
@@ -340,6 +350,151 @@ def persistent_traffic(bytes_per_launch):
     return bytes_per_launch * rec["traffic_bytes"] / rec["algorithmic_bytes"]
 
 
+def pipeline_agreement(engine, cfg, prompt, timed_gen, fast):
+    """How the benchmarked pipeline agrees with the token-identical one.
+
+    The parity pipeline (reference-order prompt pass + persistent decode) is
+    bit-identical to the reference's own kernels (the GPU test suite checks
+    its full config-2 generation token for token); the committed reference
+    sequence (tests/golden/config2_reference_tokens.json, made by the
+    reference kernels on a B200) is compared here directly.  Per block: the
+    prompt pass's output rows of both modes (block observation), cosine,
+    relative L2 and max-abs against the 36-block BF16 tolerance
+    (max-abs <= 0.0625 x peak, rel-L2 <= 0.03).  Also times the parity
+    pipeline: its prompt pass and an end-to-end generation."""
+    import torch
+    import dolittle_b200 as dl
+    L, D, P = cfg.layers, cfg.hidden, PROMPT
+    obs = {}
+    for name, mode in (("parity", dl.DL_PREFILL_PARITY), ("fast", dl.DL_PREFILL_FAST)):
+        rows = torch.zeros((L, P, D), dtype=torch.int16, device="cuda")
+        engine.reset()
+        engine.set_observation(rows.data_ptr(), P)
+        try:
+            logits = engine.consume_view(prompt, mode)
+        finally:
+            engine.set_observation(None)
+        obs[name] = (rows.view(torch.bfloat16), torch.from_numpy(logits.view(np.int16)).view(torch.bfloat16))
+
+    def compare(e, a):
+        e, a = e.double().reshape(-1), a.double().reshape(-1)
+        d = a - e
+        peak = float(e.abs().max())
+        max_abs = float(d.abs().max())
+        rel = float(d.norm() / e.norm())
+        cos = float((e @ a) / (e.norm() * a.norm()))
+        return {"cosine": cos, "rel_l2": rel, "max_abs": max_abs,
+                "within_tolerance": max_abs <= max(1e-4, 0.0625 * peak) and rel <= 0.03}
+
+    blocks = [compare(obs["parity"][0][l], obs["fast"][0][l]) for l in range(L)]
+    worst = min(range(L), key=lambda l: blocks[l]["cosine"])
+    rec = {"reference": "parity pipeline (bit-identical to the reference kernels)",
+           "worst_block": worst, "worst_block_cosine": blocks[worst]["cosine"],
+           "worst_block_rel_l2": max(b["rel_l2"] for b in blocks),
+           "blocks_within_tolerance": sum(b["within_tolerance"] for b in blocks),
+           "prompt_logits": compare(obs["parity"][1], obs["fast"][1]),
+           "capture_block24_last_row": compare(obs["parity"][0][24][P - 1], obs["fast"][0][24][P - 1])}
+    del obs
+    # The parity pipeline, timed: one warm-up generation, then one timed.
+    engine.generate(prompt, DECODE + 1, prefill=dl.DL_PREFILL_PARITY)
+    torch.cuda.synchronize()
+    t = time.perf_counter()
+    g = engine.generate(prompt, DECODE + 1, prefill=dl.DL_PREFILL_PARITY)
+    wall = time.perf_counter() - t
+    parity_tokens, fast_tokens = g.tokens, timed_gen.tokens
+    first_diff = next((i for i, (a, b) in enumerate(zip(parity_tokens, fast_tokens)) if a != b), len(fast_tokens))
+    rec["agreement_len"] = first_diff if fast else len(fast_tokens)
+    rec["generated"] = len(fast_tokens)
+    fixture = None
+    if os.path.exists(REFERENCE_TOKENS):
+        with open(REFERENCE_TOKENS) as f:
+            fixture = json.load(f)
+    if fixture is not None and fixture["prompt"] == [int(v) for v in prompt] and fixture["seed"] == SEED:
+        want = fixture["tokens"]
+        rec["parity_tokens_identical_to_reference"] = parity_tokens == want
+        rec["agreement_len_vs_reference"] = next(
+            (i for i, (a, b) in enumerate(zip(want, fast_tokens)) if a != b), len(fast_tokens))
+    parity = {"prefill_tok_s": PROMPT / (g.prefill_ms / 1000.0),
+              "decode_tok_s": g.decode_steps / (g.decode_ms / 1000.0),
+              "e2e": {"value": (DECODE + 1) / wall, "unit": "tok/s",
+                      "what": "generate() with the parity prompt pass: host IDs in/out, prompt pass + decode"}}
+    return rec, parity
+
+
+def serve_measure(world, rank, local, dist, batch, prompt_len, steps, calls, warmup, hbm, tflops, kind):
+    """Config-5-shaped batched serving, tensor-parallel over KV-head groups
+    across the launched ranks: prefill of `batch` prompts, then `calls` timed
+    decode calls of `steps` steps each (device time, max over ranks)."""
+    import torch
+    import dolittle_b200 as dl
+    from dolittle_b200 import replicas
+    from dolittle_b200.serve import Server, connect_group
+    cfg = dl.QWEN3_8B
+    pg = dist is not None and world > 1
+    srv = Server(cfg, batch=batch, capacity=prompt_len + steps * (calls + warmup) + 8, chunk_rows=2048,
+                 device=local, tp_rank=rank, tp_size=world)
+    try:
+        srv.init_random(SEED, 0.02)
+        if pg:
+            connect_group(srv, dist)
+        V = cfg.vocabulary
+        rng = np.random.default_rng(SEED + 5)
+        prompts = rng.integers(0, V, size=(batch, prompt_len), dtype=np.uint32)
+        settings = dl.Settings(dl.SelectionMode.categorical, temperature=0.8, top_p=0.95)
+        t0 = time.perf_counter()
+        srv.prefill(prompts, settings, seed=7)
+        wall_prefill = time.perf_counter() - t0
+        first = srv.decode(steps)  # warm-up: graph capture and the first steps
+        for _ in range(warmup - 1):
+            srv.decode(steps)
+        torch.cuda.synchronize()
+        if pg:
+            dist.barrier()
+        torch.cuda.synchronize()
+        clocks = Clocks(local)
+        outs = []
+        t1 = time.perf_counter()
+        for _ in range(calls):
+            outs.append(srv.decode(steps))
+        wall = time.perf_counter() - t1
+        torch.cuda.synchronize()
+        if pg:
+            dist.barrier()
+        clk = clocks.stop()
+        decode_s = sum(o.decode_ms for o in outs) / 1000.0
+        prefill_s = first.prefill_ms / 1000.0
+        decode_s, prefill_s, wall = replicas.max_over_ranks(dist if pg else None, [decode_s, prefill_s, wall])
+        total_steps = calls * steps
+        Dm, Lm, d = cfg.hidden, cfg.layers, cfg.head_width
+        w_layer = Dm * (cfg.query_heads * d + 2 * cfg.kv_heads * d) + cfg.query_heads * d * Dm + 3 * Dm * cfg.mlp_width
+        weights = 2 * (Lm * w_layer / world + Dm * V)
+        S0 = prompt_len + warmup * steps
+        mean_S = S0 + total_steps / 2.0
+        kv_bytes = batch * mean_S * Lm * 2 * (cfg.kv_heads // world) * d * 2
+        step_bytes = weights + kv_bytes
+        ms_step = 1000 * decode_s / total_steps
+        achieved = step_bytes / (ms_step * 1e-3) / 1e9
+        pf_flops = batch * prefill_flops(prompt_len) / world
+        return {
+            "tp": world, "batch": batch, "prompt": prompt_len, "decode_steps_timed": total_steps,
+            "decode_tok_s": batch * total_steps / decode_s, "decode_tok_s_per_gpu": batch * total_steps / decode_s / world,
+            "ms_per_decode_step": ms_step,
+            "prefill_tok_s": batch * prompt_len / prefill_s,
+            "prefill_tok_s_per_gpu": batch * prompt_len / prefill_s / world,
+            "prefill_roofline": {"bound": "tensor", "achieved": pf_flops / prefill_s / 1e12, "peak": tflops,
+                                 "unit": "TFLOP/s", "frac": pf_flops / prefill_s / 1e12 / tflops},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "bytes_per_step_per_gpu": step_bytes, "peak_kind": kind,
+                         "kernel": "decode step graph (split-K tcgen05 GEMMs + flash decoding + sampling)"},
+            "e2e_decode_tok_s": batch * total_steps / wall,
+            "kernels_per_decode_step": outs[0].kernels_per_decode_step,
+            "gpu_launches": outs[0].kernels_per_decode_step * total_steps,
+            "wall_prefill_s": wall_prefill, "clocks": clk,
+        }
+    finally:
+        srv.close()
+
+
 def run_ours(args):
     world, rank, local = dist_setup()
     import torch
@@ -383,6 +538,9 @@ def run_ours(args):
     step_s = decode_s + prefill_s
     # The job lasts as long as its slowest replica.
     decode_s, prefill_s, wall_s, step_s = replicas.max_over_ranks(dist, [decode_s, prefill_s, wall_s, step_s])
+    agreement = parity = None
+    if rank == 0 and not args.no_agreement:
+        agreement, parity = pipeline_agreement(engine, cfg, prompt, gens[-1], fast)
     steps_decoded = gens[0].decode_steps
     tokens = world * args.steps * steps_decoded
     value = tokens / decode_s
@@ -410,6 +568,11 @@ def run_ours(args):
             cpu = cpu_decode_sample(from_engine)
     if dist is not None:
         dist.barrier()
+    tp = None
+    if world > 1 and not args.no_tp:
+        # Tensor parallelism over all launched ranks on a config-5-shaped batch.
+        engine.close()
+        tp = serve_measure(world, rank, local, dist, TP_BATCH, TP_PROMPT, TP_STEPS, 2, 1, hbm, tflops, kind)
     if rank == 0:
         prefill_tok_s = world * args.steps * PROMPT / prefill_s
         line = {
@@ -417,12 +580,9 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": 1000 * step_s / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random-init BF16 weights ~N(0,0.02), uniform prompt IDs)",
-            "config": {"workload": "Qwen3-8B config 2: 36 blocks, V=151936, prompt 512, 256 greedy decode steps, "
-                                   "batch 1, fresh KV cache per step",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                       "prefill": ("fast: tcgen05/TMEM GEMMs, one 512-row chunk" if fast
-                                   else "parity: reference reduction order, 8-row chunks"),
-                       "l2": "weights (16.4 GB) exceed L2; streamed once per decode pass"},
+            "config": config_record(world),
+            "prefill_mode": ("fast: tcgen05/TMEM GEMMs, one 512-row chunk" if fast
+                             else "parity: reference reduction order, 8-row chunks"),
             "decode_tok_s_per_gpu": per_rank,
             "prefill_tok_s": prefill_tok_s,
             # Per GPU (each replica runs its own prompt pass; prefill_s is the max over ranks).
@@ -436,14 +596,22 @@ def run_ours(args):
             "decode_bytes_per_token": bytes_step,
             "roofline": roof,
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": "generated tok/s (prompt pass + decode, host IDs in/out)",
+            "e2e": {"value": e2e_value, "unit": "tok/s",
+                    "what": "generated tokens per second through generate(): prompt pass + decode, host IDs in/out",
                     "h2d_bytes_per_step": PROMPT * 4 + cfg.vocabulary + 64,
                     "d2h_bytes_per_step": (DECODE + 1) * 4 + 64},
             "gpu_launches": sum(g.kernels_total for g in gens),
             "kernels_per_decode_step": gens[0].kernels_per_decode_step,
             "clocks": clk,
             "tokens_check": gens[0].tokens[:8],
+            "agreement": agreement,
+            "parity_pipeline": parity,
         }
+        if parity is not None:
+            line["prefill_parity_tok_s"] = parity["prefill_tok_s"]
+            line["e2e_parity"] = parity["e2e"]
+        if tp is not None:
+            line["tp"] = tp
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.destroy_process_group()
@@ -459,91 +627,34 @@ def run_serve(args):
     torch.cuda.set_device(local)
     import torch.distributed as dist
     from datetime import timedelta
-    import numpy as np
-    import dolittle_b200 as dl
-    from dolittle_b200 import replicas
-    from dolittle_b200.serve import Server, connect_group
     pg = world > 1
     if pg:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300))
     hbm, tflops, kind = peaks()
-    cfg = dl.QWEN3_8B
     B, P, steps = args.serve_batch, args.serve_prompt, args.serve_steps
-    srv = Server(cfg, batch=B, capacity=P + steps * (args.steps + args.warmup) + 8, chunk_rows=2048, device=local,
-                 tp_rank=rank, tp_size=world)
-    srv.init_random(SEED, 0.02)
-    if pg:
-        connect_group(srv, dist)
-    V = cfg.vocabulary
-    rng = np.random.default_rng(SEED + 5)
-    prompts = rng.integers(0, V, size=(B, P), dtype=np.uint32)
-    settings = dl.Settings(dl.SelectionMode.categorical, temperature=0.8, top_p=0.95)
-    t0 = time.perf_counter()
-    srv.prefill(prompts, settings, seed=7)
-    wall_prefill = time.perf_counter() - t0
-    first = srv.decode(steps)  # warm-up: graph capture and the first steps
-    for _ in range(args.warmup - 1):
-        srv.decode(steps)
-
-    def barrier():
-        torch.cuda.synchronize()
-        if pg:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    clocks = Clocks(local)
-    barrier()
-    outs = []
-    t1 = time.perf_counter()
-    for _ in range(args.steps):
-        outs.append(srv.decode(steps))
-    wall = time.perf_counter() - t1
-    barrier()
-    clk = clocks.stop()
-    decode_s = sum(o.decode_ms for o in outs) / 1000.0
-    prefill_s = first.prefill_ms / 1000.0
-    decode_s, prefill_s, wall = replicas.max_over_ranks(dist if pg else None, [decode_s, prefill_s, wall])
-    total_steps = args.steps * steps
-    value = B * total_steps / decode_s
+    r = serve_measure(world, rank, local, dist if pg else None, B, P, steps, args.steps, args.warmup, hbm, tflops,
+                      kind)
     if rank == 0:
-        # Bytes one decode step must move per GPU: this rank's weights plus its
-        # KV heads of every sequence (mean context over the timed steps).
-        Dm, Lm = cfg.hidden, cfg.layers
-        d = cfg.head_width
-        w_layer = Dm * (cfg.query_heads * d + 2 * cfg.kv_heads * d) + cfg.query_heads * d * Dm + 3 * Dm * cfg.mlp_width
-        weights = 2 * (Lm * w_layer / world + Dm * V)
-        S0 = P + (1 + args.warmup) * steps
-        mean_S = S0 + total_steps / 2.0
-        kv_bytes = B * mean_S * Lm * 2 * (cfg.kv_heads // world) * d * 2
-        step_bytes = weights + kv_bytes
-        ms_step = 1000 * decode_s / total_steps
-        achieved = step_bytes / (ms_step * 1e-3) / 1e9
-        pf_flops = B * prefill_flops(P) / world
         line = {
-            "metric": "Qwen3-8B batched serving decode tok/s (config 5)", "value": value, "unit": "tok/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "metric": "Qwen3-8B batched serving decode tok/s (config 5)", "value": r["decode_tok_s"],
+            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": r["ms_per_decode_step"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random-init BF16 weights ~N(0,0.02), uniform prompt IDs)",
             "config": {"workload": f"Qwen3-8B config 5: batch {B}, prompts of {P} uniform IDs, decode at "
                                    f"temperature 0.8 / top-p 0.95, {steps} decode steps per timed call",
-                       "parallelism": f"tp{world} over KV-head groups (NCCL all-reduce after o_proj, down_proj)"
+                       "parallelism": f"tp{world} over KV-head groups (all-reduce after o_proj, down_proj)"
                                       if world > 1 else "single GPU",
                        "l2": "weights + KV cache (tens of GB) exceed L2"},
-            "prefill_tok_s": B * P / prefill_s,
-            "prefill_roofline": {"bound": "tensor", "achieved": pf_flops / prefill_s / 1e12, "peak": tflops,
-                                 "unit": "TFLOP/s", "frac": pf_flops / prefill_s / 1e12 / tflops},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                         "traffic": None, "bytes_per_step_per_gpu": step_bytes, "peak_kind": kind,
-                         "kernel": "decode step graph (split-K tcgen05 GEMMs + flash decoding + sampling)"},
-            "e2e": {"value": B * total_steps / wall, "unit": "tok/s (host loop incl. token readback)",
-                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": B * 4},
-            "gpu_launches": outs[0].kernels_per_decode_step * total_steps,
-            "kernels_per_decode_step": outs[0].kernels_per_decode_step,
-            "wall_prefill_s": wall_prefill,
-            "clocks": clk,
+            "prefill_tok_s": r["prefill_tok_s"], "prefill_roofline": r["prefill_roofline"],
+            "roofline": dict(r["roofline"], traffic=None),
+            "e2e": {"value": r["e2e_decode_tok_s"], "unit": "tok/s",
+                    "what": "host decode loop incl. token readback", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": B * 4},
+            "gpu_launches": r["gpu_launches"], "kernels_per_decode_step": r["kernels_per_decode_step"],
+            "wall_prefill_s": r["wall_prefill_s"], "clocks": r["clocks"],
         }
         print(json.dumps(line), flush=True)
-    srv.close()
     if pg:
         dist.barrier()
         dist.destroy_process_group()
@@ -653,8 +764,8 @@ def run_branches(args):
                        else ("config 4: 64-token prefix with the injected marker row, 16 samples x 128 tokens "
                              "at T 1.0, then the reconstructor on each sample"),
                        "parallelism": f"replicas x{world} over the {n_units} independent units"},
-            "e2e": {"value": tokens / wall, "unit": "tok/s (host loop, prompt passes"
-                    + (")" if steer else " and reconstructions)"),
+            "e2e": {"value": tokens / wall, "unit": "tok/s",
+                    "what": "host loop incl. prompt passes" + ("" if steer else " and reconstructions"),
                     "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "prefill_s": prefill_s,
             "clocks": clk,
@@ -786,6 +897,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-agreement", action="store_true",
+                    help="skip the fast-vs-parity pipeline comparison and the parity pipeline timing")
+    ap.add_argument("--no-tp", action="store_true", help="N > 1: skip the tensor-parallel config-5-shaped record")
     ap.add_argument("--no-ref-gpu", action="store_true",
                     help="reference arm: skip timing the reference's CUDA kernels on the GPU")
     ap.add_argument("--prefill", choices=["fast", "parity"], default="fast",

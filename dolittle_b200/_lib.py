@@ -91,6 +91,7 @@ SIGNATURES = {
     "dl_sampler_submit_next": (C.c_int, [vp, vp, vp, C.POINTER(vp)]),
     "dl_intervene": (C.c_int, [vp, vp, vp, vp, sz, sz, sz, C.c_float, vp]),
     "dl_normalize_injection": (C.c_int, [vp, vp, vp, vp, sz, C.c_float, vp]),
+    "dl_direction": (C.c_int, [C.c_int, vp, vp, sz, vp, vp, vp]),
     "dl_engine_tensor_count": (sz, [C.POINTER(ModelConfig)]),
     "dl_engine_tensor_shape": (C.c_int, [C.POINTER(ModelConfig), sz, C.POINTER(sz), C.POINTER(sz)]),
     "dl_engine_create": (C.c_int, [C.POINTER(ModelConfig), C.c_int, sz, sz, C.POINTER(vp)]),
@@ -104,6 +105,7 @@ SIGNATURES = {
     "dl_engine_position": (sz, [vp]),
     "dl_engine_set_capture": (C.c_int, [vp, C.c_int]),
     "dl_engine_read_capture": (C.c_int, [vp, sz, sz, u16p]),
+    "dl_engine_set_observation": (C.c_int, [vp, vp, sz]),
     "dl_engine_set_intervention": (C.c_int, [vp, C.c_int, sz, C.c_float, C.POINTER(C.c_float)]),
     "dl_engine_set_decode_path": (C.c_int, [vp, C.c_int]),
     "dl_engine_set_injection": (C.c_int, [vp, C.c_int64, u16p, C.c_float]),

@@ -22,7 +22,10 @@
 //    array: serialize them.
 //  * the first call on each device looks up the array's device address with
 //    cudaGetSymbolAddress while that device is current; make that first call
-//    before any stream capture.
+//    before any stream capture.  The address is kept for the life of the
+//    process, so calls must not span a cudaDeviceReset (which unloads the
+//    library's device module and may move the array).
+#include <climits>
 #include <mutex>
 #include <string>
 
@@ -74,13 +77,19 @@ DL_API dl_status dl_attention_fixed_scratch(dl_dtype type, const void* query, co
                                             size_t first_position, const size_t* device_position,
                                             size_t capacity) {
   if (type != DL_BF16) return fixed_fail(DL_UNSUPPORTED, "attention: only BF16 storage is supported");
-  if (!query || !key || !value || !output || !positions || !kv_heads || !width)
+  if (!query || !key || !value || !output || !positions || !query_heads || !kv_heads || !width)
     return fixed_fail(DL_INVALID_ARGUMENT, "attention: arguments");
+  if (positions > INT_MAX || query_heads > INT_MAX)
+    return fixed_fail(DL_INVALID_ARGUMENT, "attention: positions and query heads must fit an int");
   if (query_heads % kv_heads || query_heads / kv_heads > 8 || width > 128 || width % 8)
     return fixed_fail(DL_UNSUPPORTED, "attention: GQA group <= 8 and head width <= 128 (multiple of 8)");
+  if (!device_position && first_position > 200 * 1024 / 4)
+    return fixed_fail(DL_UNSUPPORTED, "attention: more than 51200 keys");
   const size_t cap = device_position ? capacity : first_position + positions;
+  if (!cap) return fixed_fail(DL_INVALID_ARGUMENT, "attention: zero key capacity");
   if (cap * 4 > 200 * 1024) return fixed_fail(DL_UNSUPPORTED, "attention: more than 51200 keys");
-  if (positions * query_heads * cap > kFixedScratchScores)
+  // positions * query_heads * cap > limit, checked without a product that could wrap.
+  if (positions > kFixedScratchScores / query_heads / cap)
     return fixed_fail(DL_INVALID_ARGUMENT,
                       "attention: positions * query_heads * key capacity exceeds the fixed scratch of " +
                           std::to_string(kFixedScratchScores) + " scores (4 MiB)");

@@ -397,6 +397,19 @@ DL_API dl_status dl_intervene(void* residual, const float* direction, const int6
                      "intervene");
 }
 
+DL_API dl_status dl_direction(dl_dtype type, const void* original, const void* edited, size_t width,
+                              float* direction, uint32_t* status, void* stream) {
+  if (type != DL_BF16 && type != DL_F32) return fail(DL_UNSUPPORTED, "direction: BF16 or FP32 reconstructions");
+  if (!original || !edited || !direction || !status || !width || width > 0x7fffffffu)
+    return fail(DL_INVALID_ARGUMENT, "direction: arguments");
+  const size_t element = type == DL_BF16 ? 2 : 4;
+  if (reinterpret_cast<uintptr_t>(original) % element || reinterpret_cast<uintptr_t>(edited) % element ||
+      reinterpret_cast<uintptr_t>(direction) % 4 || reinterpret_cast<uintptr_t>(status) % 4)
+    return fail(DL_INVALID_ARGUMENT, "direction: misaligned pointer");
+  return cuda_status(dl::launch_direction(type == DL_BF16, original, edited, direction, status, int(width), st(stream)),
+                     "direction");
+}
+
 DL_API dl_status dl_normalize_injection(const void* source, void* output, float* norm, uint32_t* status,
                                         size_t width, float scale, void* stream) {
   if (!source || !output || !norm || !status || !width) return fail(DL_INVALID_ARGUMENT, "normalize: arguments");
@@ -523,6 +536,9 @@ DL_API size_t dl_engine_position(dl_engine* e) {
   }
 }
 DL_API dl_status dl_engine_set_capture(dl_engine* e, int layer) { DL_ENGINE_CALL(e->impl->set_capture(layer)); }
+DL_API dl_status dl_engine_set_observation(dl_engine* e, void* device_rows, size_t positions) {
+  DL_ENGINE_CALL(e->impl->set_observation(device_rows, positions));
+}
 DL_API dl_status dl_engine_read_capture(dl_engine* e, size_t first, size_t count, uint16_t* host) {
   DL_ENGINE_CALL(e->impl->read_capture(first, count, host));
 }

@@ -380,6 +380,7 @@ void Engine::run_layers(int rows, bool pdl) {
         ++launches_;
       }
     }
+    observe_block(l, rows);
   }
 }
 
@@ -518,11 +519,19 @@ void Engine::run_layers_fast(int rows, long long first) {
       check(launch_copy_rows(residual_, capture_arena_, &state_->position, D, rows, stream_, false), "capture copy");
       ++launches_;
     }
+    observe_block(l, rows);
   }
 }
 
 void Engine::consume_rows(const uint32_t* tokens, size_t n, bool pdl, int mode, long long first) {
   const bool fast = mode == DL_PREFILL_FAST && fast_prefill_supported();
+  if (observe_rows_ && size_t(first) + n > observe_positions_)
+    throw std::invalid_argument("prompt pass reaches past the observation rows");
+  observing_ = observe_rows_ != nullptr;
+  struct Off {
+    bool& flag;
+    ~Off() { flag = false; }
+  } off{observing_};
   for (size_t c0 = 0; c0 < n; c0 += max_rows_) {
     const int rows = int(std::min(max_rows_, n - c0));
     check(cudaMemcpyAsync(tokens_dev_, tokens + c0, rows * 4, cudaMemcpyHostToDevice, stream_), "tokens");
@@ -603,6 +612,20 @@ void Engine::reconstruct(const uint32_t* tokens, size_t n, uint16_t* out_host) {
   check(cudaMemcpyAsync(out_host, xn_, size_t(D) * 2, cudaMemcpyDeviceToHost, stream_), "reconstruction out");
   check(cudaStreamSynchronize(stream_), "reconstruct sync");
   check_fault();
+}
+
+void Engine::set_observation(void* device_rows, size_t positions) {
+  if (device_rows && !positions) throw std::invalid_argument("observation needs positions");
+  observe_rows_ = static_cast<bf16*>(device_rows);
+  observe_positions_ = device_rows ? positions : 0;
+}
+
+void Engine::observe_block(size_t layer, int rows) {
+  if (!observe_rows_ || !observing_) return;
+  check(launch_copy_rows(residual_, observe_rows_ + layer * observe_positions_ * cfg_.hidden, &state_->position,
+                         int(cfg_.hidden), rows, stream_, false),
+        "observe copy");
+  ++launches_;
 }
 
 void Engine::set_capture(int layer) {

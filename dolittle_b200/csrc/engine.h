@@ -64,6 +64,7 @@ class Engine {
   size_t position();
   void set_capture(int layer);
   void read_capture(size_t first, size_t count, uint16_t* host);
+  void set_observation(void* device_rows, size_t positions);
   void set_intervention(int layer, size_t selected, float strength, const float* direction);
   void read_kv(size_t layer, int values, size_t first, size_t count, uint16_t* host);
   void set_injection(long long position, const uint16_t* source_bits, float scale);
@@ -101,6 +102,7 @@ class Engine {
   void launch_persistent_step(bool greedy);
   void check(cudaError_t e, const char* what);
   void check_fault();
+  void observe_block(size_t layer, int rows);
 
   dl_model_config cfg_;
   int device_;
@@ -128,6 +130,9 @@ class Engine {
   // capture / steering
   int capture_layer_ = -1;
   bf16* capture_arena_ = nullptr;
+  bf16* observe_rows_ = nullptr;  // caller-owned [layers][observe_positions_][D]
+  size_t observe_positions_ = 0;
+  bool observing_ = false;  // set only inside a prompt pass
   int edit_layer_ = -1;
   size_t edit_row_ = 0;
   float edit_strength_ = 0.f;

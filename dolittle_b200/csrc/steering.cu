@@ -6,6 +6,11 @@
 // h' = round(h + beta*u) with finiteness latches; state = {invalid, count},
 // count making the edit one-shot (a second application is invalid).
 // normalize: src/kernels/cuda/injection.cu:48-102, out = BF16((h/||h||)*scale).
+// direction: src/kernels/cuda/steering.cu:68-98 (DeviceDirection::submit,
+// :211-258).  delta_i = FP32(edited_i) - FP32(original_i); lane L of 8 sums
+// fmul(delta, delta) serially over i = L + 8k; lane 0 adds the 8 lane sums in
+// order; norm = sqrt_rn; status 1 (output untouched) on a zero or non-finite
+// norm, else direction_i = delta_i / norm (div_rn), stored FP32.
 #include "launch.h"
 #include "steering.h"
 
@@ -106,7 +111,60 @@ __global__ void normalize_kernel(const bf16* source, bf16* out, float* norm, uns
   if (threadIdx.x == 0) *status = invalid;
 }
 
+// One CTA.  Only the 8 lane chains are serial (the law's order): every
+// thread computes a tile of squared differences into shared memory first, and
+// the chains then walk that tile with one shared load per step; the tile
+// loop carries each lane's running sum.
+template <typename T>
+__global__ void direction_kernel(const T* original, const T* edited, float* out, unsigned* status, int width) {
+  constexpr int kTile = 4096;
+  __shared__ float sq[kTile];
+  __shared__ float lane_sum[kLanes];
+  __shared__ float norm_s;
+  if (threadIdx.x < kLanes) lane_sum[threadIdx.x] = 0.f;
+  for (int t0 = 0; t0 < width; t0 += kTile) {
+    const int n = min(kTile, width - t0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const float delta = __fsub_rn(float(edited[t0 + i]), float(original[t0 + i]));
+      sq[i] = __fmul_rn(delta, delta);
+    }
+    __syncthreads();
+    if (threadIdx.x < kLanes) {
+      // kTile is a multiple of 8, so lane L's features in this tile are
+      // t0 + L + 8k: the serial chain continues across tiles in order.
+      float acc = lane_sum[threadIdx.x];
+      for (int i = threadIdx.x; i < n; i += kLanes) acc = __fadd_rn(acc, sq[i]);
+      lane_sum[threadIdx.x] = acc;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float total = 0.f;
+    for (int i = 0; i < kLanes; ++i) total = __fadd_rn(total, lane_sum[i]);
+    const float norm = __fsqrt_rn(total);
+    norm_s = norm;
+    *status = (!isfinite(norm) || norm == 0.f) ? 1u : 0u;
+  }
+  __syncthreads();
+  const float norm = norm_s;
+  if (!isfinite(norm) || norm == 0.f) return;
+  for (int i = threadIdx.x; i < width; i += blockDim.x)
+    out[i] = __fdiv_rn(__fsub_rn(float(edited[i]), float(original[i])), norm);
+}
+
 }  // namespace
+
+cudaError_t launch_direction(bool bf16_input, const void* original, const void* edited, float* out,
+                             unsigned* status, int width, cudaStream_t stream) {
+  if (bf16_input)
+    direction_kernel<<<1, 512, 0, stream>>>(static_cast<const bf16*>(original), static_cast<const bf16*>(edited),
+                                            out, status, width);
+  else
+    direction_kernel<<<1, 512, 0, stream>>>(static_cast<const float*>(original), static_cast<const float*>(edited),
+                                            out, status, width);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_intervene(bf16* residual, const float* direction, const long long* position, unsigned* state,
                              int width, long long selected, int rows, float strength, cudaStream_t stream,

@@ -150,6 +150,12 @@ class Engine:
         check(lib().dl_engine_read_capture(self._h, first, count, out.ctypes.data_as(_lib.u16p)))
         return out
 
+    def set_observation(self, device_rows_ptr: int | None, positions: int = 0) -> None:
+        """Every block's output rows of later prompt passes go to the caller's
+        device buffer [layers][positions][hidden] (BF16); None turns it off."""
+        check(lib().dl_engine_set_observation(self._h, device_rows_ptr or None,
+                                              positions if device_rows_ptr else 0))
+
     def set_intervention(self, layer: int, selected: int = 0, strength: float = 0.0, direction=None) -> None:
         d = np.ascontiguousarray(direction if direction is not None else np.zeros(self.config.hidden),
                                  dtype=np.float32)

@@ -19,8 +19,11 @@
  *   dl_add ............... launch_add              src/kernels/cuda/launch.h:105-106
  *   dl_silu_multiply ..... launch_silu_multiply    src/kernels/cuda/launch.h:107-109
  *   dl_sampler_* ......... DeviceCategorical       src/inference/sampling/device.h:54-85
- *   dl_intervene ......... DeviceIntervention      src/inference/steering/device.h:30-68
+ *   dl_intervene ......... DeviceIntervention      src/inference/steering/device.h:50-68
  *                          (kernel src/kernels/cuda/steering.cu:106-159)
+ *   dl_direction ......... DeviceDirection         src/inference/steering/device.h:30-48
+ *                          (submit/finish src/kernels/cuda/steering.cu:200-258,
+ *                           kernel :68-98)
  *   dl_normalize_injection DeviceInjection         src/inference/injection/device.h:26-47
  *                          (kernel src/kernels/cuda/injection.cu:48-102)
  *   dl_engine_* .......... CachedForwardPlan       src/inference/executor.h:242-342
@@ -63,7 +66,8 @@ DL_API const char* dl_version(void);
 
 /* ------------------------------------------------------------------------ */
 /* Operation launches (reference launch.h mirrors).  The product computes in */
-/* BF16 storage with FP32 arithmetic; DL_F32 is rejected with DL_UNSUPPORTED.*/
+/* BF16 storage with FP32 arithmetic; DL_F32 is rejected with DL_UNSUPPORTED
+ * (except by dl_direction, whose reconstructions may be FP32). */
 /* Positions: device_position (size_t on device) overrides first_position.  */
 /* ------------------------------------------------------------------------ */
 
@@ -100,7 +104,8 @@ DL_API dl_status dl_attention(dl_dtype type, const void* query, const void* key,
  * share the array and it keeps the last call's contents; calls that overlap
  * on the GPU race on it, so serialize them.  The first call on each device
  * looks up the array's address (cudaGetSymbolAddress) with that device
- * current; make that first call before any stream capture. */
+ * current; make that first call before any stream capture.  The address is
+ * kept for the life of the process: calls must not span a cudaDeviceReset. */
 #define DL_ATTENTION_FIXED_SCRATCH_SCORES ((size_t)1 << 20)
 DL_API dl_status dl_attention_fixed_scratch(dl_dtype type, const void* query, const void* key,
                                             const void* value, void* output, size_t positions,
@@ -209,6 +214,16 @@ DL_API dl_status dl_sampler_submit_next(dl_sampler* s, const void* row, void* st
 DL_API dl_status dl_intervene(void* residual, const float* direction, const int64_t* position,
                               uint32_t* state, size_t width, size_t selected, size_t rows,
                               float strength, void* stream);
+/* Steering direction from two reconstructions (DeviceDirection::submit;
+ * finish = read *status after the stream completes):
+ * direction = (edited - original) / ||edited - original||, FP32 [width].
+ * The norm follows the reference law: 8 lanes, lane L summing the rounded
+ * squares of FP32(edited[i]) - FP32(original[i]) over i = L + 8k in order,
+ * then lane sums 0..7 in order, sqrt_rn; each quotient div_rn.  *status = 1
+ * (direction left untouched) on a zero or non-finite norm, else 0.
+ * type: DL_BF16 or DL_F32 reconstructions; all pointers device memory. */
+DL_API dl_status dl_direction(dl_dtype type, const void* original, const void* edited, size_t width,
+                              float* direction, uint32_t* status, void* stream);
 /* out = BF16((h/||h||)*scale); norm and status written to device memory. */
 DL_API dl_status dl_normalize_injection(const void* source, void* output, float* norm,
                                         uint32_t* status, size_t width, float scale,
@@ -276,6 +291,15 @@ DL_API size_t dl_engine_position(dl_engine* e);
  * arena [capacity][D] (layer < 0 disables). */
 DL_API dl_status dl_engine_set_capture(dl_engine* e, int layer);
 DL_API dl_status dl_engine_read_capture(dl_engine* e, size_t first, size_t count, uint16_t* host);
+/* Observe every block's output (the residual after block l, the site the
+ * reference's ObservationPlan resolves per advertised block,
+ * src/inference/observations.h) during later prompt passes: the BF16 row of
+ * absolute position p after block l is written to
+ * device_rows + (l * positions + p) * D.  device_rows is caller-owned device
+ * memory of layers * positions * D BF16 values; a prompt pass reaching a
+ * position >= `positions` is rejected (DL_INVALID_ARGUMENT).  Decode steps do
+ * not observe.  device_rows == NULL turns observation off. */
+DL_API dl_status dl_engine_set_observation(dl_engine* e, void* device_rows, size_t positions);
 /* One-shot steering edit at block `layer`, absolute row `selected`. */
 DL_API dl_status dl_engine_set_intervention(dl_engine* e, int layer, size_t selected,
                                             float strength, const float* host_direction);

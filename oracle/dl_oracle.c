@@ -361,6 +361,38 @@ OR_API void or_intervene(uint16_t* residual, const float* direction,
   state[0] = invalid;
 }
 
+/* Steering direction from two reconstructions: src/kernels/cuda/
+ * steering.cu:68-98 (DeviceDirection::submit/finish :200-258).  delta =
+ * FP32(edited) - FP32(original); lane L of 8 sums delta*delta (rounded) over
+ * i = L + 8k in order; lanes added 0..7 in order; norm = sqrt (correctly
+ * rounded); returns 1 and leaves out untouched on a zero or non-finite
+ * norm, else out[i] = delta_i / norm.  Inputs are BF16 bits (bf16 != 0) or
+ * FP32 values.                                                              */
+OR_API uint32_t or_direction(int bf16, const void* original, const void* edited,
+                             size_t width, float* out) {
+  const uint16_t* ob = (const uint16_t*)original;
+  const uint16_t* eb = (const uint16_t*)edited;
+  const float* of = (const float*)original;
+  const float* ef = (const float*)edited;
+#define OR_DELTA(i) (bf16 ? bf(eb[i]) - bf(ob[i]) : ef[i] - of[i])
+  float sums[8];
+  for (int l = 0; l < 8; ++l) {
+    float s = 0.0f;
+    for (size_t i = (size_t)l; i < width; i += 8) {
+      float delta = OR_DELTA(i);
+      s = s + delta * delta;
+    }
+    sums[l] = s;
+  }
+  float sum = 0.0f;
+  for (int l = 0; l < 8; ++l) sum = sum + sums[l];
+  float norm = sqrtf(sum);
+  if (!isfinite(norm) || norm == 0.0f) return 1u;
+  for (size_t i = 0; i < width; ++i) out[i] = OR_DELTA(i) / norm;
+#undef OR_DELTA
+  return 0u;
+}
+
 /* Injection normalisation: src/kernels/cuda/injection.cu:48-102.           */
 OR_API uint32_t or_normalize_injection(const uint16_t* source, uint16_t* out,
                                        size_t width, float scale,

@@ -26,12 +26,28 @@ u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
 f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 
 
+def reference_tree() -> str | None:
+    """The reference source tree: $DOLITTLE_REFERENCE, else BASELINE.json's
+    ``reference_path``; None when neither names an existing directory (the
+    GPU box has no reference tree and uses the prebuilt _ref libraries)."""
+    path = os.environ.get("DOLITTLE_REFERENCE")
+    if not path:
+        try:
+            import json
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                path = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            path = None
+    return path if path and os.path.isdir(os.path.join(path, "src")) else None
+
+
 def build(reference: bool = True) -> None:
     """Compile the oracle (and, when the reference tree is present, _ref)."""
     targets = ["oracle"]
-    if reference and os.path.isdir("/root/reference"):
+    ref = reference_tree() if reference else None
+    if ref:
         targets.append("ref")
-    subprocess.run(["make", "-s", "-C", HERE, *targets], check=True)
+    subprocess.run(["make", "-s", "-C", HERE, *targets] + ([f"REF={ref}"] if ref else []), check=True)
 
 
 class OrConfig(C.Structure):
@@ -81,6 +97,8 @@ def lib():
         L.or_normalize_injection.restype = C.c_uint32
         L.or_normalize_injection.argtypes = [u16p, u16p, sz, C.c_float,
                                              C.POINTER(C.c_float)]
+        L.or_direction.restype = C.c_uint32
+        L.or_direction.argtypes = [C.c_int, C.c_void_p, C.c_void_p, sz, f32p]
         L.or_mt64_seed.argtypes = [C.c_void_p, C.c_uint64]
         L.or_mt64_next.restype = C.c_uint64
         L.or_mt64_next.argtypes = [C.c_void_p]
@@ -186,6 +204,19 @@ def uniform_ids(n, seed, stream, bound):
     out = np.empty(n, np.uint32)
     lib().or_fill_uniform_ids(out, n, seed, stream, bound)
     return out
+
+
+def direction(original, edited):
+    """(status, FP32 direction) of the DeviceDirection law; inputs are BF16
+    bits (uint16) or FP32 arrays of one width.  On status 1 the direction
+    is all NaN (the law leaves its output untouched)."""
+    bf16 = np.asarray(original).dtype == np.uint16
+    dt = np.uint16 if bf16 else np.float32
+    a = np.ascontiguousarray(original, dt).reshape(-1)
+    b = np.ascontiguousarray(edited, dt).reshape(-1)
+    out = np.full(a.size, np.nan, np.float32)
+    status = lib().or_direction(int(bf16), a.ctypes.data, b.ctypes.data, a.size, out)
+    return int(status), out
 
 
 class MT64:
@@ -362,10 +393,28 @@ def ref_cuda():
                                         sz, C.c_double, C.c_uint64, u32p]
         L.ref_device_sequence.argtypes = [f32p, sz, C.c_int, C.c_double, sz,
                                           C.c_double, C.c_uint64, sz, u32p]
+        L.ref_direction.argtypes = [C.c_int, C.c_void_p, C.c_void_p, sz, f32p,
+                                    C.POINTER(C.c_uint32)]
         for name in ("ref_projection", "ref_rms_norm", "ref_rotary",
                      "ref_attention_scale", "ref_attention", "ref_embedding",
                      "ref_add", "ref_silu_multiply", "ref_qwen3_forward",
-                     "ref_device_select", "ref_device_sequence"):
+                     "ref_device_select", "ref_device_sequence", "ref_direction"):
             getattr(L, name).restype = C.c_int
         _ref_cuda = L
     return _ref_cuda
+
+
+def ref_direction(original, edited):
+    """(status, FP32 direction) from the reference's own DeviceDirection on
+    the GPU (oracle/_ref/libref_cuda.so); direction all NaN on status 1."""
+    L = ref_cuda()
+    bf16 = np.asarray(original).dtype == np.uint16
+    dt = np.uint16 if bf16 else np.float32
+    a = np.ascontiguousarray(original, dt).reshape(-1)
+    b = np.ascontiguousarray(edited, dt).reshape(-1)
+    out = np.full(a.size, np.nan, np.float32)
+    status = C.c_uint32(7)
+    rc = L.ref_direction(int(bf16), a.ctypes.data, b.ctypes.data, a.size, out, C.byref(status))
+    if rc:
+        raise RuntimeError("reference DeviceDirection failed")
+    return int(status.value), out

@@ -10,6 +10,7 @@
 // Wrapped reference interfaces:
 //   launch_* : src/kernels/cuda/launch.h:79-109
 //   DeviceCategorical : src/inference/sampling/device.h:54-85
+//   DeviceDirection : src/inference/steering/device.h:30-48
 // ref_qwen3_forward composes the launch_* calls in the reference recipe
 // order, src/models/qwen3/model.cpp:343-409.
 #include <cuda_runtime.h>
@@ -23,6 +24,7 @@
 
 #include "gpu/cuda/device.h"
 #include "inference/sampling/device.h"
+#include "inference/steering/device.h"
 #include "kernels/cuda/launch.h"
 #include "tensors/representations/bf16.h"
 
@@ -207,8 +209,12 @@ REF_API int ref_qwen3_forward(const RefConfig* c, const void* const* tensors,
       k::launch_silu_multiply(bt, gate, up, gate, rows * F, s);
       k::launch_projection(bt, gate, w[10], proj, rows, F, D, s);
       k::launch_add(bt, residual, proj, residual, rows * D, s);
-      if (capture_rows && capture_layer == static_cast<int>(l)) {
-        if (cudaMemcpyAsync(capture_rows, residual, 2 * rows * D,
+      // capture_layer >= 0: that block's output rows; -2: every block's,
+      // as [layers][rows][D].
+      if (capture_rows && (capture_layer == static_cast<int>(l) || capture_layer == -2)) {
+        auto* dst = static_cast<std::uint16_t*>(capture_rows) +
+                    (capture_layer == -2 ? l * rows * D : 0);
+        if (cudaMemcpyAsync(dst, residual, 2 * rows * D,
                             cudaMemcpyDeviceToDevice, s) != cudaSuccess)
           return 2;
       }
@@ -308,6 +314,47 @@ REF_API int ref_device_sequence(const float* logits, std::size_t n, int bf16,
       h.queue->drain();
       std::memcpy(results + 2 * i, answer.bytes().data(), 8);
     }
+    return 0;
+  } catch (...) {
+    return 1;
+  }
+}
+
+// DeviceDirection over two reconstructions given as host bytes (BF16 bits or
+// FP32): submit + finish through the reference's own gpu::Device.  status 1
+// when finish rejects a zero or non-finite difference (the direction is then
+// not read); otherwise the FP32 direction goes to `direction`.
+REF_API int ref_direction(int bf16, const void* original, const void* edited,
+                          std::size_t width, float* direction,
+                          unsigned* status) {
+  try {
+    auto& h = harness();
+    const std::size_t bytes = width * (bf16 ? 2 : 4);
+    auto upload = [&](const void* src) {
+      auto buffer = std::make_shared<dolittle::gpu::DeviceBuffer>(
+          h.device->allocate({bytes, 256}));
+      auto staging = h.device->allocate_staging({bytes, 8});
+      std::memcpy(staging.bytes().data(), src, bytes);
+      h.queue->upload({buffer.get(), 0, bytes}, {&staging, 0, bytes});
+      h.queue->drain();
+      return dolittle::inference::DeviceCapture{buffer, 0, bytes};
+    };
+    dolittle::inference::DeviceDirection dir(
+        *h.device, *h.queue, upload(original), upload(edited),
+        bf16 ? ElementType::bfloat16 : ElementType::float32, width);
+    dir.submit();
+    dolittle::inference::DeviceCapture out;
+    try {
+      out = dir.finish();
+    } catch (const std::invalid_argument&) {
+      *status = 1;
+      return 0;
+    }
+    *status = 0;
+    auto answer = h.device->allocate_staging({width * 4, 8});
+    h.queue->download({&answer, 0, width * 4}, out.region());
+    h.queue->drain();
+    std::memcpy(direction, answer.bytes().data(), width * 4);
     return 0;
   } catch (...) {
     return 1;

@@ -1,10 +1,10 @@
 #!/usr/bin/env python3
 """Regenerate tests/golden/tiny-bf16/ from the reference's own Python oracle.
 
-Run in the development container, where the reference tree is mounted
-(default /root/reference; override with DOLITTLE_REFERENCE):
+Run in the development container, where the reference tree is mounted,
+with DOLITTLE_REFERENCE naming it (else BASELINE.json's reference_path):
 
-    python tests/golden/make_tiny_fixture.py
+    DOLITTLE_REFERENCE=<reference tree> python tests/golden/make_tiny_fixture.py
 
 It imports scripts/validation/forward_reference.py from the reference and
 calls its generate(kind="tiny-bf16", device="cpu") directly.  That function
@@ -19,15 +19,19 @@ at test time reads the reference tree: only the committed outputs.
 """
 import importlib
 import json
-import os
 import sys
 from pathlib import Path
 
-REFERENCE = Path(os.environ.get("DOLITTLE_REFERENCE", "/root/reference"))
 OUT = Path(__file__).resolve().parent / "tiny-bf16"
 
 
 def main() -> None:
+    sys.path.insert(0, str(Path(__file__).resolve().parents[2]))
+    from oracle.oracle import reference_tree
+    ref = reference_tree()
+    if ref is None:
+        raise SystemExit("set DOLITTLE_REFERENCE to the reference source tree")
+    REFERENCE = Path(ref)
     sys.path.insert(0, str(REFERENCE / "scripts" / "validation"))
     fr = importlib.import_module("forward_reference")
     import torch

@@ -73,11 +73,16 @@ class RefModel:
                                c.vocabulary, c.layers, c.epsilon, c.theta)
 
     def forward(self, tokens, first: int, capture_layer: int = -1):
+        """BF16 logits bits of the last row, and the captured block output
+        rows: [rows][D] for capture_layer >= 0, [layers][rows][D] for -2."""
         tokens = np.ascontiguousarray(tokens, np.uint32)
         rows = tokens.size
         assert rows <= self.max_rows
         self.tokens[:rows].copy_(torch().from_numpy(tokens.view(np.int32)).cuda())
-        cap = zeros_dev((rows, self.cfg.hidden)) if capture_layer >= 0 else None
+        if capture_layer == -2:
+            cap = zeros_dev((self.cfg.layers, rows, self.cfg.hidden))
+        else:
+            cap = zeros_dev((rows, self.cfg.hidden)) if capture_layer >= 0 else None
         rc = self.L.ref_qwen3_forward(C.byref(self._ocfg()), self._tp, self._cp, self.capacity,
                                       ptr(self.tokens), rows, first, ptr(self.logits), capture_layer,
                                       ptr(cap) if cap is not None else None, ptr(self.scratch), None)
