@@ -10,8 +10,8 @@
 //   each thread reads its part of the row of S; the parts exchange their max
 //   and sum through shared memory to update the row's running max m and sum
 //   l of exp2(s - m) (masked beyond the row's position); each writes its
-//   p = exp2(s - m) as BF16 into a 128-byte-swizzled K-major tile;
-//   O[kb] = P V[kb] (A = P, B = V^T) into TMEM; each thread rescales its
+//   p = exp2(s - m) as FP16 into a 128-byte-swizzled K-major tile;
+//   O[kb] = P V[kb] (A = P, B = V^T, both FP16) into TMEM; each thread rescales its
 //   register copy of its 64 output columns by exp2(m_old - m_new) and adds
 //   those of O[kb]; the output is O / l at the end.
 // K and V^T blocks stream through two TMA stages, and the next block's score
@@ -19,8 +19,14 @@
 // output update.  Scores carry the softmax scale times log2(e).  Q and K come
 // in by TMA from the rotated queries and the K cache; V is read as V^T from a
 // transposed copy (launch_vt_transpose) so both operands of both products are
-// K-major.
+// K-major.  The second product runs in FP16 (10-bit mantissa): p in [0, 1]
+// rounded to FP16 carries 1/8 of the BF16 rounding error, and the BF16 values
+// of V convert to FP16 exactly (the copy saturates at +-65504, far beyond any
+// value a normed projection produces).  In BF16 the P rounding alone added as
+// much error to the attention output as its final BF16 rounding.
 #include <cudaTypedefs.h>
+
+#include <cuda_fp16.h>
 
 #include <cmath>
 #include <mutex>
@@ -70,10 +76,12 @@ __device__ __forceinline__ void tma_load4(void* dst, const CUtensorMap* map, int
       : "memory");
 }
 
-// 8 MMAs of K = 16 across the two swizzle atoms of a 128-wide K dimension.
+// 8 MMAs of K = 16 across the two swizzle atoms of a 128-wide K dimension;
+// BF16 operands (S = Q K^T) or FP16 operands (O = P V).
+template <bool F16>
 __device__ __forceinline__ void mma_tile(uint32_t tmem_d, const unsigned char* a_tile, const unsigned char* b_tile,
                                          bool accumulate) {
-  constexpr uint32_t idesc = instr_desc_bf16(kTile, kTile);
+  constexpr uint32_t idesc = F16 ? instr_desc_f16(kTile, kTile) : instr_desc_bf16(kTile, kTile);
   const uint32_t sa = smem_addr(a_tile), sb = smem_addr(b_tile);
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk) {
@@ -154,7 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const
       fail();
     } else {
       fence_after_sync();
-      mma_tile(t_s(0), sq, sk(0), false);
+      mma_tile<false>(t_s(0), sq, sk(0), false);
       mma_commit(&s_bar[0]);
     }
   }
@@ -199,8 +207,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const
         const int k0 = key0 + c * 32 + i;
         const float p0 = (use && k0 <= pos) ? exp2f(__uint_as_float(sv[i]) * a.scale_log2 - mn) : 0.f;
         const float p1 = (use && k0 + 1 <= pos) ? exp2f(__uint_as_float(sv[i + 1]) * a.scale_log2 - mn) : 0.f;
-        const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
-        sum += __low2float(h2) + __high2float(h2);  // l sums the BF16 weights the MMA sees
+        const __half2 h2 = __floats2half2_rn(p0, p1);
+        sum += __low2float(h2) + __high2float(h2);  // l sums the FP16 weights the MMA sees
         packed[i / 2] = *reinterpret_cast<const uint32_t*>(&h2);
       }
       // Keys c*32 .. c*32+31 of the block: atom c / 2, chunks (c % 2) * 4 .. + 3.
@@ -225,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const
     }
     if (threadIdx.x == 0 && !abort_flag) {
       fence_after_sync();
-      mma_tile(t_o, sp, svt(st), false);
+      mma_tile<true>(t_o, sp, svt(st), false);
       mma_commit(&o_bar);
       if (kb + 1 < nkb) {
         // The next block's scores overlap this block's output update.
@@ -233,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const
           fail();
         } else {
           fence_after_sync();
-          mma_tile(t_s(st ^ 1), sq, sk(st ^ 1), false);
+          mma_tile<false>(t_s(st ^ 1), sq, sk(st ^ 1), false);
           mma_commit(&s_bar[st ^ 1]);
         }
       }
@@ -271,17 +279,20 @@ __global__ void __launch_bounds__(kThreads, 1) attention_prefill_tc_kernel(const
   if (warp == 0) tmem_dealloc(tmem, kTmemCols);
 }
 
-// V^T of one block's cache: vt[g][f][j] = v[j][g][f] for j < keys.
-__global__ void vt_transpose_kernel(const bf16* __restrict__ v, bf16* __restrict__ vt, int keys, int kv_heads,
+// V^T of one block's cache in FP16: vt[g][f][j] = v[j][g][f] for j < keys
+// (BF16 -> FP16 is exact in FP16's normal range; saturated beyond it).
+__global__ void vt_transpose_kernel(const bf16* __restrict__ v, __half* __restrict__ vt, int keys, int kv_heads,
                                     int width, int vt_stride) {
-  __shared__ bf16 tile[32][33];
+  __shared__ __half tile[32][33];
   allow_next();
   wait_prior();
   const int g = blockIdx.z;
   const int j0 = blockIdx.x * 32, f0 = blockIdx.y * 32;
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
     const int j = j0 + i, f = f0 + threadIdx.x;
-    if (j < keys && f < width) tile[i][threadIdx.x] = v[(size_t(j) * kv_heads + g) * width + f];
+    if (j < keys && f < width)
+      tile[i][threadIdx.x] =
+          __float2half_rn(fminf(fmaxf(__bfloat162float(v[(size_t(j) * kv_heads + g) * width + f]), -65504.f), 65504.f));
   }
   __syncthreads();
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
@@ -304,11 +315,11 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 bool encode(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
-            const cuuint32_t* box) {
+            const cuuint32_t* box, CUtensorMapDataType type = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint32_t es[4] = {1, 1, 1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides_bytes, box, es,
+  return fn(map, type, rank, const_cast<void*>(base), dims, strides_bytes, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -339,7 +350,7 @@ AttnTcMaps* attention_prefill_tc_maps(const bf16* q, int max_rows, int query_hea
   const cuuint64_t vs[2] = {uint64_t(vt_stride) * 2, uint64_t(width) * vt_stride * 2};
   const cuuint32_t vb[3] = {64, 128, 1};
   if (!encode(&m->q, q, 3, qd, qs, qb) || !encode(&m->k, kv_arena, 4, kd, ks, kb) ||
-      !encode(&m->vt, vt, 3, vd, vs, vb)) {
+      !encode(&m->vt, vt, 3, vd, vs, vb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16)) {
     delete m;
     return nullptr;
   }
@@ -369,7 +380,8 @@ cudaError_t launch_vt_transpose(const bf16* v_cache, bf16* vt, int keys, int kv_
   if (keys <= 0) return cudaSuccess;
   cudaLaunchAttribute attr[1];
   auto cfg = pdl_config(dim3((keys + 31) / 32, (width + 31) / 32, kv_heads), dim3(32, 8), 0, stream, attr, pdl);
-  return cudaLaunchKernelEx(&cfg, vt_transpose_kernel, v_cache, vt, keys, kv_heads, width, vt_stride);
+  return cudaLaunchKernelEx(&cfg, vt_transpose_kernel, v_cache, reinterpret_cast<__half*>(vt), keys, kv_heads, width,
+                            vt_stride);
 }
 
 cudaError_t launch_attention_prefill_tc(const AttnTcMaps* maps, bf16* out, int rows, long long first, int layer,

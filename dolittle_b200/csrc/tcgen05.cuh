@@ -30,6 +30,10 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
 __host__ __device__ constexpr uint32_t instr_desc_bf16(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
 }
+// The same with A = B = FP16 (format code 0 in bits 7 and 10).
+__host__ __device__ constexpr uint32_t instr_desc_f16(int M, int N) {
+  return (1u << 4) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
 
 __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                          uint32_t accumulate) {
