@@ -661,6 +661,107 @@ def run_serve(args):
     return 0
 
 
+def run_steer_batch(args):
+    """Config 3 as BASELINE states it: the steered and the unsteered
+    continuation of one 256-token prompt as ONE batch of 2 in the batched
+    server (tensor-parallel over the launched ranks when N > 1).  Block 24's
+    output is captured; the steering vector is a seeded unit Gaussian u
+    (Philox seed 7) with strength beta = 4 x ||h|| of the unsteered
+    sequence's block-24 row at token 200 (the one-row edit's norm law,
+    computed on the device during the prompt pass) and is added at block 24
+    for every position >= 200 of sequence 1.  512 decode steps at
+    temperature 0.7 / top-p 0.9 with the Philox4x32-10 draw source, seed 7.
+    One step = prompt pass of both sequences + 512 decode steps."""
+    world, rank, local = dist_setup()
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+    import dolittle_b200 as dl
+    from dolittle_b200 import replicas
+    from dolittle_b200.serve import Server, connect_group
+    hbm, tflops, kind = peaks()
+    cfg = dl.QWEN3_8B
+    V = cfg.vocabulary
+    P, new_tokens, layer, p0 = 256, 512, 24, 200
+    prompt = np.random.Generator(np.random.Philox(SEED + 3)).integers(0, V, P, dtype=np.uint32)
+    prompts = np.stack([prompt, prompt])
+    u = np.random.Generator(np.random.Philox(7)).standard_normal(cfg.hidden).astype(np.float32)
+    u /= np.linalg.norm(u)
+    settings = dl.Settings(dl.SelectionMode.categorical, temperature=0.7, top_p=0.9)
+    srv = Server(cfg, batch=2, capacity=P + new_tokens + 8, chunk_rows=P, device=local, tp_rank=rank,
+                 tp_size=world)
+    srv.init_random(SEED, 0.02)
+    if world > 1:
+        connect_group(srv, dist)
+    srv.set_sampler_engine(dl.DL_RNG_PHILOX4X32_10)
+    srv.set_capture(layer)
+    srv.set_steering(layer, first_position=p0, strength=4.0, direction=u, sequences=[1], source_sequence=0,
+                     source_position=p0)
+
+    def step():
+        t = time.perf_counter()
+        srv.prefill(prompts, settings, seed=7)
+        res = srv.decode(new_tokens)
+        return res, time.perf_counter() - t
+
+    for _ in range(args.warmup):
+        step()
+    clocks = Clocks(local)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    outs = [step() for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    decode_s = sum(r.decode_ms for r, _ in outs) / 1000.0
+    prefill_s = sum(r.prefill_ms for r, _ in outs) / 1000.0
+    wall = sum(w for _, w in outs)
+    decode_s, prefill_s, wall = replicas.max_over_ranks(dist, [decode_s, prefill_s, wall])
+    beta = srv.steering_strength()
+    res = outs[-1][0]
+    diverged = next((i for i in range(new_tokens) if res.tokens[i, 0] != res.tokens[i, 1]), new_tokens)
+    if rank == 0:
+        tokens = args.steps * 2 * new_tokens
+        D, d, Lm = cfg.hidden, cfg.head_width, cfg.layers
+        w_layer = D * (cfg.query_heads * d + 2 * cfg.kv_heads * d) + cfg.query_heads * d * D + 3 * D * cfg.mlp_width
+        step_bytes = 2 * (Lm * w_layer / world + D * V) + 2 * (P + new_tokens / 2) * Lm * 2 * (cfg.kv_heads // world) * d * 2
+        ms_step = 1000 * decode_s / (args.steps * new_tokens)
+        achieved = step_bytes / (ms_step * 1e-3) / 1e9
+        line = {
+            "metric": "Qwen3-8B steering comparison decode tok/s (config 3)",
+            "value": tokens / decode_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000 * wall / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init BF16 weights ~N(0,0.02), uniform prompt IDs)",
+            "config": {"workload": "config 3: 256-token prompt; steered and unsteered continuations as one batch "
+                                   "of 2; block 24 captured; steering 4 x ||h[200]|| along a seeded unit Gaussian "
+                                   "added at block 24 for every position >= 200; 512 tokens at T 0.7 / top-p 0.9, "
+                                   "Philox seed 7",
+                       "parallelism": f"tp{world} over KV-head groups" if world > 1 else "single GPU"},
+            "decode_ms_per_step": ms_step,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "bytes_per_step_per_gpu": step_bytes, "peak_kind": kind,
+                         "kernel": "batched decode step graph (B = 2)"},
+            "e2e": {"value": tokens / wall, "unit": "tok/s", "what": "prefill + decode calls with host token readback",
+                    "h2d_bytes_per_step": 2 * P * 4, "d2h_bytes_per_step": 2 * new_tokens * 4},
+            "prefill_s": prefill_s,
+            "steering_beta": beta,
+            "first_divergent_step": diverged,
+            "gpu_launches": outs[0][0].kernels_per_decode_step * new_tokens * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    srv.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_branches(args):
     """Configs 3 and 4 as data-parallel units (replicas: the units split
     round-robin over the launched ranks, no collective on the data path).
@@ -687,7 +788,7 @@ def run_branches(args):
     from dolittle_b200 import replicas
     cfg = dl.QWEN3_8B
     V = cfg.vocabulary
-    steer = args.workload == "steer"
+    steer = args.workload == "steer-pair"
     prompt = np.random.Generator(np.random.Philox(SEED + 3)).integers(0, V, 256, dtype=np.uint32)
     engine = dl.Engine(cfg, device=local, capacity=256 + 512 + 8, max_rows=256)
     engine.init_random(SEED, 0.02)
@@ -910,16 +1011,20 @@ def main():
     ap.add_argument("--gemm-shape", choices=["all", "qkv", "o", "gu", "down"], default="all",
                     help="--profile gemm: one prompt-pass projection only")
     ap.add_argument("--gemm-tile", default="", help="--profile gemm: TM,TN,PARTS tiling (e.g. 256,256,1)")
-    ap.add_argument("--workload", choices=["decode", "serve", "steer", "nla"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "serve", "steer", "steer-pair", "nla"], default="decode",
                     help="decode: config 2 (headline); serve: config 5 batched serving, TP over the ranks; "
-                         "steer / nla: configs 3 / 4, units split over the ranks")
+                         "steer: config 3 as one batch of 2 (steered + unsteered, every position >= 200); "
+                         "steer-pair: config 3 with the reference's one-row edit, two engines; "
+                         "nla: config 4, units split over the ranks")
     ap.add_argument("--serve-batch", type=int, default=32)
     ap.add_argument("--serve-prompt", type=int, default=8192)
     ap.add_argument("--serve-steps", type=int, default=32, help="decode steps per timed call (config 5)")
     args = ap.parse_args()
     if args.workload == "serve" and args.impl == "ours":
         return run_serve(args)
-    if args.workload in ("steer", "nla") and args.impl == "ours":
+    if args.workload == "steer" and args.impl == "ours":
+        return run_steer_batch(args)
+    if args.workload in ("steer-pair", "nla") and args.impl == "ours":
         return run_branches(args)
     if args.profile:
         return run_profile_case(args)

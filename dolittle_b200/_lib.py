@@ -19,6 +19,7 @@ DL_REASON_LIMIT, DL_REASON_EOS, DL_REASON_CANCELLED, DL_REASON_FAILURE = range(4
 DL_BF16, DL_F32 = 0, 1
 DL_PREFILL_PARITY, DL_PREFILL_FAST = 0, 1
 DL_DECODE_PERSISTENT, DL_DECODE_KERNELS = 0, 1
+DL_RNG_MT19937_64, DL_RNG_PHILOX4X32_10 = 0, 1
 
 
 class DolittleError(RuntimeError):
@@ -86,6 +87,7 @@ SIGNATURES = {
     "dl_sampler_required_bytes": (sz, [sz]),
     "dl_sampler_create": (C.c_int, [sz, C.c_int, C.POINTER(vp)]),
     "dl_sampler_destroy": (None, [vp]),
+    "dl_sampler_set_engine": (C.c_int, [vp, C.c_int]),
     "dl_sampler_start": (C.c_int, [vp, C.POINTER(Sampling), C.c_uint64, u32p, sz, vp]),
     "dl_sampler_submit": (C.c_int, [vp, vp, C.POINTER(Sampling), C.c_uint64, vp, C.POINTER(vp)]),
     "dl_sampler_submit_next": (C.c_int, [vp, vp, vp, C.POINTER(vp)]),
@@ -108,6 +110,7 @@ SIGNATURES = {
     "dl_engine_set_observation": (C.c_int, [vp, vp, sz]),
     "dl_engine_set_intervention": (C.c_int, [vp, C.c_int, sz, C.c_float, C.POINTER(C.c_float)]),
     "dl_engine_set_decode_path": (C.c_int, [vp, C.c_int]),
+    "dl_engine_set_sampler_engine": (C.c_int, [vp, C.c_int]),
     "dl_engine_set_injection": (C.c_int, [vp, C.c_int64, u16p, C.c_float]),
     "dl_engine_set_reconstruction_head": (C.c_int, [vp, u16p]),
     "dl_engine_reconstruct": (C.c_int, [vp, u32p, sz, u16p]),
@@ -125,12 +128,18 @@ SIGNATURES = {
     "dl_serve_ipc_handle": (C.c_int, [vp, vp]),
     "dl_serve_connect_peers": (C.c_int, [vp, vp]),
     "dl_serve_init_random": (C.c_int, [vp, C.c_uint64, C.c_float]),
+    "dl_serve_set_sampler_engine": (C.c_int, [vp, C.c_int]),
     "dl_serve_set_tensor": (C.c_int, [vp, sz, vp, sz]),
     "dl_serve_get_tensor": (C.c_int, [vp, sz, vp, sz]),
     "dl_serve_slice_shape": (C.c_int, [vp, sz, C.POINTER(sz), C.POINTER(sz), C.POINTER(sz), C.POINTER(sz)]),
     "dl_serve_prefill": (C.c_int, [vp, u32p, sz, C.POINTER(Sampling), C.c_uint64, u32p]),
     "dl_serve_decode": (C.c_int, [vp, sz, u32p, u16p, C.POINTER(ServeStats)]),
     "dl_serve_position": (sz, [vp]),
+    "dl_serve_set_capture": (C.c_int, [vp, C.c_int]),
+    "dl_serve_read_capture": (C.c_int, [vp, sz, sz, sz, u16p]),
+    "dl_serve_set_steering": (C.c_int, [vp, C.c_int, sz, C.c_float, C.POINTER(C.c_float), C.POINTER(C.c_uint8),
+                                        C.c_int64, sz]),
+    "dl_serve_steering_strength": (C.c_int, [vp, C.POINTER(C.c_float)]),
     "dl_gemm_bf16_parts_workspace_bytes": (sz, [sz, sz, sz, sz]),
     "dl_gemm_bf16_parts": (C.c_int, [vp, sz, vp, vp, sz, sz, sz, sz, C.c_int, sz, vp, vp]),
     "dl_attention_decode_batched_workspace_bytes": (sz, [sz, sz, sz, sz]),

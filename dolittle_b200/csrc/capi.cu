@@ -442,6 +442,14 @@ DL_API void dl_sampler_destroy(dl_sampler* s) {
   delete s;
 }
 
+DL_API dl_status dl_sampler_set_engine(dl_sampler* s, int engine) {
+  if (!s || (engine != DL_RNG_MT19937_64 && engine != DL_RNG_PHILOX4X32_10))
+    return fail(DL_INVALID_ARGUMENT, "sampler_set_engine: unknown engine");
+  if (s->s.started) return fail(DL_INVALID_ARGUMENT, "sampler_set_engine: sampler already started");
+  s->s.engine = unsigned(engine);
+  return DL_OK;
+}
+
 DL_API dl_status dl_sampler_start(dl_sampler* s, const dl_sampling* settings, uint64_t seed,
                                   const uint32_t* stop_ids, size_t n_stop, void* stream) {
   if (!s || !settings || (n_stop && !stop_ids)) return fail(DL_INVALID_ARGUMENT, "sampler_start: arguments");
@@ -549,6 +557,11 @@ DL_API dl_status dl_engine_set_intervention(dl_engine* e, int layer, size_t sele
 DL_API dl_status dl_engine_set_decode_path(dl_engine* e, int path) {
   DL_ENGINE_CALL(e->impl->set_decode_path(path));
 }
+DL_API dl_status dl_engine_set_sampler_engine(dl_engine* e, int engine) {
+  if (engine != DL_RNG_MT19937_64 && engine != DL_RNG_PHILOX4X32_10)
+    return fail(DL_INVALID_ARGUMENT, "set_sampler_engine: unknown engine");
+  DL_ENGINE_CALL(e->impl->set_sampler_engine(engine));
+}
 DL_API dl_status dl_engine_set_injection(dl_engine* e, int64_t position, const uint16_t* source_bits,
                                          float scale) {
   if (position >= 0 && !source_bits) return fail(DL_INVALID_ARGUMENT, "injection: source required");
@@ -647,6 +660,11 @@ DL_API dl_status dl_serve_connect_peers(dl_serve* s, const unsigned char* handle
 DL_API dl_status dl_serve_init_random(dl_serve* s, uint64_t seed, float sigma) {
   DL_SERVE_CALL(s->impl->init_random(seed, sigma));
 }
+DL_API dl_status dl_serve_set_sampler_engine(dl_serve* s, int engine) {
+  if (engine != DL_RNG_MT19937_64 && engine != DL_RNG_PHILOX4X32_10)
+    return fail(DL_INVALID_ARGUMENT, "set_sampler_engine: unknown engine");
+  DL_SERVE_CALL(s->impl->set_sampler_engine(engine));
+}
 DL_API dl_status dl_serve_set_tensor(dl_serve* s, size_t index, const void* host_bits, size_t bytes) {
   if (!host_bits) return fail(DL_INVALID_ARGUMENT, "serve_set_tensor: null");
   DL_SERVE_CALL(s->impl->set_tensor(index, host_bits, bytes));
@@ -668,6 +686,24 @@ DL_API dl_status dl_serve_prefill(dl_serve* s, const uint32_t* tokens, size_t pr
 DL_API dl_status dl_serve_decode(dl_serve* s, size_t steps, uint32_t* tokens_out, uint16_t* logits_out,
                                  dl_serve_stats* stats) {
   DL_SERVE_CALL(s->impl->decode(steps, tokens_out, logits_out, stats));
+}
+DL_API dl_status dl_serve_set_capture(dl_serve* s, int layer) { DL_SERVE_CALL(s->impl->set_capture(layer)); }
+DL_API dl_status dl_serve_read_capture(dl_serve* s, size_t sequence, size_t first, size_t count,
+                                       uint16_t* host_bits) {
+  if (!host_bits) return fail(DL_INVALID_ARGUMENT, "serve_read_capture: null");
+  DL_SERVE_CALL(s->impl->read_capture(sequence, first, count, host_bits));
+}
+DL_API dl_status dl_serve_set_steering(dl_serve* s, int layer, size_t first_position, float strength,
+                                       const float* host_direction, const uint8_t* host_sequence_mask,
+                                       int64_t source_sequence, size_t source_position) {
+  if (layer >= 0 && (!host_direction || !host_sequence_mask))
+    return fail(DL_INVALID_ARGUMENT, "serve_set_steering: direction and mask required");
+  DL_SERVE_CALL(s->impl->set_steering(layer, first_position, strength, host_direction, host_sequence_mask,
+                                      (long long)source_sequence, source_position));
+}
+DL_API dl_status dl_serve_steering_strength(dl_serve* s, float* beta) {
+  if (!beta) return fail(DL_INVALID_ARGUMENT, "serve_steering_strength: null");
+  DL_SERVE_CALL(*beta = s->impl->steering_strength());
 }
 DL_API size_t dl_serve_position(dl_serve* s) {
   if (!s || !s->impl) return 0;

@@ -34,6 +34,7 @@ enum : unsigned {
   kErrWaitEmpty = 2,   // producer gave up waiting for a free stage
   kErrBounds = 3,      // a device-side position/index check failed
   kErrGridSync = 4,    // a persistent kernel's grid barrier gave up waiting
+  kErrSteer = 5,       // a steering strength or steered value was not finite
 };
 
 __device__ __forceinline__ void record_error(unsigned* err, unsigned code) {

@@ -182,6 +182,7 @@ class Engine {
 
  public:
   void set_decode_path(int path);
+  void set_sampler_engine(int engine) { sampler_.engine = unsigned(engine); }
 };
 
 }  // namespace dl

@@ -9,7 +9,12 @@
 //    first i with cum/total >= top_p; selection = first i <= cutoff with
 //    u < cum/retained; u = (word >> 11) * 2^-53;
 //  * the device-owned stream is MT19937-64 (std::mt19937_64), one word per
-//    categorical selection, latched after a stop ID or a failed selection.
+//    categorical selection, latched after a stop ID or a failed selection;
+//    or, when selected, Philox4x32-10 (Salmon et al., SC'11): draw k of row r
+//    is the first two words of the block at counter {k lo, k hi, stream
+//    0x5A4D504C, 0} under key seed + r, w = (word1 << 32) | word0, with the
+//    same u = (w >> 11) * 2^-53.  The reference has only the MT19937-64
+//    stream; the Philox stream is stateless per draw (no 312-word state).
 // The stable order is produced by an LSD radix sort over the 32-bit keys.  For
 // BF16 logits the low 16 key bits are a function of the sign, so sorting on
 // the high 16 bits alone gives the same order (two passes instead of four).
@@ -18,6 +23,7 @@
 #include <type_traits>
 #include <vector>
 
+#include "qknorm.cuh"
 #include "sampler.h"
 
 namespace dl {
@@ -27,7 +33,13 @@ struct SamplerState {
   unsigned index, terminal;
   double draw;
   unsigned previous[2];
+  unsigned engine;   // DL_RNG_MT19937_64 or DL_RNG_PHILOX4X32_10
+  unsigned pad;
+  uint64_t key;      // Philox key: seed + row
+  uint64_t counter;  // Philox draws made
 };
+
+constexpr uint32_t kPhiloxSamplerStream = 0x5A4D504Cu;
 
 namespace {
 
@@ -94,9 +106,12 @@ __device__ __forceinline__ unsigned descending_key(float v) {
 }
 
 // ---- MT19937-64 -----------------------------------------------------------
-__global__ void seed_kernel(SamplerState* s, uint64_t seed, size_t stride) {
+__global__ void seed_kernel(SamplerState* s, uint64_t seed, size_t stride, unsigned engine) {
   s = at_row(s, stride);
   seed += blockIdx.y;  // row r draws from the stream seeded with seed + r
+  s->engine = engine;
+  s->key = seed;
+  s->counter = 0;
   s->words[0] = seed;
   for (unsigned i = 1; i < 312; ++i) {
     const uint64_t p = s->words[i - 1];
@@ -111,6 +126,14 @@ __global__ void seed_kernel(SamplerState* s, uint64_t seed, size_t stride) {
 __global__ void next_random_kernel(SamplerState* s, bool greedy, size_t stride) {
   s = at_row(s, stride);
   if (s->terminal || greedy) return;
+  if (s->engine == DL_RNG_PHILOX4X32_10) {
+    const uint64_t k = s->counter++;
+    uint32_t c[4] = {uint32_t(k), uint32_t(k >> 32), kPhiloxSamplerStream, 0u};
+    philox4x32_10(c, uint32_t(s->key), uint32_t(s->key >> 32));
+    const uint64_t w = (uint64_t(c[1]) << 32) | c[0];
+    s->draw = static_cast<double>(w >> 11) * 0x1.0p-53;
+    return;
+  }
   if (s->index == 312) {
     for (unsigned i = 0; i < 312; ++i) {
       const uint64_t x = (s->words[i] & 0xffffffff80000000ULL) | (s->words[(i + 1) % 312] & 0x7fffffffULL);
@@ -499,7 +522,7 @@ cudaError_t sampler_start(Sampler& s, const dl_sampling& settings, uint64_t seed
   if (e != cudaSuccess) return e;
   e = cudaStreamSynchronize(stream);
   if (e != cudaSuccess) return e;
-  seed_kernel<<<dim3(1, s.rows), 1, 0, stream>>>(s.state, seed, s.stride);
+  seed_kernel<<<dim3(1, s.rows), 1, 0, stream>>>(s.state, seed, s.stride, s.engine);
   s.settings = settings;
   s.started = true;
   return cudaGetLastError();

@@ -16,7 +16,8 @@ struct SamplerState;  // device-resident MT19937-64 words + latches
 
 // One sampler serves `rows` logits rows at once (every kernel launches with
 // gridDim.y = rows); row r owns the arena slice at r * stride bytes and draws
-// from the MT19937-64 stream seeded with seed + r.
+// from the device-owned stream (MT19937-64, or Philox4x32-10 when selected)
+// seeded with seed + r.
 struct Sampler {
   size_t vocabulary = 0;
   bool bf16_input = true;
@@ -28,6 +29,7 @@ struct Sampler {
   unsigned char* stop_mask = nullptr;
   dl_sampling settings = {0, 1.0, 0, 1.0};
   bool started = false;
+  unsigned engine = DL_RNG_MT19937_64;  // draw source of the device-owned stream (set before start)
 };
 
 // Settings law of src/inference/sampling/categorical.cpp:37-47; throws

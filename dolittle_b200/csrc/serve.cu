@@ -12,6 +12,7 @@
 #include "attention_prefill_tc.h"
 #include "gemm_tcgen05.h"
 #include "serve.h"
+#include "steering.h"
 
 namespace dl {
 
@@ -197,6 +198,8 @@ Server::~Server() {
   cudaFree(scratch_);
   cudaFree(kv_arena_);
   cudaFree(weight_arena_);
+  cudaFree(capture_);
+  cudaFree(steer_mem_);
   if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -477,6 +480,7 @@ void Server::prefill_sequence(size_t b, const uint32_t* tokens, size_t n) {
         gemm(xn_, D, y.wgu, rows, 2 * F, D, kGemmSwiGLU, 1, n0s, outs, lds);
       }
       row_projection_out(act_, F, y.wd, rows, F, false);
+      block_output_hooks(l, b, c0, rows);
     }
     if (c0 + rows == n)
       check(cudaMemcpyAsync(xlast_ + b * D_, residual_ + size_t(rows - 1) * D_, D_ * 2, cudaMemcpyDeviceToDevice,
@@ -529,6 +533,115 @@ void Server::prefill(const uint32_t* tokens, size_t prompt_len, const dl_samplin
   }
 }
 
+// Block-output hooks, in the reference's order: the steering edit, then the
+// capture of the (edited) rows.  Prompt chunk: rows c0 .. c0+rows-1 of
+// sequence b.  beta comes from the source sequence's row before its edit.
+void Server::block_output_hooks(size_t l, size_t b, size_t c0, int rows) {
+  const int D = int(D_);
+  if (int(l) == steer_layer_) {
+    if (steer_source_ == (long long)b && steer_source_pos_ >= c0 && steer_source_pos_ < c0 + size_t(rows)) {
+      check(launch_steer_beta(residual_ + (steer_source_pos_ - c0) * D_, D, steer_strength_, steer_beta_, err_,
+                              stream_),
+            "steer beta");
+      ++launches_;
+    }
+    check(launch_steer_rows(residual_, D, rows, nullptr, (long long)c0, false, steer_mask_ + b, steer_first_,
+                            steer_beta_, steer_dir_, err_, stream_),
+          "steer rows");
+    ++launches_;
+  }
+  if (int(l) == capture_layer_) {
+    check(cudaMemcpyAsync(capture_ + (b * capacity_ + c0) * D_, residual_, size_t(rows) * D_ * 2,
+                          cudaMemcpyDeviceToDevice, stream_),
+          "capture rows");
+  }
+}
+
+void Server::block_output_hooks_decode(size_t l) {
+  const int D = int(D_), B = int(batch_);
+  if (int(l) == steer_layer_) {
+    check(launch_steer_rows(residual_, D, B, position_, 0, true, steer_mask_, steer_first_, steer_beta_, steer_dir_,
+                            err_, stream_),
+          "steer rows");
+    ++launches_;
+  }
+  if (int(l) == capture_layer_) {
+    check(launch_capture_batch(residual_, capture_, capacity_ * D_, position_, D, B, stream_), "capture rows");
+    ++launches_;
+  }
+}
+
+void Server::set_capture(int layer) {
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  if (layer >= int(L_)) throw std::invalid_argument("capture layer out of range");
+  if (layer >= 0 && !capture_) {
+    check(cudaMalloc(&capture_, batch_ * capacity_ * D_ * 2), "capture arena");
+    check(cudaMemsetAsync(capture_, 0, batch_ * capacity_ * D_ * 2, stream_), "capture clear");
+  }
+  capture_layer_ = layer < 0 ? -1 : layer;
+  if (step_exec_) {
+    cudaGraphExecDestroy(step_exec_);
+    step_exec_ = nullptr;
+  }
+}
+
+void Server::read_capture(size_t sequence, size_t first, size_t count, uint16_t* host) {
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  if (!capture_ || sequence >= batch_ || first + count > capacity_) throw std::invalid_argument("capture range");
+  check(cudaMemcpyAsync(host, capture_ + (sequence * capacity_ + first) * D_, count * D_ * 2, cudaMemcpyDeviceToHost,
+                        stream_),
+        "read capture");
+  check(cudaStreamSynchronize(stream_), "read capture sync");
+}
+
+void Server::set_steering(int layer, size_t first, float strength, const float* direction, const uint8_t* mask,
+                          long long source_sequence, size_t source_position) {
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  if (layer >= int(L_)) throw std::invalid_argument("steering layer out of range");
+  if (step_exec_) {
+    cudaGraphExecDestroy(step_exec_);
+    step_exec_ = nullptr;
+  }
+  if (layer < 0) {
+    steer_layer_ = -1;
+    return;
+  }
+  if (!direction || !mask || !std::isfinite(strength)) throw std::invalid_argument("steering arguments");
+  for (size_t i = 0; i < D_; ++i)
+    if (!std::isfinite(direction[i])) throw std::invalid_argument("steering direction must be finite");
+  if (source_sequence >= 0) {
+    // beta comes from the source row in the prompt pass, before any masked
+    // sequence prefilled after it needs it.
+    if (size_t(source_sequence) >= batch_ || source_position >= capacity_)
+      throw std::invalid_argument("steering source out of range");
+    for (size_t b = 0; b < size_t(source_sequence); ++b)
+      if (mask[b]) throw std::invalid_argument("steered sequences must follow the strength source");
+  }
+  if (!steer_mem_) check(cudaMalloc(&steer_mem_, D_ * 4 + 256 + batch_), "steering state");
+  steer_dir_ = static_cast<float*>(steer_mem_);
+  steer_beta_ = reinterpret_cast<float*>(static_cast<unsigned char*>(steer_mem_) + D_ * 4);
+  steer_mask_ = static_cast<unsigned char*>(steer_mem_) + D_ * 4 + 256;
+  check(cudaMemcpyAsync(steer_dir_, direction, D_ * 4, cudaMemcpyHostToDevice, stream_), "steering direction");
+  check(cudaMemcpyAsync(steer_beta_, &strength, 4, cudaMemcpyHostToDevice, stream_), "steering strength");
+  check(cudaMemcpyAsync(steer_mask_, mask, batch_, cudaMemcpyHostToDevice, stream_), "steering mask");
+  check(cudaStreamSynchronize(stream_), "steering sync");
+  steer_layer_ = layer;
+  steer_first_ = (long long)first;
+  steer_strength_ = strength;
+  steer_source_ = source_sequence;
+  steer_source_pos_ = source_position;
+}
+
+float Server::steering_strength() {
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  float b = 0.f;
+  if (steer_beta_) {
+    check(cudaMemcpyAsync(&b, steer_beta_, 4, cudaMemcpyDeviceToHost, stream_), "steering strength");
+    check(cudaStreamSynchronize(stream_), "steering strength sync");
+  }
+  return b;
+}
+
 // One decode step for all B rows at the shared position.
 void Server::decode_body() {
   const int B = int(batch_), D = int(D_), Q = int(Ql_), G = int(Gl_), F = int(Fl_), d = int(d_);
@@ -565,6 +678,7 @@ void Server::decode_body() {
     check(launch_gemm_splitk_epilogue(parts_, parts, B, p.N, kGemmSwiGLU, act_, F, nullptr, stream_), "swiglu");
     launches_ += 3;
     row_projection_out(act_, F, y.wd, B, F, true);
+    block_output_hooks_decode(l);
   }
   check(launch_rms_norm(residual_, final_norm_, xn_, batch_, D, cfg_.epsilon, stream_), "final norm");
   {

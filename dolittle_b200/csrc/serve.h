@@ -42,6 +42,7 @@ class Server {
   void ipc_handle(unsigned char* out64);
   void connect_peers(const unsigned char* handles);
   void init_random(uint64_t seed, float sigma);
+  void set_sampler_engine(int engine) { sampler_.engine = unsigned(engine); }
   // Full tensor `index` (engine order) from the host; this rank keeps its slice.
   void set_tensor(size_t index, const void* host, size_t bytes);
   // This rank's slice of tensor `index` ([rows][cols] as held).
@@ -50,6 +51,15 @@ class Server {
   void prefill(const uint32_t* tokens, size_t prompt_len, const dl_sampling& s, uint64_t seed, uint32_t* first_out);
   void decode(size_t steps, uint32_t* tokens_out, uint16_t* logits_out, dl_serve_stats* stats);
   size_t position();
+  // Block `layer`'s output rows of every sequence and position (prompt and
+  // decode) into an arena [B][capacity][D]; layer < 0 disables.
+  void set_capture(int layer);
+  void read_capture(size_t sequence, size_t first, size_t count, uint16_t* host);
+  // Fixed-strength steering of every position >= first at block `layer` for
+  // the sequences in mask[B] (see dl_serve_set_steering); layer < 0 disables.
+  void set_steering(int layer, size_t first, float strength, const float* direction, const uint8_t* mask,
+                    long long source_sequence, size_t source_position);
+  float steering_strength();
 
  private:
   struct Slice {
@@ -64,6 +74,8 @@ class Server {
             bf16* const* outs, const int* lds);
   void row_projection_out(const bf16* x, int ldx, const bf16* w, int M, int K, bool decode);  // o / down
   void prefill_sequence(size_t b, const uint32_t* tokens, size_t n);
+  void block_output_hooks(size_t l, size_t b, size_t c0, int rows);  // prompt chunk rows of sequence b
+  void block_output_hooks_decode(size_t l);
   void decode_body();
   void all_reduce(float* buf, size_t n);
   void check(cudaError_t e, const char* what);
@@ -114,6 +126,18 @@ class Server {
   size_t launches_ = 0;
   double prefill_ms_ = 0.0;
   cudaEvent_t ev_[2] = {};
+  // block-output capture [B][capacity][D] and fixed-strength steering
+  int capture_layer_ = -1;
+  bf16* capture_ = nullptr;
+  int steer_layer_ = -1;
+  long long steer_first_ = 0;
+  float steer_strength_ = 0.f;
+  long long steer_source_ = -1;   // sequence whose row sets beta = strength * ||row||; -1: beta = strength
+  size_t steer_source_pos_ = 0;
+  void* steer_mem_ = nullptr;     // direction [D] FP32, beta, mask [B]
+  float* steer_dir_ = nullptr;
+  float* steer_beta_ = nullptr;
+  unsigned char* steer_mask_ = nullptr;
 };
 
 }  // namespace dl

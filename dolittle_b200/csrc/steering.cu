@@ -6,6 +6,11 @@
 // h' = round(h + beta*u) with finiteness latches; state = {invalid, count},
 // count making the edit one-shot (a second application is invalid).
 // normalize: src/kernels/cuda/injection.cu:48-102, out = BF16((h/||h||)*scale).
+// steer_rows / steer_beta: fixed-strength steering of every position from a
+// first one (no reference counterpart; the reference edits one row once):
+// beta = alpha * ||h_source|| by the intervene norm law, then the intervene
+// update h' = round(h + beta*u) on every selected row, so at the source row
+// it equals the one-row edit bit for bit.
 // direction: src/kernels/cuda/steering.cu:68-98 (DeviceDirection::submit,
 // :211-258).  delta_i = FP32(edited_i) - FP32(original_i); lane L of 8 sums
 // fmul(delta, delta) serially over i = L + 8k; lane 0 adds the 8 lane sums in
@@ -153,7 +158,88 @@ __global__ void direction_kernel(const T* original, const T* edited, float* out,
     out[i] = __fdiv_rn(__fsub_rn(float(edited[i]), float(original[i])), norm);
 }
 
+// Steering strength from a row: beta = alpha * ||h|| with the intervene
+// law's norm (8 strided lane sums of fmul(v, v), lanes added in order,
+// sqrt_rn), so a fixed-strength edit of that row equals the one-row edit.
+__global__ void steer_beta_kernel(const bf16* row, int width, float alpha, float* beta, unsigned* err) {
+  __shared__ float sums[kLanes];
+  if (threadIdx.x < kLanes) {
+    float s = 0.f;
+    for (int i = threadIdx.x; i < width; i += kLanes) {
+      const float v = widen(row[i]);
+      s = __fadd_rn(s, __fmul_rn(v, v));
+    }
+    sums[threadIdx.x] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.f;
+    for (int i = 0; i < kLanes; ++i) s = __fadd_rn(s, sums[i]);
+    const float b = __fmul_rn(alpha, __fsqrt_rn(s));
+    *beta = b;
+    if (!isfinite(b)) record_error(err, kErrSteer);
+  }
+}
+
+// Fixed-strength steering of every row at a position >= first: one CTA per
+// row, h' = round(h + fmul(beta, u)) (the intervene law's arithmetic).  Row r
+// sits at position (pos ? *pos : base) + (per_sequence ? 0 : r) and belongs
+// to sequence per_sequence ? r : 0 of `mask`.
+__global__ void steer_rows_kernel(bf16* residual, int width, const long long* pos, long long base, int per_sequence,
+                                  const unsigned char* mask, long long first, const float* beta,
+                                  const float* direction, unsigned* err) {
+  allow_next();
+  wait_prior();
+  const int r = blockIdx.x;
+  const long long p = (pos ? *pos : base) + (per_sequence ? 0 : r);
+  if (p < first || !mask[per_sequence ? r : 0]) return;
+  const float b = *beta;
+  bf16* row = residual + size_t(r) * width;
+  bool bad = !isfinite(b);
+  for (int i = threadIdx.x; i < width && !bad; i += blockDim.x) {
+    const float value = __fadd_rn(widen(row[i]), __fmul_rn(b, direction[i]));
+    const bf16 stored = narrow(value);
+    if (!isfinite(value) || !isfinite(widen(stored))) bad = true;
+    row[i] = stored;
+  }
+  if (bad) record_error(err, kErrSteer);
+}
+
+// arena[b][*position] = rows[b] for b < batch (block-output capture of a
+// lockstep batch at the shared position).
+__global__ void capture_batch_kernel(const bf16* rows, bf16* arena, size_t seq_stride, const long long* position,
+                                     int width) {
+  allow_next();
+  wait_prior();
+  const int b = blockIdx.x;
+  const uint4* src = reinterpret_cast<const uint4*>(rows + size_t(b) * width);
+  uint4* dst = reinterpret_cast<uint4*>(arena + b * seq_stride + size_t(*position) * width);
+  for (int i = threadIdx.x; i < width / 8; i += blockDim.x) dst[i] = src[i];
+}
+
 }  // namespace
+
+cudaError_t launch_steer_beta(const bf16* row, int width, float alpha, float* beta, unsigned* err,
+                              cudaStream_t stream) {
+  steer_beta_kernel<<<1, 32, 0, stream>>>(row, width, alpha, beta, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_steer_rows(bf16* residual, int width, int rows, const long long* position, long long base,
+                              bool per_sequence, const unsigned char* mask, long long first, const float* beta,
+                              const float* direction, unsigned* err, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  steer_rows_kernel<<<rows, 256, 0, stream>>>(residual, width, position, base, per_sequence ? 1 : 0, mask, first,
+                                              beta, direction, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_capture_batch(const bf16* rows, bf16* arena, size_t seq_stride, const long long* position,
+                                 int width, int batch, cudaStream_t stream) {
+  if (width % 8) return cudaErrorInvalidValue;
+  capture_batch_kernel<<<batch, 128, 0, stream>>>(rows, arena, seq_stride, position, width);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_direction(bool bf16_input, const void* original, const void* edited, float* out,
                              unsigned* status, int width, cudaStream_t stream) {

@@ -167,6 +167,11 @@ class Engine:
         DL_DECODE_KERNELS (per-operation kernels); the results are identical."""
         check(lib().dl_engine_set_decode_path(self._h, path))
 
+    def set_sampler_engine(self, engine: int) -> None:
+        """Draw source of later categorical generations: DL_RNG_MT19937_64
+        (the reference's stream, default) or DL_RNG_PHILOX4X32_10."""
+        check(lib().dl_engine_set_sampler_engine(self._h, engine))
+
     def set_injection(self, position: int, source_bits=None, scale: float = 150.0) -> None:
         """Verbalizer injection: prompt position `position` gets
         BF16((h/||h||) * scale) of the BF16 row `source_bits` instead of its

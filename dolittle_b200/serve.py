@@ -73,6 +73,44 @@ class Server:
     def init_random(self, seed: int, sigma: float = 0.02) -> None:
         check(lib().dl_serve_init_random(self._h, seed, sigma))
 
+    def set_sampler_engine(self, engine: int) -> None:
+        """Draw source of later prefills' sequences (DL_RNG_*)."""
+        check(lib().dl_serve_set_sampler_engine(self._h, engine))
+
+    def set_capture(self, layer: int) -> None:
+        """Block `layer`'s output rows of every sequence and position; -1 off."""
+        check(lib().dl_serve_set_capture(self._h, layer))
+
+    def read_capture(self, sequence: int, first: int, count: int) -> np.ndarray:
+        out = np.empty((count, self.config.hidden), np.uint16)
+        check(lib().dl_serve_read_capture(self._h, sequence, first, count, out.ctypes.data_as(_lib.u16p)))
+        return out
+
+    def set_steering(self, layer: int, first_position: int = 0, strength: float = 0.0, direction=None,
+                     sequences=(), source_sequence: int = -1, source_position: int = 0) -> None:
+        """Fixed-strength steering of every position >= first_position at
+        block `layer` for the listed sequences: h' = round(h + beta*u).
+        beta = strength, or strength * ||h|| of sequence source_sequence's
+        block output at source_position (computed in the prompt pass).
+        layer < 0 turns it off."""
+        if layer < 0:
+            check(lib().dl_serve_set_steering(self._h, -1, 0, 0.0, None, None, -1, 0))
+            return
+        u = np.ascontiguousarray(direction, np.float32)
+        if u.size != self.config.hidden:
+            raise ValueError("steering direction must have the hidden width")
+        mask = np.zeros(self.batch, np.uint8)
+        mask[list(sequences)] = 1
+        check(lib().dl_serve_set_steering(self._h, layer, first_position, strength,
+                                          u.ctypes.data_as(C.POINTER(C.c_float)),
+                                          mask.ctypes.data_as(C.POINTER(C.c_uint8)), source_sequence,
+                                          source_position))
+
+    def steering_strength(self) -> float:
+        b = C.c_float()
+        check(lib().dl_serve_steering_strength(self._h, C.byref(b)))
+        return b.value
+
     def set_tensor(self, index: int, full_bits: np.ndarray) -> None:
         b = np.ascontiguousarray(full_bits, dtype=np.uint16)
         check(lib().dl_serve_set_tensor(self._h, index, b.ctypes.data, b.nbytes))

@@ -196,7 +196,18 @@ typedef struct {
 DL_API size_t dl_sampler_required_bytes(size_t vocabulary);
 DL_API dl_status dl_sampler_create(size_t vocabulary, dl_dtype type, dl_sampler** out);
 DL_API void dl_sampler_destroy(dl_sampler* s);
-/* Seed the device MT19937-64 stream and the stop-ID mask. */
+/* Draw source of the device-owned stream (dl_sampler_submit_next and the
+ * engine / server sequences).  DL_RNG_MT19937_64 is the reference's stream
+ * (std::mt19937_64 seeded with the seed, src/kernels/cuda/sampling.cu:
+ * 106-137) and the default; DL_RNG_PHILOX4X32_10 is a counter-based stream
+ * with no counterpart in the reference: draw k of row r is the first two
+ * 32-bit words w0, w1 of Philox4x32-10 (Salmon et al., SC'11) at counter
+ * {k mod 2^32, k >> 32, 0x5A4D504C, 0} under key seed + r (low word first),
+ * u = (((w1 << 32) | w0) >> 11) * 2^-53.  The selection law given u is the
+ * same for both.  Set before dl_sampler_start. */
+enum { DL_RNG_MT19937_64 = 0, DL_RNG_PHILOX4X32_10 = 1 };
+DL_API dl_status dl_sampler_set_engine(dl_sampler* s, int engine);
+/* Seed the device-owned stream and the stop-ID mask. */
 DL_API dl_status dl_sampler_start(dl_sampler* s, const dl_sampling* settings, uint64_t seed,
                                   const uint32_t* stop_ids, size_t n_stop, void* stream);
 /* One selection of a device logits row; result = device {token, status}. */
@@ -304,6 +315,9 @@ DL_API dl_status dl_engine_set_observation(dl_engine* e, void* device_rows, size
 DL_API dl_status dl_engine_set_intervention(dl_engine* e, int layer, size_t selected,
                                             float strength, const float* host_direction);
 DL_API dl_status dl_engine_set_decode_path(dl_engine* e, int path);
+/* Draw source of later generations' categorical selections (DL_RNG_*, see
+ * dl_sampler_set_engine); the default is the reference's MT19937-64. */
+DL_API dl_status dl_engine_set_sampler_engine(dl_engine* e, int engine);
 /* Verbalizer (AV) injection: every later prompt pass replaces the embedding
  * of absolute position `position` with BF16((h / ||h||) * scale) of the BF16
  * row `source_bits` [D] (DeviceInjection::normalize + the marker-row replace,
@@ -366,6 +380,8 @@ DL_API dl_status dl_serve_connect_peers(dl_serve* s, const unsigned char* handle
 /* Seeded weights as dl_engine_init_random; each rank generates only its
  * slice of the same tensors. */
 DL_API dl_status dl_serve_init_random(dl_serve* s, uint64_t seed, float sigma);
+/* Draw source of later prefills' sequences (DL_RNG_*; row r uses seed + r). */
+DL_API dl_status dl_serve_set_sampler_engine(dl_serve* s, int engine);
 /* Full tensor `index` (engine order, host BF16 bits); the rank keeps its
  * slice.  dl_serve_get_tensor returns the slice [rows][cols] held, at
  * rows r0.., columns c0.. of the full tensor (dl_serve_slice_shape). */
@@ -383,6 +399,31 @@ DL_API dl_status dl_serve_prefill(dl_serve* s, const uint32_t* tokens, size_t pr
 DL_API dl_status dl_serve_decode(dl_serve* s, size_t steps, uint32_t* tokens_out, uint16_t* logits_out,
                                  dl_serve_stats* stats);
 DL_API size_t dl_serve_position(dl_serve* s);
+/* Block `layer`'s output rows (after any steering edit, as the reference
+ * captures, src/inference/executor.cpp:1633-1656) of every sequence at every
+ * prompt and decode position into an arena [batch][capacity][D] the server
+ * allocates on first use; layer < 0 disables.  Read back one sequence's rows
+ * [first, first + count) as BF16 bits. */
+DL_API dl_status dl_serve_set_capture(dl_serve* s, int layer);
+DL_API dl_status dl_serve_read_capture(dl_serve* s, size_t sequence, size_t first, size_t count,
+                                       uint16_t* host_bits);
+/* Fixed-strength steering of every position from first_position on, at the
+ * output of block `layer`, for the sequences whose host_sequence_mask[b] is
+ * nonzero (prompt and decode rows): h' = round(h + beta * u) with the
+ * arithmetic of the reference's one-row edit (src/kernels/cuda/
+ * steering.cu:106-159), u = host_direction [D] (FP32).  No counterpart in the
+ * reference, which edits one row once.  source_sequence < 0: beta = strength.
+ * Otherwise beta = strength * ||h|| of sequence source_sequence's block
+ * output at source_position before its edit (the one-row edit's norm law),
+ * computed on the device during the prompt pass; the edit of that row then
+ * equals the reference's one-row edit of it bit for bit.  Sequences prefilled
+ * before the source may not be steered.  layer < 0 disables.  Applies from
+ * the next prefill / decode call. */
+DL_API dl_status dl_serve_set_steering(dl_serve* s, int layer, size_t first_position, float strength,
+                                       const float* host_direction, const uint8_t* host_sequence_mask,
+                                       int64_t source_sequence, size_t source_position);
+/* The beta the steering edit used (host read). */
+DL_API dl_status dl_serve_steering_strength(dl_serve* s, float* beta);
 
 /* Split-K GEMM for few rows: Y = epilogue(X W^T) as dl_gemm_bf16, the K
  * extent cut in `parts` (0 = fill the SMs) whose FP32 partials

@@ -393,6 +393,41 @@ OR_API uint32_t or_direction(int bf16, const void* original, const void* edited,
   return 0u;
 }
 
+/* Fixed-strength steering (no reference counterpart; the reference edits one
+ * row once, or_intervene): beta = alpha * sqrt(8-lane sum of v*v) of a source
+ * row, the one-row edit's norm law; then every row at a position >= first gets
+ * h' = round(h + beta * u).  Returns 1 if a value or beta is not finite.     */
+OR_API float or_steer_beta(const uint16_t* row, size_t width, float alpha) {
+  float sums[8];
+  for (int l = 0; l < 8; ++l) {
+    float s = 0.0f;
+    for (size_t i = (size_t)l; i < width; i += 8) {
+      float v = bf(row[i]);
+      s = s + v * v;
+    }
+    sums[l] = s;
+  }
+  float sum = 0.0f;
+  for (int l = 0; l < 8; ++l) sum = sum + sums[l];
+  return alpha * sqrtf(sum);
+}
+
+OR_API uint32_t or_steer_rows(uint16_t* residual, const float* direction, size_t width, size_t rows,
+                              size_t first_position, size_t steer_from, float beta) {
+  uint32_t bad = isfinite(beta) ? 0u : 1u;
+  for (size_t r = 0; r < rows && !bad; ++r) {
+    if (first_position + r < steer_from) continue;
+    uint16_t* row = residual + r * width;
+    for (size_t i = 0; i < width; ++i) {
+      float value = bf(row[i]) + beta * direction[i];
+      uint16_t stored = to_bf(value);
+      if (!isfinite(value) || !isfinite(bf(stored))) bad = 1;
+      row[i] = stored;
+    }
+  }
+  return bad;
+}
+
 /* Injection normalisation: src/kernels/cuda/injection.cu:48-102.           */
 OR_API uint32_t or_normalize_injection(const uint16_t* source, uint16_t* out,
                                        size_t width, float scale,

@@ -97,6 +97,10 @@ def lib():
         L.or_normalize_injection.restype = C.c_uint32
         L.or_normalize_injection.argtypes = [u16p, u16p, sz, C.c_float,
                                              C.POINTER(C.c_float)]
+        L.or_steer_beta.restype = C.c_float
+        L.or_steer_beta.argtypes = [u16p, sz, C.c_float]
+        L.or_steer_rows.restype = C.c_uint32
+        L.or_steer_rows.argtypes = [u16p, f32p, sz, sz, sz, sz, C.c_float]
         L.or_direction.restype = C.c_uint32
         L.or_direction.argtypes = [C.c_int, C.c_void_p, C.c_void_p, sz, f32p]
         L.or_mt64_seed.argtypes = [C.c_void_p, C.c_uint64]
@@ -206,6 +210,21 @@ def uniform_ids(n, seed, stream, bound):
     return out
 
 
+def steer_beta(row_bits, alpha):
+    """alpha * ||h|| with the one-row edit's norm law (FP32)."""
+    r = np.ascontiguousarray(row_bits, np.uint16).reshape(-1)
+    return np.float32(lib().or_steer_beta(r, r.size, alpha))
+
+
+def steer_rows(rows_bits, direction, first_position, steer_from, beta):
+    """Rows [n][D] at positions first_position + r: those >= steer_from get
+    round(h + beta * u).  Returns (status, new rows)."""
+    h = np.array(rows_bits, np.uint16, copy=True, order="C")
+    u = np.ascontiguousarray(direction, np.float32)
+    st = lib().or_steer_rows(h, u, h.shape[1], h.shape[0], first_position, steer_from, beta)
+    return int(st), h
+
+
 def direction(original, edited):
     """(status, FP32 direction) of the DeviceDirection law; inputs are BF16
     bits (uint16) or FP32 arrays of one width.  On status 1 the direction
@@ -217,6 +236,18 @@ def direction(original, edited):
     out = np.full(a.size, np.nan, np.float32)
     status = lib().or_direction(int(bf16), a.ctypes.data, b.ctypes.data, a.size, out)
     return int(status), out
+
+
+PHILOX_SAMPLER_STREAM = 0x5A4D504C
+
+
+def philox_word(seed: int, k: int) -> int:
+    """Draw k of the sampler's Philox4x32-10 stream under key `seed`: the
+    first two words of the block at counter {k lo, k hi, 0x5A4D504C, 0}, low
+    word first (the same generator as or_fill_normal_bf16)."""
+    out = np.zeros(4, np.uint32)
+    lib().or_philox(C.c_uint64(seed), PHILOX_SAMPLER_STREAM, C.c_uint64(k), out)
+    return (int(out[1]) << 32) | int(out[0])
 
 
 class MT64:

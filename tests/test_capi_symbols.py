@@ -37,6 +37,10 @@ def test_invalid_arguments_are_rejected_before_any_launch():
     assert L.dl_projection(dl.DL_F32, None, None, None, 1, 8, 8, None, None) == _lib.DL_UNSUPPORTED
     assert L.dl_projection(dl.DL_BF16, None, None, None, 1, 8, 8, None, None) == _lib.DL_INVALID_ARGUMENT
     assert b"null" in L.dl_last_error()
+    # The draw source is chosen from the two known engines only.
+    assert L.dl_sampler_set_engine(None, dl.DL_RNG_PHILOX4X32_10) == _lib.DL_INVALID_ARGUMENT
+    assert L.dl_engine_set_sampler_engine(None, 5) == _lib.DL_INVALID_ARGUMENT
+    assert L.dl_direction(dl.DL_BF16, None, None, 8, None, None, None) == _lib.DL_INVALID_ARGUMENT
     with pytest.raises(dl.DolittleError):
         dl.Qwen3Config().tensor_shape(10_000)
 

@@ -302,3 +302,68 @@ def test_intervene_and_injection_bit_exact_vs_law():
     nrm = C.c_float()
     assert oracle.lib().or_normalize_injection(src, exp2, D, 150.0, C.byref(nrm)) == 0
     assert np.array_equal(gu.from_dev_u16(out), exp2)
+
+
+# ---------------------------------------------------------------------------
+# Philox4x32-10 draw source (selectable; the reference's stream is MT19937-64)
+# ---------------------------------------------------------------------------
+def test_sampler_philox_stream_matches_law_and_is_deterministic():
+    """Draw k of row 0 comes from the Philox block at counter k under key
+    seed; each selection equals the device law (oracle) given that word.
+    Same seed -> same sequence; another seed -> another sequence."""
+    n = 8449
+    logits = _device_cases(n)
+    row = gu.to_dev(nm.f32_to_bf16_bits(logits))
+    st = dl.Settings(dl.SelectionMode.categorical, 0.7, 0, 0.9)
+
+    def run(seed, draws):
+        smp = _Sampler(n, True)
+        try:
+            assert dl.lib().dl_sampler_set_engine(smp.h, dl.DL_RNG_PHILOX4X32_10) == 0
+            s = st.c()
+            assert dl.lib().dl_sampler_start(smp.h, C.byref(s), seed, None, 0, None) == 0
+            # The engine is fixed once the stream is seeded.
+            assert dl.lib().dl_sampler_set_engine(smp.h, dl.DL_RNG_MT19937_64) != 0
+            out = []
+            for _ in range(draws):
+                res = C.c_void_p()
+                assert dl.lib().dl_sampler_submit_next(smp.h, gu.ptr(row), None, C.byref(res)) == 0
+                out.append(smp._read(res))
+            return out
+        finally:
+            smp.close()
+
+    bf = nm.bf16_bits_to_f32(nm.f32_to_bf16_bits(logits))
+    a = run(7, 64)
+    for k, got in enumerate(a):
+        want = oracle.select_device(bf, True, st.temperature, st.top_k, st.top_p, oracle.philox_word(7, k))
+        assert got == want, k
+    assert run(7, 64) == a
+    assert run(8, 64) != a
+
+
+def test_engine_generation_with_philox_draws_matches_law():
+    """A categorical generation through the engine's device loop with the
+    Philox source: every selected token equals the device law on that step's
+    logits with draw k of the stream seeded with the generation's seed."""
+    cfg = dl.Qwen3Config(hidden=256, query_heads=4, kv_heads=2, head_width=64, mlp_width=512,
+                         vocabulary=1000, layers=2)
+    e = dl.Engine(cfg, capacity=64, max_rows=8)
+    e.init_random(3, 0.02)
+    e.set_sampler_engine(dl.DL_RNG_PHILOX4X32_10)
+    st = dl.Settings(dl.SelectionMode.categorical, 0.9, 0, 0.95)
+    prompt = oracle.uniform_ids(9, 1, 3, cfg.vocabulary)
+    g = e.generate(prompt, 12, settings=st, seed=11, want_logits=True)
+    assert g.status == 0 and len(g.tokens) == 12
+    for k in range(12):
+        want = oracle.select_device(nm.bf16_bits_to_f32(g.logits[k]), True, st.temperature, st.top_k, st.top_p,
+                                    oracle.philox_word(11, k))
+        assert g.tokens[k] == want[0], k
+    # The reference's MT19937-64 stream stays the default (and selectable).
+    e.set_sampler_engine(dl.DL_RNG_MT19937_64)
+    g2 = e.generate(prompt, 12, settings=st, seed=11, want_logits=True)
+    mt = oracle.MT64(11)
+    for k in range(12):
+        want = oracle.select_device(nm.bf16_bits_to_f32(g2.logits[k]), True, st.temperature, st.top_k, st.top_p, mt())
+        assert g2.tokens[k] == want[0], k
+    e.close()
