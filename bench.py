@@ -467,7 +467,7 @@ def serve_measure(world, rank, local, dist, batch, prompt_len, steps, calls, war
         total_steps = calls * steps
         Dm, Lm, d = cfg.hidden, cfg.layers, cfg.head_width
         w_layer = Dm * (cfg.query_heads * d + 2 * cfg.kv_heads * d) + cfg.query_heads * d * Dm + 3 * Dm * cfg.mlp_width
-        weights = 2 * (Lm * w_layer / world + Dm * V)
+        weights = 2 * (Lm * w_layer + Dm * V) / world  # blocks and vocabulary head are split over the ranks
         S0 = prompt_len + warmup * steps
         mean_S = S0 + total_steps / 2.0
         kv_bytes = batch * mean_S * Lm * 2 * (cfg.kv_heads // world) * d * 2
@@ -728,7 +728,7 @@ def run_steer_batch(args):
         tokens = args.steps * 2 * new_tokens
         D, d, Lm = cfg.hidden, cfg.head_width, cfg.layers
         w_layer = D * (cfg.query_heads * d + 2 * cfg.kv_heads * d) + cfg.query_heads * d * D + 3 * D * cfg.mlp_width
-        step_bytes = 2 * (Lm * w_layer / world + D * V) + 2 * (P + new_tokens / 2) * Lm * 2 * (cfg.kv_heads // world) * d * 2
+        step_bytes = 2 * (Lm * w_layer + D * V) / world + 2 * (P + new_tokens / 2) * Lm * 2 * (cfg.kv_heads // world) * d * 2
         ms_step = 1000 * decode_s / (args.steps * new_tokens)
         achieved = step_bytes / (ms_step * 1e-3) / 1e9
         line = {

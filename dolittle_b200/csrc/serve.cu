@@ -26,6 +26,7 @@ struct NcclApi {
   ncclResult_t (*get_unique_id)(ncclUniqueId*);
   ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int);
   ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
   ncclResult_t (*comm_destroy)(ncclComm_t);
   const char* (*error_string)(ncclResult_t);
 };
@@ -39,9 +40,11 @@ const NcclApi& nccl() {
     a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
     a.comm_init_rank = reinterpret_cast<decltype(a.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
     a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    a.all_gather = reinterpret_cast<decltype(a.all_gather)>(dlsym(h, "ncclAllGather"));
     a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
     a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
-    if (!a.get_unique_id || !a.comm_init_rank || !a.all_reduce || !a.comm_destroy || !a.error_string)
+    if (!a.get_unique_id || !a.comm_init_rank || !a.all_reduce || !a.all_gather || !a.comm_destroy ||
+        !a.error_string)
       throw std::runtime_error("libnccl.so.2 lacks the NCCL 2 API");
     return a;
   }();
@@ -72,8 +75,15 @@ Server::Server(const dl_model_config& cfg, int device, size_t batch, size_t capa
   Ql_ = size_t(hq_) * d_;
   Gl_ = size_t(hkv_) * d_;
   Fl_ = cfg.mlp_width / tp_;
+  // The vocabulary head is split by rows too: rank r holds vocabulary rows
+  // [r V/t, (r+1) V/t), padded with zero rows to a multiple of 128 (the GEMM
+  // tile); the ranks' logits meet in an all-gather.
+  if (V_ % size_t(tp_)) throw std::invalid_argument("tensor-parallel size must divide the vocabulary");
+  Vl_ = V_ / tp_;
+  Vp_ = tp_ == 1 ? V_ : align_up(Vl_, 128);
   if (!batch || batch > 128 || !capacity || !chunk_rows || chunk_rows > 4096 || cfg.query_heads % cfg.kv_heads ||
-      d_ != 128 || D_ % 128 || V_ % 128 || Ql_ % 128 || !L_ || !attention_prefill_tc_supported(hq_, hkv_, int(d_)))
+      d_ != 128 || D_ % 128 || V_ % 128 || Ql_ % 128 || (tp_ > 1 && Vl_ % 8) || !L_ ||
+      !attention_prefill_tc_supported(hq_, hkv_, int(d_)))
     throw std::invalid_argument("unsupported serving configuration");
   check(cudaSetDevice(device), "cudaSetDevice");
   check(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, device), "sm count");
@@ -87,7 +97,7 @@ Server::Server(const dl_model_config& cfg, int device, size_t batch, size_t capa
     off = align_up(off + elems * 2, 256);
     return o;
   };
-  const size_t o_embed = take(V_ * D_), o_final = take(D_), o_head = take(V_ * D_);
+  const size_t o_embed = take(V_ * D_), o_final = take(D_), o_head = take(Vp_ * D_);
   std::vector<size_t> lo(L_ * 8);
   for (size_t l = 0; l < L_; ++l) {
     lo[l * 8 + 0] = take(D_);
@@ -100,6 +110,7 @@ Server::Server(const dl_model_config& cfg, int device, size_t batch, size_t capa
     lo[l * 8 + 7] = take(D_ * Fl_);
   }
   check(cudaMalloc(&weight_arena_, off), "weights");
+  check(cudaMemsetAsync(weight_arena_, 0, off, stream_), "weights clear");  // zero padding rows of the head slice
   auto* base = static_cast<unsigned char*>(weight_arena_);
   embed_ = reinterpret_cast<bf16*>(base + o_embed);
   final_norm_ = reinterpret_cast<bf16*>(base + o_final);
@@ -144,6 +155,7 @@ Server::Server(const dl_model_config& cfg, int device, size_t batch, size_t capa
   const size_t o_res = grab(R * D_ * 2), o_xn = grab(R * D_ * 2), o_qkv = grab(B * (Ql_ + 2 * Gl_) * 2),
                o_qraw = grab(R * Ql_ * 2), o_kraw = grab(R * Gl_ * 2), o_qrot = grab(R * Ql_ * 2),
                o_att = grab(R * Ql_ * 2), o_act = grab(R * Fl_ * 2), o_logits = grab(B * V_ * 2),
+               o_hlocal = grab(tp_ > 1 ? B * Vp_ * 2 : 0), o_hgather = grab(tp_ > 1 ? size_t(tp_) * B * Vp_ * 2 : 0),
                o_xlast = grab(B * D_ * 2), o_vt = grab(size_t(hkv_) * d_ * vt_stride_ * 2),
                o_parts = grab(parts_floats_ * 4),
                o_ws = grab(attention_decode_ws_floats(int(B), hq_, attn_splits_) * 4), o_tok = grab(R * 4),
@@ -161,6 +173,8 @@ Server::Server(const dl_model_config& cfg, int device, size_t batch, size_t capa
   att_ = reinterpret_cast<bf16*>(sb + o_att);
   act_ = reinterpret_cast<bf16*>(sb + o_act);
   logits_ = reinterpret_cast<bf16*>(sb + o_logits);
+  head_local_ = reinterpret_cast<bf16*>(sb + o_hlocal);
+  head_gather_ = reinterpret_cast<bf16*>(sb + o_hgather);
   xlast_ = reinterpret_cast<bf16*>(sb + o_xlast);
   vt_ = reinterpret_cast<bf16*>(sb + o_vt);
   parts_ = reinterpret_cast<float*>(sb + o_parts);
@@ -275,7 +289,11 @@ Server::Slice Server::slice(size_t index) {
   Slice s{nullptr, fr, fc, fc, 0, 0, fc};
   if (index == 0) s.ptr = embed_;
   else if (index == 1) s.ptr = final_norm_;
-  else if (index == 2) s.ptr = lm_head_;
+  else if (index == 2) {
+    s.ptr = lm_head_;
+    s.rows = Vl_;
+    s.r0 = size_t(rank_) * Vl_;
+  }
   else {
     const size_t l = (index - 3) / 11, role = (index - 3) % 11;
     const Layer& y = layers_[l];
@@ -392,6 +410,26 @@ void Server::gemm(const bf16* x, int ldx, const bf16* w, int M, int N, int K, in
   ++launches_;
 }
 
+// Logits [B][V] of the B normed rows in xn_.  One rank: one GEMM.  Several
+// ranks: this rank's vocabulary rows [B][Vp], the all-gather of every rank's
+// rows, then the ranks' valid columns into [B][V] (every rank then samples
+// the same tokens from the same logits).
+void Server::vocabulary_head(int B) {
+  const int n0s[1] = {0};
+  const int lds[1] = {int(Vp_)};
+  if (tp_ == 1) {
+    bf16* outs[1] = {logits_};
+    gemm(xn_, int(D_), lm_head_, B, int(V_), int(D_), kGemmStore, 1, n0s, outs, lds);
+    return;
+  }
+  bf16* outs[1] = {head_local_};
+  gemm(xn_, int(D_), lm_head_, B, int(Vp_), int(D_), kGemmStore, 1, n0s, outs, lds);
+  check_nccl(nccl().all_gather(head_local_, head_gather_, size_t(B) * Vp_, ncclBfloat16, comm_, stream_),
+             "ncclAllGather");
+  check(launch_gather_vocab_slices(head_gather_, logits_, tp_, B, int(Vl_), int(Vp_), stream_), "vocab gather");
+  launches_ += 2;
+}
+
 void Server::all_reduce(float* buf, size_t n) {
   check_nccl(nccl().all_reduce(buf, buf, n, ncclFloat, ncclSum, comm_, stream_), "ncclAllReduce");
 }
@@ -502,12 +540,7 @@ void Server::prefill(const uint32_t* tokens, size_t prompt_len, const dl_samplin
   // (the sampler feeds the token's embedding row in as the next input).
   const int B = int(batch_);
   check(launch_rms_norm(xlast_, final_norm_, xn_, batch_, int(D_), cfg_.epsilon, stream_), "final norm");
-  {
-    const int n0s[1] = {0};
-    bf16* outs[1] = {logits_};
-    const int lds[1] = {int(V_)};
-    gemm(xn_, int(D_), lm_head_, B, int(V_), int(D_), kGemmStore, 1, n0s, outs, lds);
-  }
+  vocabulary_head(B);
   check(cudaMemsetAsync(steps_, 0, batch_ * 4, stream_), "steps");
   // Row b draws from the stream seeded with seed + b.
   check(sampler_start(sampler_, s, seed, nullptr, 0, stream_), "sampler start");
@@ -681,12 +714,7 @@ void Server::decode_body() {
     block_output_hooks_decode(l);
   }
   check(launch_rms_norm(residual_, final_norm_, xn_, batch_, D, cfg_.epsilon, stream_), "final norm");
-  {
-    const int n0s[1] = {0};
-    bf16* outs[1] = {logits_};
-    const int lds[1] = {int(V_)};
-    gemm(xn_, D, lm_head_, B, int(V_), D, kGemmStore, 1, n0s, outs, lds);
-  }
+  vocabulary_head(B);
   check(sampler_submit(sampler_, logits_, settings_, 0, true, stream_, V_), "sampler");
   check(sampler_feed(sampler_, history_, steps_, embed_, residual_, D, nullptr, stream_, history_cap_), "sampler feed");
   launches_ += sampler_launch_count(sampler_, settings_, true) + 1;

@@ -11,7 +11,8 @@
 //  * tensor parallelism over KV-head groups (rank r of t holds query heads
 //    [r Hq/t, (r+1) Hq/t), the matching KV heads and MLP columns): q/k/v and
 //    gate/up are column slices, o_proj and down_proj row slices whose FP32
-//    partial sums meet in an NCCL all-reduce before the residual add.
+//    partial sums meet in an NCCL all-reduce before the residual add; the
+//    vocabulary head is split by rows, its logits meeting in an all-gather.
 // All sequences have the same prompt length and advance together, so one
 // device position serves the batch.  The decode step is one CUDA graph
 // (the all-reduces included).
@@ -78,6 +79,7 @@ class Server {
   void block_output_hooks_decode(size_t l);
   void decode_body();
   void all_reduce(float* buf, size_t n);
+  void vocabulary_head(int rows);
   void check(cudaError_t e, const char* what);
   void check_nccl(ncclResult_t r, const char* what);
   void check_fault();
@@ -88,6 +90,7 @@ class Server {
   int rank_, tp_;
   int hq_, hkv_;        // local heads
   size_t D_, Ql_, Gl_, Fl_, V_, d_, L_;
+  size_t Vl_ = 0, Vp_ = 0;  // vocabulary rows of this rank, padded to the GEMM tile
   cudaStream_t stream_ = nullptr;
   ncclComm_t comm_ = nullptr;
   // peer all-reduce: this rank's slots + flags, the peers' mapped copies
@@ -107,6 +110,7 @@ class Server {
   // scratch
   void* scratch_ = nullptr;
   bf16 *residual_, *xn_, *qkv_, *q_raw_, *k_raw_, *q_rot_, *att_, *act_, *logits_, *xlast_, *vt_;
+  bf16 *head_local_ = nullptr, *head_gather_ = nullptr;  // tensor parallelism: [B][Vp], [tp][B][Vp]
   float *parts_, *attn_ws_;
   size_t parts_floats_ = 0;
   uint32_t* tokens_dev_;

@@ -406,6 +406,28 @@ cudaError_t launch_peer_allreduce_residual(const PeerBuffers& pb, const float* p
   return cudaGetLastError();
 }
 
+__global__ void gather_vocab_slices_kernel(const bf16* src, bf16* dst, int ranks, int batch, int vl, int vp) {
+  // 16-byte moves: vl and vp are multiples of 8 (checked by the launcher).
+  const int per_row = vl / 8;
+  const size_t n = size_t(ranks) * batch * per_row;
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
+    const int c = int(i % per_row);
+    const size_t rb = i / per_row;
+    const int b = int(rb % batch), r = int(rb / batch);
+    const uint4 v = *reinterpret_cast<const uint4*>(src + (size_t(r) * batch + b) * vp + 8 * c);
+    *reinterpret_cast<uint4*>(dst + size_t(b) * ranks * vl + size_t(r) * vl + 8 * c) = v;
+  }
+}
+
+cudaError_t launch_gather_vocab_slices(const bf16* src, bf16* dst, int ranks, int batch, int vl, int vp,
+                                       cudaStream_t stream) {
+  if (vl % 8 || vp % 8 || vl > vp) return cudaErrorInvalidValue;
+  const size_t n = size_t(ranks) * batch * (vl / 8);
+  gather_vocab_slices_kernel<<<int(std::min<size_t>((n + 255) / 256, 1184)), 256, 0, stream>>>(src, dst, ranks, batch,
+                                                                                               vl, vp);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_add_fp32_residual(const float* sum, bf16* residual, size_t n, cudaStream_t stream) {
   add_fp32_residual_kernel<<<grid_for(n), 256, 0, stream>>>(sum, residual, n);
   return cudaGetLastError();

@@ -41,6 +41,11 @@ cudaError_t launch_attention_decode_batched(const bf16* q, KvPlanes planes, cons
                                             int query_heads, int kv_heads, int splits, float scale, float* ws,
                                             bf16* out, cudaStream_t stream);
 
+// Vocabulary-split head: src [t][B][Vp] (rank r's logits of vocabulary rows
+// [r Vl, (r+1) Vl) in its first Vl columns) -> dst [B][t Vl].
+cudaError_t launch_gather_vocab_slices(const bf16* src, bf16* dst, int ranks, int batch, int vl, int vp,
+                                       cudaStream_t stream);
+
 // residual[m][n] = round(residual + round(sum[m][n])): the residual epilogue
 // applied to an FP32 sum (after the tensor-parallel all-reduce).
 cudaError_t launch_add_fp32_residual(const float* sum, bf16* residual, size_t n, cudaStream_t stream);

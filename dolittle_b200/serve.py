@@ -5,8 +5,9 @@ The reference serves long-context batches by running each sequence through
 CachedForwardPlan::prepare_device_generation / start_sequence
 (src/inference/executor.cpp:1482-1716) one after another.  `Server` runs the
 batch together: every weight read serves all B rows, and with tp_size > 1
-each GPU holds 1/tp_size of the query heads, KV heads and MLP columns, the
-o_proj and down_proj partial sums meeting in an NCCL all-reduce.
+each GPU holds 1/tp_size of the query heads, KV heads, MLP columns and
+vocabulary-head rows, the o_proj and down_proj partial sums meeting in an
+all-reduce and the logits in an all-gather.
 """
 from __future__ import annotations
 
@@ -161,10 +162,12 @@ _ROLE_CUT = {0: None, 1: ("rows", "q"), 2: ("rows", "kv"), 3: ("rows", "kv"), 4:
 
 def tp_slices(config: Qwen3Config, rank: int, size: int) -> list:
     """(rows, cols, r0, c0) of every tensor (engine order) that rank `rank`
-    of a tensor-parallel group of `size` holds: query heads, KV heads and MLP
-    columns in `size` equal contiguous slices (the layout Server uses)."""
-    if size < 1 or not 0 <= rank < size or config.kv_heads % size or config.mlp_width % size:
-        raise ValueError("tensor-parallel size must divide the KV heads and the MLP width")
+    of a tensor-parallel group of `size` holds: query heads, KV heads, MLP
+    columns and vocabulary-head rows in `size` equal contiguous slices (the
+    layout Server uses)."""
+    if (size < 1 or not 0 <= rank < size or config.kv_heads % size or config.mlp_width % size
+            or config.vocabulary % size):
+        raise ValueError("tensor-parallel size must divide the KV heads, the MLP width and the vocabulary")
     d = config.head_width
     width = {"q": config.query_heads * d // size, "kv": config.kv_heads * d // size, "mlp": config.mlp_width // size}
     shapes = [(config.vocabulary, config.hidden), (1, config.hidden), (config.vocabulary, config.hidden)]
@@ -173,6 +176,8 @@ def tp_slices(config: Qwen3Config, rank: int, size: int) -> list:
                  (1, d), (1, d), (config.hidden, full_q), (1, config.hidden), (config.mlp_width, config.hidden),
                  (config.mlp_width, config.hidden), (config.hidden, config.mlp_width)]
     out = [(r, c, 0, 0) for r, c in shapes]
+    vl = config.vocabulary // size
+    out[2] = (vl, config.hidden, rank * vl, 0)  # vocabulary head: row slices
     for _ in range(config.layers):
         for role, (r, c) in enumerate(per_block):
             cut = _ROLE_CUT[role]

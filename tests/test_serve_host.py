@@ -45,6 +45,8 @@ def test_slices_follow_kv_head_groups():
     assert s[o] == (4096, 1024, 0, 1024)
     assert s[gate] == (3072, 4096, 3072, 0)
     assert s[down] == (4096, 3072, 0, 3072)
+    assert s[2] == (37984, 4096, 37984, 0)     # vocabulary head rows 37984..75967
+    assert s[0] == (151936, 4096, 0, 0)         # the embedding stays whole
     with pytest.raises(ValueError):
         serve.tp_slices(cfg, 0, 3)
 
