@@ -976,6 +976,8 @@ __device__ __forceinline__ void consumer_main(const PersistArgs& a, unsigned cha
   }
   auto sync = [&] {
     if (aborted) return;
+    // Let the producer pull the next stages into L2 while this CTA waits.
+    if (threadIdx.x == 0 && a.prefetch_stages > 0) vstore(&h->pf_req, vload(&h->pf_req) + 1);
     target += gridDim.x;
     if (!grid_sync(a.barrier, target, h)) {
       aborted = true;
@@ -989,7 +991,6 @@ __device__ __forceinline__ void consumer_main(const PersistArgs& a, unsigned cha
     gemv_phase(a, desc(4 * l), uni, ring, h, g, failed, nullptr, none);
     sync();
     if (aborted) break;
-    if (threadIdx.x == 0 && a.prefetch_stages > 0) vstore(&h->pf_req, vload(&h->pf_req) + 1);
     for (int u = blockIdx.x; u < score_units; u += gridDim.x)
       score_unit(a, h->attn[l & 1], u % a.kv_heads, u / a.kv_heads, int(S), uni, h);
     sync();
