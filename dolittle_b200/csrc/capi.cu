@@ -314,10 +314,11 @@ DL_API dl_status dl_gemm_bf16_config(const void* x, size_t ldx, const void* w, v
   if (workspace && n_tickets < ((M + 127) / 128) * (N / 128))
     return fail(DL_INVALID_ARGUMENT, "gemm split: one ticket per 128 x 128 tile required");
   if ((tile_m != 0 && tile_m != 128 && tile_m != 256) || (tile_n != 0 && tile_n != 128 && tile_n != 256) ||
-      (tile_m == 256 && tile_n == 128) || parts < 0 || parts > dl::kGemmMaxSplit || (parts > 1 && !workspace))
+      (tile_m == 256 && tile_n == 128) || parts < -1 || parts > dl::kGemmMaxSplit || (parts > 1 && !workspace) ||
+      (parts == -1 && (!workspace || tile_m == 256)))
     return fail(DL_INVALID_ARGUMENT,
-                "gemm: tile_m 0/128/256, tile_n 0/128/256 (256 x 128 does not exist), parts 0..4 (more than 1 needs "
-                "the workspace)");
+                "gemm: tile_m 0/128/256, tile_n 0/128/256 (256 x 128 does not exist), parts -1..4 (more than 1 and "
+                "stream-K (-1, single-SM tiles) need the workspace)");
   if (!x || !w || !y || !M) return fail(DL_INVALID_ARGUMENT, "gemm: null pointer or empty shape");
   if (epilogue != dl::kGemmStore && epilogue != dl::kGemmResidual && epilogue != dl::kGemmSwiGLU)
     return fail(DL_INVALID_ARGUMENT, "gemm: epilogue must be 0, 1 or 3");
@@ -346,7 +347,9 @@ DL_API dl_status dl_gemm_bf16_config(const void* x, size_t ldx, const void* w, v
   }
   p.force_bm = tile_m;
   p.force_bn = tile_n;
-  p.force_split = parts;
+  // parts -1: stream-K; 1..4: that many K parts (no stream-K); 0: the cost model.
+  p.force_split = parts > 0 ? parts : 0;
+  p.force_streamk = parts == -1 ? 1 : parts > 0 ? -1 : 0;
   return cuda_status(dl::launch_gemm_tcgen05(p, st(stream), false), "gemm");
 }
 

@@ -45,6 +45,12 @@ constexpr double kStep128 = 0.95;
 constexpr double kStepPair = 1.25;
 constexpr double kSplitFixed = 16.0;
 constexpr double kSplitPerByte = 1.0 / 1.5e6;
+// Stream-K (every CTA an equal share of the k-steps) is available on request
+// only: measured against the tile choices above it never won by more than
+// 2 % (down at M = 2048: 176 vs 180 us) and lost up to 12 % at M = 512 (qkv
+// 47 vs 42, gate|up 119 vs 109, down 78 vs 70 us with 2 K parts).  The
+// k-steps it saves in the last wave are spent on the partial tiles' stores,
+// the finishers' sums and restarting the pipeline per unit.
 
 struct alignas(64) GemmArgs {
   CUtensorMap map_a;
@@ -61,6 +67,61 @@ struct alignas(64) GemmArgs {
   float* partial;      // [split][M][N] FP32
   unsigned* tickets;   // per tile (split >= 2 with the epilogue in the kernel)
   int partial_only;    // every part stores its FP32 partial; no epilogue
+  int streamk;         // stream-K: equal (tile, k-step) ranges per CTA (see WorkIter)
+};
+
+// The units of work of one CTA.  Split mode: units b, b + grid, ... of
+// tiles x split, unit u = K part u / tiles of tile u % tiles.  Stream-K mode:
+// the CTAs form one group per row of M tiles (CTA b serves M tile b % mt, as
+// rank b / mt of its group); each group cuts its row's flattened
+// (N tile, k-step) space into equal contiguous ranges, and a CTA walks its
+// range tile by tile from the END, so each unit is a k-range of one tile.
+// CTAs b .. b + mt - 1 cover the same k-steps of the same N tiles of all M
+// rows at the same time, so a weight tile is read from DRAM once and shared
+// through L2, as in the tile mode.  A tile cut between CTAs is summed by the
+// CTA that holds its last k-step, in k order (see tile_epilogue_streamk).
+// Walking backwards puts a CTA's contribution to the next tile (the end of
+// its range) first and its finishing work (the start of its range) last: no
+// CTA waits on a partial that is itself queued behind a wait.
+struct Work {
+  int tile, k_lo, k_hi, part;
+};
+// Stream-K range of group rank r of R over a row of nt N tiles x kt k-steps.
+__device__ __forceinline__ long long sk_bound(int r, int R, int nt, int kt) {
+  return (long long)r * nt * kt / R;
+}
+
+struct WorkIter {
+  bool sk;
+  int u, units, stride, tiles, kt, split, mt, m;
+  long long w, w1;
+  __device__ WorkIter(const GemmArgs& a, int tiles_, int kt_all, int mt_)
+      : sk(a.streamk != 0), u(blockIdx.x), units(tiles_ * a.split), stride(gridDim.x), tiles(tiles_), kt(kt_all),
+        split(a.split), mt(mt_), m(int(blockIdx.x) % mt_) {
+    const int R = int(gridDim.x) / mt_, r = int(blockIdx.x) / mt_, nt = tiles_ / mt_;
+    w = sk_bound(r, R, nt, kt_all);
+    w1 = sk_bound(r + 1, R, nt, kt_all);
+  }
+  __device__ bool next(Work& o) {
+    if (sk) {
+      if (w1 <= w) return false;
+      const int n = int((w1 - 1) / kt);  // N tile of this row
+      const long long t0 = (long long)n * kt;
+      o.tile = n * mt + m;
+      o.k_hi = int(w1 - t0);
+      o.k_lo = int(max(w, t0) - t0);
+      o.part = 0;
+      w1 = t0 + o.k_lo;
+      return true;
+    }
+    if (u >= units) return false;
+    o.tile = u % tiles;
+    o.part = u / tiles;
+    o.k_lo = o.part * kt / split;
+    o.k_hi = (o.part + 1) * kt / split;
+    u += stride;
+    return true;
+  }
 };
 
 __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -219,6 +280,102 @@ __device__ __forceinline__ void tile_epilogue(const GemmArgs& a, uint32_t acc, b
   }
 }
 
+// Stream-K epilogue of one unit (tile `tile`, k-steps [k_lo, k_hi) of kt):
+//  * the whole tile: the plain epilogue;
+//  * a unit without the tile's last k-step (a contributor; only a CTA's last
+//    unit can be one): its FP32 partial into this CTA's slot, a block
+//    [BN columns][128 rows] so a warp store is one 128-byte line; then one
+//    ticket on the tile;
+//  * the unit holding the last k-step (the finisher): waits (bounded) until
+//    every contributor -- the CTAs before this one whose ranges reach into
+//    the tile -- has ticked, adds their partials in k order and its own
+//    accumulator last, applies the epilogue and resets the ticket.
+// Contributors hold a tile's early k-steps, which they reach at the start of
+// their ranges, so the finisher rarely waits; the sum order is fixed, so
+// repeated runs are bit-identical.
+template <int BN>
+__device__ __forceinline__ void tile_epilogue_streamk(const GemmArgs& a, uint32_t acc, bf16* out, int ld, int row,
+                                                      int c0, const Work& wk, int tiles, int kt, int mt, int q,
+                                                      int lane, int* shared_flag) {
+  if (wk.k_lo == 0 && wk.k_hi == kt) {
+    bool unused = false;
+    GemmArgs one = a;
+    one.split = 1;
+    tile_epilogue<BN>(one, acc, out, ld, row, c0, wk.tile, tiles, 0, q, lane, unused);
+    return;
+  }
+  const size_t blk = size_t(BN) * kBM;
+  if (wk.k_hi < kt) {
+    float* mine = a.partial + size_t(blockIdx.x) * blk + q * 32 + lane;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(acc + uint32_t(c * 32), r);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) mine[size_t(c * 32 + i) * kBM] = __uint_as_float(r[i]);
+    }
+    __threadfence();
+    named_sync(1, 128);
+    if (threadIdx.x == 64) atomicAdd(&a.tickets[wk.tile], 1u);
+    return;
+  }
+  // Finisher: the contributors are the lower ranks of this CTA's group whose
+  // ranges reach into this tile (CTAs (r - 1) mt + m, (r - 2) mt + m, ...).
+  const int m = int(blockIdx.x) % mt;
+  const int R = int(gridDim.x) / mt, r = int(blockIdx.x) / mt, nt = tiles / mt;
+  const long long tile_w0 = (long long)(wk.tile / mt) * kt;
+  int first_r = r;
+  while (first_r > 0 && sk_bound(first_r, R, nt, kt) > tile_w0) --first_r;  // rank whose range holds k-step 0
+  const unsigned contrib = unsigned(r - first_r);
+  if (threadIdx.x == 64) {
+    int ok = 1;
+    const long long start = clock64();
+    for (;;) {
+      unsigned v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&a.tickets[wk.tile]) : "memory");
+      if (v >= contrib) break;
+      if (clock64() - start > (1ll << 32)) {
+        ok = 0;
+        record_error(a.err, kErrWaitFull);
+        break;
+      }
+    }
+    *shared_flag = ok;
+  }
+  named_sync(1, 128);
+  const bool ok = *shared_flag != 0;
+  __threadfence();
+  const bool resid = a.epilogue == kGemmResidual && row < a.M;
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    float sum[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) sum[i] = 0.f;
+    for (int rr = first_r; rr < r && ok; ++rr) {
+      const float* src = a.partial + size_t(rr * mt + m) * blk + size_t(c * 32) * kBM + q * 32 + lane;
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __ldcg(src + size_t(i) * kBM);
+      if (rr == first_r) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sum[i] = v[i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sum[i] = __fadd_rn(sum[i], v[i]);
+      }
+    }
+    uint4 res[4] = {};
+    if (resid) load_residual(out, ld, row, c0 + c * 32, res);
+    uint32_t r[32];
+    tmem_ld32(acc + uint32_t(c * 32), r);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__fadd_rn(sum[i], __uint_as_float(r[i])));
+    if (row < a.M && ok) store_chunk(a, out, ld, row, c0 + c * 32, r, res);
+  }
+  named_sync(1, 128);
+  if (threadIdx.x == 64) a.tickets[wk.tile] = 0;
+}
+
 // Persistent, warp-specialized: CTA b processes tiles b, b + grid, ... with
 // M tiles varying fastest (the CTAs that share a weight tile run together,
 // so it is read from DRAM once).  Warp 0 streams A/B stages by TMA through
@@ -245,10 +402,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mt = SWAP ? 1 : (a.M + kBM - 1) / kBM;
   const int tiles = SWAP ? a.N / kBM : mt * (a.N / BN);
-  const int units = tiles * a.split;  // unit u: tile u % tiles, K half u / tiles
-  // K part h of a tile covers k-steps [h kt / split, (h + 1) kt / split).
+  // Units: (tile, K part) in split mode, k-ranges of tiles under stream-K.
   const int kt_all = a.K / kBK;
   const int S = a.stages;
+  __shared__ int sk_flag;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -278,24 +435,30 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
       // before waiting for the previous kernel (programmatic dependent launch):
       // no kernel writes the weights, so they stream in during its tail.
       int pre = 0;
-      for (int u = blockIdx.x; u < units && pre < S; u += gridDim.x) {
-        const int tile = u % tiles, half = u / tiles;
-        const int m0 = SWAP ? tile * kBM : (tile % mt) * kBM, n0 = SWAP ? 0 : (tile / mt) * BN;
-        for (int kt = half * kt_all / a.split; kt < (half + 1) * kt_all / a.split && pre < S; ++kt, ++pre) {
-          unsigned char* st = ring + pre * kStageBytes;
-          mbar_arrive_expect_tx(&full[pre], kStageBytes);
-          if (SWAP)
-            tma_2d(st, &a.map_a, kt * kBK, m0, &full[pre]);
-          else
-            tma_2d(st + kABytes, &a.map_b, kt * kBK, n0, &full[pre]);
+      {
+        WorkIter it(a, tiles, kt_all, mt);
+        Work wk;
+        while (pre < S && it.next(wk)) {
+          const int tile = wk.tile;
+          const int m0 = SWAP ? tile * kBM : (tile % mt) * kBM, n0 = SWAP ? 0 : (tile / mt) * BN;
+          for (int kt = wk.k_lo; kt < wk.k_hi && pre < S; ++kt, ++pre) {
+            unsigned char* st = ring + pre * kStageBytes;
+            mbar_arrive_expect_tx(&full[pre], kStageBytes);
+            if (SWAP)
+              tma_2d(st, &a.map_a, kt * kBK, m0, &full[pre]);
+            else
+              tma_2d(st + kABytes, &a.map_b, kt * kBK, n0, &full[pre]);
+          }
         }
       }
       wait_prior();
       int g = 0;
-      for (int u = blockIdx.x; u < units && !*reinterpret_cast<volatile int*>(&abort_flag); u += gridDim.x) {
-        const int tile = u % tiles, half = u / tiles;
+      WorkIter it(a, tiles, kt_all, mt);
+      Work wk;
+      while (!*reinterpret_cast<volatile int*>(&abort_flag) && it.next(wk)) {
+        const int tile = wk.tile;
         const int m0 = SWAP ? tile * kBM : (tile % mt) * kBM, n0 = SWAP ? 0 : (tile / mt) * BN;
-        for (int kt = half * kt_all / a.split; kt < (half + 1) * kt_all / a.split; ++kt, ++g) {
+        for (int kt = wk.k_lo; kt < wk.k_hi; ++kt, ++g) {
           const int s = g % S;
           unsigned char* st = ring + s * kStageBytes;
           if (g < pre) {
@@ -322,7 +485,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
       // MMA issuer.
       constexpr uint32_t idesc = instr_desc_bf16(kBM, BN);
       int g = 0, t = 0;
-      for (int u = blockIdx.x; u < units && !*reinterpret_cast<volatile int*>(&abort_flag); u += gridDim.x, ++t) {
+      WorkIter it(a, tiles, kt_all, mt);
+      Work wk;
+      for (; !*reinterpret_cast<volatile int*>(&abort_flag) && it.next(wk); ++t) {
         const int buf = t & 1;
         if (t >= 2 && !mbar_wait(&acc_empty[buf], ((t >> 1) - 1) & 1)) {
           record_error(a.err, kErrWaitEmpty);
@@ -332,8 +497,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
         fence_after_sync();
         const uint32_t acc = tmem + uint32_t(buf * BN);
         bool ok = true;
-        const int part = u / tiles;
-        const int kt_n = (part + 1) * kt_all / a.split - part * kt_all / a.split;
+        const int kt_n = wk.k_hi - wk.k_lo;
         for (int kt = 0; kt < kt_n; ++kt, ++g) {
           const int s = g % S;
           if (!mbar_wait(&full[s], (g / S) & 1)) {
@@ -360,8 +524,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
     // 32q .. 32q+31 of the tile.
     const int q = warp & 3;
     int t = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++t) {
-      const int tile = u % tiles, half = u / tiles;
+    WorkIter it(a, tiles, kt_all, mt);
+    Work wk;
+    for (; it.next(wk); ++t) {
+      const int tile = wk.tile, half = wk.part;
       const int buf = t & 1;
       if (!mbar_wait(&acc_full[buf], (t >> 1) & 1)) {
         record_error(a.err, kErrWaitFull);
@@ -404,6 +570,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
             for (int i = 0; i < 8; ++i) d[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
           }
         }
+      } else if (a.streamk) {
+        tile_epilogue_streamk<BN>(a, acc, out, ld, row, c0, wk, tiles, kt_all, mt, q, lane, &sk_flag);
       } else {
         tile_epilogue<BN>(a, acc, out, ld, row, c0, tile, tiles, half, q, lane, last_half);
       }
@@ -435,14 +603,15 @@ __device__ __forceinline__ void tma_2d_pair(void* dst, const CUtensorMap* map, i
 // CTA's stage barrier; each MMA batch is committed to both CTAs' stage-free
 // barriers, each finished tile to both CTAs' accumulator barriers; the
 // epilogue warps of both CTAs drain their 128 TMEM rows and report to the
-// even CTA.  One 256-column accumulator per CTA.  Units are (tile, K part)
+// even CTA.  Two 256-column accumulators per CTA, so a tile's epilogue
+// overlaps the next tile's MMAs.  Units are (tile, K part)
 // as in the single-CTA kernel; pair p takes units p, p + pairs, ...
 constexpr int kPairN = 256;
-constexpr uint32_t kPairCols = 256;
+constexpr uint32_t kPairCols = 2 * kPairN;  // two 256-column accumulators per CTA
 
 __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_constant__ GemmArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  __shared__ uint64_t full[8], empty[8], acc_full, acc_empty;
+  __shared__ uint64_t full[8], empty[8], acc_full[2], acc_empty[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   __shared__ bool last_half;
@@ -465,8 +634,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_con
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(&acc_full, 1);
-    mbar_init(&acc_empty, 8);  // 4 epilogue warps in each CTA
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);  // 4 epilogue warps in each CTA
+    }
     abort_flag = 0;
     fence_barrier_init();
   }
@@ -516,16 +687,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_con
     if (lane == 0 && rank == 0) {
       // MMA issuer (even CTA).
       constexpr uint32_t idesc = instr_desc_bf16(2 * kBM, kPairN);
-      const uint32_t acc_full0 = mapa_shared(smem_addr(&acc_full), 0);
-      const uint32_t acc_full1 = mapa_shared(smem_addr(&acc_full), 1);
       int g = 0, t = 0;
       for (int u = pair; u < units && !*reinterpret_cast<volatile int*>(&abort_flag); u += pairs, ++t) {
-        if (t >= 1 && !mbar_wait_cluster(&acc_empty, (t - 1) & 1)) {
+        // Two accumulators: tile t's MMAs run while tile t - 1 drains.
+        const int buf = t & 1;
+        if (t >= 2 && !mbar_wait_cluster(&acc_empty[buf], ((t >> 1) - 1) & 1)) {
           record_error(a.err, kErrWaitEmpty);
           atomicExch(&abort_flag, 1);
           break;
         }
         fence_after_sync();
+        const uint32_t acc = tmem + uint32_t(buf * kPairN);
         bool ok = true;
         const int part = u / tiles;
         const int kt_n = (part + 1) * kt_all / a.split - part * kt_all / a.split;
@@ -543,24 +715,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_con
           const uint64_t bdesc = smem_desc_sw128(sa + kABytes);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
-            mma_bf16_pair(tmem, adesc + uint64_t(kk * 2), bdesc + uint64_t(kk * 2), idesc, (kt | kk) != 0);
+            mma_bf16_pair(acc, adesc + uint64_t(kk * 2), bdesc + uint64_t(kk * 2), idesc, (kt | kk) != 0);
           mma_commit_pair(mapa_shared(smem_addr(&empty[s]), 0));
           mma_commit_pair(mapa_shared(smem_addr(&empty[s]), 1));
         }
         if (!ok) break;
-        mma_commit_pair(acc_full0);
-        mma_commit_pair(acc_full1);
+        mma_commit_pair(mapa_shared(smem_addr(&acc_full[buf]), 0));
+        mma_commit_pair(mapa_shared(smem_addr(&acc_full[buf]), 1));
       }
     }
   } else {
     // Epilogue warps (both CTAs): TMEM lane group q = warp % 4 holds rows
     // 32q .. 32q+31 of this CTA's 128 rows of the tile.
     const int q = warp & 3;
-    const uint32_t acc_empty0 = mapa_shared(smem_addr(&acc_empty), 0);
     int t = 0;
     for (int u = pair; u < units; u += pairs, ++t) {
       const int tile = u % tiles, half = u / tiles;
-      if (!mbar_wait_cluster(&acc_full, t & 1)) {
+      const int buf = t & 1;
+      if (!mbar_wait_cluster(&acc_full[buf], (t >> 1) & 1)) {
         record_error(a.err, kErrWaitFull);
         atomicExch(&abort_flag, 1);
         break;
@@ -572,11 +744,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_con
       for (int i = 1; i < a.nseg; ++i)
         if (n0 >= a.seg_n0[i]) si = i;
       // Split-K blocks and tickets per 128-row half tile.
-      tile_epilogue<kPairN>(a, tmem + (uint32_t(q * 32) << 16), a.seg_out[si], a.seg_ld[si], row,
-                            n0 - a.seg_n0[si], tile * 2 + int(rank), tiles * 2, half, q, lane, last_half);
+      tile_epilogue<kPairN>(a, tmem + uint32_t(buf * kPairN) + (uint32_t(q * 32) << 16), a.seg_out[si],
+                            a.seg_ld[si], row, n0 - a.seg_n0[si], tile * 2 + int(rank), tiles * 2, half, q, lane,
+                            last_half);
       fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive_remote(acc_empty0);
+      if (lane == 0) mbar_arrive_remote(mapa_shared(smem_addr(&acc_empty[buf]), 0));
     }
   }
   fence_before_sync();
@@ -814,6 +987,26 @@ cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool 
       }
     }
   }
+  // Stream-K on single-SM tiles: one partial block per CTA in the workspace,
+  // one ticket per tile.
+  int sk_grid = 0;
+  if (workspace && p.force_streamk > 0 && !p.force_split && p.force_bm != 256) {
+    for (const int bn : {256, 128}) {
+      if (bn == 256 && !(aligned256 && p.wide_tiles)) continue;
+      if (p.force_bn && bn != p.force_bn) continue;
+      const long long tiles = mt * (p.N / bn);
+      // One group of CTAs per row of M tiles, at least 8 k-steps per CTA.
+      const long long per_row = std::min<long long>(sms / mt, (p.N / bn) * kt / 8);
+      const int G = int(per_row * mt);
+      if (per_row < 1 || G < 2 || tiles > p.n_tickets || size_t(G) * bn * kBM > p.partial_floats) continue;
+      if (BN == 0 || sk_grid == 0) {
+        BN = bn;
+        split = 1;
+        pair = false;
+        sk_grid = G;
+      }
+    }
+  }
   if (!BN) return cudaErrorInvalidValue;
   for (int i = 0; i < p.nseg; ++i)
     if (p.seg_n0[i] % BN) return cudaErrorInvalidValue;  // tiles never straddle outputs
@@ -857,7 +1050,8 @@ cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool 
     return cudaLaunchKernelEx(&cfg, gemm_pair_kernel, a);
   }
   const long long units = mt * (p.N / BN) * split;
-  cfg.gridDim = dim3(unsigned(std::min<long long>(units, sms)));
+  a.streamk = sk_grid > 0 ? 1 : 0;
+  cfg.gridDim = dim3(unsigned(sk_grid > 0 ? sk_grid : std::min<long long>(units, sms)));
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;

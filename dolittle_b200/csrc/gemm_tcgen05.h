@@ -35,6 +35,9 @@ struct GemmProblem {
   // Tuning overrides (0 = chosen by the launcher): tile height 128 (one SM)
   // or 256 (a CTA pair, 256 wide), tile width 128 / 256, the number of K parts.
   int force_bm, force_bn, force_split;
+  // Stream-K (single-SM tiles, needs the workspace): 0 = by the cost model,
+  // 1 = always, -1 = never.
+  int force_streamk;
 };
 
 constexpr int kGemmMaxSplit = 4;

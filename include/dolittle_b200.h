@@ -170,8 +170,12 @@ DL_API dl_status dl_gemm_bf16_split(const void* x, size_t ldx, const void* w, vo
                                     unsigned* tickets, size_t n_tickets);
 /* dl_gemm_bf16_split with the tiling chosen by the caller: tile_m 128 rows
  * per tile on one SM or 256 on a pair of SMs (then 256 columns), tile_n 128
- * or 256 output columns, and `parts` K parts (1..4); 0 = chosen by the
- * library for any of them.  workspace / tickets may be NULL when parts <= 1. */
+ * or 256 output columns, and `parts` K parts (1..4), or parts = -1 for
+ * stream-K (single-SM tiles: every CTA takes an equal contiguous share of
+ * the tiles' k-steps; a tile cut between CTAs is summed in k order by the
+ * CTA holding its last k-step, so results are bit-identical run to run);
+ * 0 = chosen by the library for any of them.  workspace / tickets may be NULL
+ * when parts is 0 or 1. */
 DL_API dl_status dl_gemm_bf16_config(const void* x, size_t ldx, const void* w, void* y, size_t ldy, size_t M,
                                      size_t N, size_t K, int epilogue, void* stream, void* workspace,
                                      unsigned* tickets, size_t n_tickets, int tile_m, int tile_n, int parts);

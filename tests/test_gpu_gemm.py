@@ -132,3 +132,50 @@ def test_gemm_rejects_unsupported_shapes():
     x = torch.zeros(8, 100, device="cuda", dtype=torch.bfloat16)
     assert dl.lib().dl_gemm_bf16(x.data_ptr(), 100, x.data_ptr(), x.data_ptr(), 128, 8, 128, 100, 0,
                                  None) == dl._lib.DL_UNSUPPORTED
+
+
+@pytest.mark.parametrize("M,N,K,epi,bn", [(512, 6144, 4096, 0, 256), (512, 4096, 12288, 1, 256),
+                                          (200, 2048, 4096, 3, 256), (512, 4096, 4096, 1, 128),
+                                          (77, 1024, 1024, 0, 128)])
+def test_gemm_streamk_matches_fp32_reference_and_repeats_bit_identically(M, N, K, epi, bn):
+    """Stream-K (parts = -1): every CTA takes an equal share of the k-steps;
+    tiles cut between CTAs are summed in k order by the CTA holding their last
+    k-step.  Store / residual / SwiGLU epilogues against the FP32 reference;
+    two runs bit-identical (fixed sum order)."""
+    torch = _torch()
+    L = dl.lib()
+    x, w = _case(M, N, K, seed=3 * M + N + K)
+    cols = N // 2 if epi == 3 else N
+    base = torch.randn(M, cols, device="cuda").to(torch.bfloat16)
+    ws = torch.empty(L.dl_gemm_bf16_split_workspace_bytes(M, N), device="cuda", dtype=torch.uint8)
+    n_t = ((M + 255) // 256) * 2 * (N // 128)
+    tickets = torch.zeros(n_t, device="cuda", dtype=torch.int32)
+    outs = []
+    for _ in range(2):
+        y = base.clone()
+        rc = L.dl_gemm_bf16_config(x.data_ptr(), K, w.data_ptr(), y.data_ptr(), cols, M, N, K, epi, None,
+                                   ws.data_ptr(), tickets.data_ptr(), n_t, 128, bn, -1)
+        assert rc == 0, L.dl_last_error()
+        torch.cuda.synchronize()
+        outs.append(y)
+    assert torch.equal(outs[0], outs[1])
+    assert int(tickets.abs().sum().item()) == 0   # every finisher reset its ticket
+    proj = x.float() @ w.float().T
+    got = outs[0].float()
+    if epi == 0:
+        r = nm.compare_elementwise(proj.cpu().numpy(), got.cpu().numpy(), 1e-3, 1.6e-2)
+    elif epi == 1:
+        # round(old + round(proj)): a one-ulp flip of the inner rounding is
+        # relative to |proj|, not to the (possibly cancelled) sum.
+        pb = proj.to(torch.bfloat16).float()
+        ref = (base.float() + pb).to(torch.bfloat16).float()
+        err = (got - ref).abs()
+        bound = 1e-2 + 2.0 ** -6 * torch.maximum(ref.abs(), pb.abs())  # one ulp of each rounding
+        r = {"mismatched": int((err > bound).sum().item()), "max_abs": float(err.max().item())}
+        r["passed"] = r["mismatched"] == 0
+    else:
+        yy = proj.to(torch.bfloat16).float()
+        gg, uu = yy[:, 0::2], yy[:, 1::2]
+        ref = ((gg * torch.sigmoid(gg)).to(torch.bfloat16).float() * uu).to(torch.bfloat16).float()
+        r = nm.compare_elementwise(ref.cpu().numpy(), got.cpu().numpy(), 1e-2, 3e-2)
+    assert r["passed"], r
