@@ -91,19 +91,21 @@ __device__ __forceinline__ long long sk_bound(int r, int R, int nt, int kt) {
   return (long long)r * nt * kt / R;
 }
 
+template <bool SK>
 struct WorkIter {
-  bool sk;
   int u, units, stride, tiles, kt, split, mt, m;
   long long w, w1;
   __device__ WorkIter(const GemmArgs& a, int tiles_, int kt_all, int mt_)
-      : sk(a.streamk != 0), u(blockIdx.x), units(tiles_ * a.split), stride(gridDim.x), tiles(tiles_), kt(kt_all),
-        split(a.split), mt(mt_), m(int(blockIdx.x) % mt_) {
-    const int R = int(gridDim.x) / mt_, r = int(blockIdx.x) / mt_, nt = tiles_ / mt_;
-    w = sk_bound(r, R, nt, kt_all);
-    w1 = sk_bound(r + 1, R, nt, kt_all);
+      : u(blockIdx.x), units(tiles_ * a.split), stride(gridDim.x), tiles(tiles_), kt(kt_all), split(a.split), mt(mt_),
+        m(int(blockIdx.x) % mt_) {
+    if constexpr (SK) {
+      const int R = int(gridDim.x) / mt_, r = int(blockIdx.x) / mt_, nt = tiles_ / mt_;
+      w = sk_bound(r, R, nt, kt_all);
+      w1 = sk_bound(r + 1, R, nt, kt_all);
+    }
   }
   __device__ bool next(Work& o) {
-    if (sk) {
+    if constexpr (SK) {
       if (w1 <= w) return false;
       const int n = int((w1 - 1) / kt);  // N tile of this row
       const long long t0 = (long long)n * kt;
@@ -386,7 +388,7 @@ __device__ __forceinline__ void tile_epilogue_streamk(const GemmArgs& a, uint32_
 // operand and the M <= BN input rows the N side, D = W X^T lands in TMEM as
 // [128 output features][BN rows]; a stage then carries 16 KB of weights and
 // BN x 128 bytes of inputs instead of a mostly zero-filled 128-row input tile.
-template <int BN, bool SWAP = false>
+template <int BN, bool SWAP = false, bool SK = false>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_constant__ GemmArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ uint64_t full[8], empty[8], acc_full[2], acc_empty[2];
@@ -436,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
       // no kernel writes the weights, so they stream in during its tail.
       int pre = 0;
       {
-        WorkIter it(a, tiles, kt_all, mt);
+        WorkIter<SK> it(a, tiles, kt_all, mt);
         Work wk;
         while (pre < S && it.next(wk)) {
           const int tile = wk.tile;
@@ -453,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
       }
       wait_prior();
       int g = 0;
-      WorkIter it(a, tiles, kt_all, mt);
+      WorkIter<SK> it(a, tiles, kt_all, mt);
       Work wk;
       while (!*reinterpret_cast<volatile int*>(&abort_flag) && it.next(wk)) {
         const int tile = wk.tile;
@@ -485,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
       // MMA issuer.
       constexpr uint32_t idesc = instr_desc_bf16(kBM, BN);
       int g = 0, t = 0;
-      WorkIter it(a, tiles, kt_all, mt);
+      WorkIter<SK> it(a, tiles, kt_all, mt);
       Work wk;
       for (; !*reinterpret_cast<volatile int*>(&abort_flag) && it.next(wk); ++t) {
         const int buf = t & 1;
@@ -524,7 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
     // 32q .. 32q+31 of the tile.
     const int q = warp & 3;
     int t = 0;
-    WorkIter it(a, tiles, kt_all, mt);
+    WorkIter<SK> it(a, tiles, kt_all, mt);
     Work wk;
     for (; it.next(wk); ++t) {
       const int tile = wk.tile, half = wk.part;
@@ -570,7 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
             for (int i = 0; i < 8; ++i) d[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
           }
         }
-      } else if (a.streamk) {
+      } else if constexpr (SK) {
         tile_epilogue_streamk<BN>(a, acc, out, ld, row, c0, wk, tiles, kt_all, mt, q, lane, &sk_flag);
       } else {
         tile_epilogue<BN>(a, acc, out, ld, row, c0, tile, tiles, half, q, lane, last_half);
@@ -1060,12 +1062,12 @@ cudaError_t launch_gemm_tcgen05(const GemmProblem& p, cudaStream_t stream, bool 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (BN == 256) {
-    cudaFuncSetAttribute(gemm_tcgen05_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    return cudaLaunchKernelEx(&cfg, gemm_tcgen05_kernel<256>, a);
-  }
-  cudaFuncSetAttribute(gemm_tcgen05_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  return cudaLaunchKernelEx(&cfg, gemm_tcgen05_kernel<128>, a);
+  auto go = [&](auto kernel) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    return cudaLaunchKernelEx(&cfg, kernel, a);
+  };
+  if (a.streamk) return BN == 256 ? go(gemm_tcgen05_kernel<256, false, true>) : go(gemm_tcgen05_kernel<128, false, true>);
+  return BN == 256 ? go(gemm_tcgen05_kernel<256>) : go(gemm_tcgen05_kernel<128>);
 }
 
 }  // namespace dl
