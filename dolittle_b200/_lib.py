@@ -140,6 +140,7 @@ SIGNATURES = {
     "dl_serve_set_steering": (C.c_int, [vp, C.c_int, sz, C.c_float, C.POINTER(C.c_float), C.POINTER(C.c_uint8),
                                         C.c_int64, sz]),
     "dl_serve_steering_strength": (C.c_int, [vp, C.POINTER(C.c_float)]),
+    "dl_serve_set_step_fusion": (C.c_int, [vp, C.c_int]),
     "dl_gemm_bf16_parts_workspace_bytes": (sz, [sz, sz, sz, sz]),
     "dl_gemm_bf16_parts": (C.c_int, [vp, sz, vp, vp, sz, sz, sz, sz, C.c_int, sz, vp, vp]),
     "dl_attention_decode_batched_workspace_bytes": (sz, [sz, sz, sz, sz]),

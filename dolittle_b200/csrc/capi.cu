@@ -704,6 +704,9 @@ DL_API dl_status dl_serve_set_steering(dl_serve* s, int layer, size_t first_posi
   DL_SERVE_CALL(s->impl->set_steering(layer, first_position, strength, host_direction, host_sequence_mask,
                                       (long long)source_sequence, source_position));
 }
+DL_API dl_status dl_serve_set_step_fusion(dl_serve* s, int on) {
+  DL_SERVE_CALL(s->impl->set_step_fusion(on != 0));
+}
 DL_API dl_status dl_serve_steering_strength(dl_serve* s, float* beta) {
   if (!beta) return fail(DL_INVALID_ARGUMENT, "serve_steering_strength: null");
   DL_SERVE_CALL(*beta = s->impl->steering_strength());

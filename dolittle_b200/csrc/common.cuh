@@ -199,4 +199,28 @@ __device__ __forceinline__ float rms_inverse_warp(const float* x, unsigned width
   return rsqrtf(__fadd_rn(mean, eps));
 }
 
+// The staged-law inverse (width > 128) of one row held as FP32 in shared
+// memory, computed by a whole CTA of at least 128 threads: thread t < 128
+// runs component chain t (columns t, t + 128, ...), warp 0 adds each lane's
+// four chains in order and runs the 32-lane tree; the same value as
+// rms_inverse_warp.  Every thread of the CTA calls it and gets the value.
+// `chains` is shared memory of 129 floats.
+__device__ __forceinline__ float rms_inverse_block(const float* xs, int width, float eps, float* chains) {
+  if (threadIdx.x < 128) {
+    float chain = 0.f;
+    for (int col = threadIdx.x; col < width; col += 128) chain = __fadd_rn(chain, __fmul_rn(xs[col], xs[col]));
+    chains[threadIdx.x] = chain;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const float* c4 = chains + 4 * threadIdx.x;
+    float sum = __fadd_rn(__fadd_rn(__fadd_rn(c4[0], c4[1]), c4[2]), c4[3]);
+    sum = shuffle_down_tree32(sum);
+    const float total = __shfl_sync(0xffffffffu, sum, 0);
+    if (threadIdx.x == 0) chains[128] = rsqrtf(__fadd_rn(__fmul_rn(total, 1.0f / static_cast<float>(width)), eps));
+  }
+  __syncthreads();
+  return chains[128];
+}
+
 }  // namespace dl

@@ -32,6 +32,10 @@ using namespace tc;
 constexpr int kBM = 128;
 constexpr int kBK = 64;   // one 128-byte swizzle atom of BF16
 constexpr int kThreads = 192;  // producer warp, MMA warp, 4 epilogue warps
+// Ring depth of the single-SM kernel.  The few-row split-K form streams
+// weights only, so it takes as many stages as fit in 224 KB (five 40 KB
+// stages of two k-steps at 32 rows).
+constexpr int kMaxStages = 12;
 // Tile choice, in units of one 256-wide k-step (~0.5 us on a B200): a
 // 128-wide k-step takes nearly as long (the narrow MMA is bound by shared
 // memory reads), and split-K costs a fixed ~8 us plus its FP32 partials'
@@ -131,6 +135,16 @@ __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x,
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
           "r"(smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// {64 features, rows from y, feature blocks from z} box of a 3D map (see
+// encode_3d): consecutive [rows][64] tiles in shared memory.
+__device__ __forceinline__ void tma_3d(void* dst, const CUtensorMap* map, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y), "r"(z), "r"(smem_addr(bar))
       : "memory");
 }
 
@@ -388,15 +402,20 @@ __device__ __forceinline__ void tile_epilogue_streamk(const GemmArgs& a, uint32_
 // operand and the M <= BN input rows the N side, D = W X^T lands in TMEM as
 // [128 output features][BN rows]; a stage then carries 16 KB of weights and
 // BN x 128 bytes of inputs instead of a mostly zero-filled 128-row input tile.
-template <int BN, bool SWAP = false, bool SK = false>
+// NB (SWAP only): k-steps per stage, loaded as one 3D box per operand
+// ({64 features, rows, NB feature blocks}), so each weight row is read NB x
+// 128 contiguous bytes at a time.
+template <int BN, bool SWAP = false, bool SK = false, int NB = 1>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_constant__ GemmArgs a) {
+  static_assert(NB == 1 || SWAP, "multi-block stages are for the swapped form");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  __shared__ uint64_t full[8], empty[8], acc_full[2], acc_empty[2];
+  __shared__ uint64_t full[kMaxStages], empty[kMaxStages], acc_full[2], acc_empty[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   __shared__ bool last_half;
-  constexpr int kABytes = kBM * kBK * 2;
-  constexpr int kBBytes = BN * kBK * 2;
+  constexpr int kABlock = kBM * kBK * 2, kBBlock = BN * kBK * 2;
+  constexpr int kABytes = kABlock * NB;
+  constexpr int kBBytes = kBBlock * NB;
   constexpr int kStageBytes = kABytes + kBBytes;
   constexpr uint32_t kCols = 2 * BN;
   const uint32_t base_s = (smem_addr(smem_raw) + 1023u) & ~1023u;
@@ -405,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
   const int mt = SWAP ? 1 : (a.M + kBM - 1) / kBM;
   const int tiles = SWAP ? a.N / kBM : mt * (a.N / BN);
   // Units: (tile, K part) in split mode, k-ranges of tiles under stream-K.
-  const int kt_all = a.K / kBK;
+  const int kt_all = a.K / (kBK * NB);
   const int S = a.stages;
   __shared__ int sk_flag;
 
@@ -446,7 +465,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
           for (int kt = wk.k_lo; kt < wk.k_hi && pre < S; ++kt, ++pre) {
             unsigned char* st = ring + pre * kStageBytes;
             mbar_arrive_expect_tx(&full[pre], kStageBytes);
-            if (SWAP)
+            if constexpr (NB > 1)
+              tma_3d(st, &a.map_a, m0, kt * NB, &full[pre]);
+            else if (SWAP)
               tma_2d(st, &a.map_a, kt * kBK, m0, &full[pre]);
             else
               tma_2d(st + kABytes, &a.map_b, kt * kBK, n0, &full[pre]);
@@ -465,7 +486,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
           unsigned char* st = ring + s * kStageBytes;
           if (g < pre) {
             // Weights already requested: the input half completes the stage.
-            if (SWAP)
+            if constexpr (NB > 1)
+              tma_3d(st + kABytes, &a.map_b, n0, kt * NB, &full[s]);
+            else if (SWAP)
               tma_2d(st + kABytes, &a.map_b, kt * kBK, n0, &full[s]);
             else
               tma_2d(st, &a.map_a, kt * kBK, m0, &full[s]);
@@ -477,8 +500,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
             break;
           }
           mbar_arrive_expect_tx(&full[s], kStageBytes);
-          tma_2d(st, &a.map_a, kt * kBK, m0, &full[s]);
-          tma_2d(st + kABytes, &a.map_b, kt * kBK, n0, &full[s]);
+          if constexpr (NB > 1) {
+            tma_3d(st, &a.map_a, m0, kt * NB, &full[s]);
+            tma_3d(st + kABytes, &a.map_b, n0, kt * NB, &full[s]);
+          } else {
+            tma_2d(st, &a.map_a, kt * kBK, m0, &full[s]);
+            tma_2d(st + kABytes, &a.map_b, kt * kBK, n0, &full[s]);
+          }
         }
       }
     }
@@ -510,11 +538,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(const __grid_
           }
           fence_after_sync();
           const uint32_t sa = smem_addr(ring + s * kStageBytes);
-          const uint64_t adesc = smem_desc_sw128(sa);
-          const uint64_t bdesc = smem_desc_sw128(sa + kABytes);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            mma_bf16(acc, adesc + uint64_t(kk * 2), bdesc + uint64_t(kk * 2), idesc, (kt | kk) != 0);
+          for (int j = 0; j < NB; ++j) {
+            const uint64_t adesc = smem_desc_sw128(sa + j * kABlock);
+            const uint64_t bdesc = smem_desc_sw128(sa + kABytes + j * kBBlock);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              mma_bf16(acc, adesc + uint64_t(kk * 2), bdesc + uint64_t(kk * 2), idesc, (kt | j | kk) != 0);
+          }
           mma_commit(&empty[s]);
         }
         if (!ok) break;
@@ -790,6 +821,22 @@ bool encode_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// [rows][cols] BF16 (row stride ld elements) as {64 features, rows, cols /
+// 64 feature blocks}: a box of `blocks` blocks holds `blocks` consecutive
+// 128-byte-swizzled [box_rows][64] tiles.
+bool encode_3d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
+               uint32_t blocks) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {uint64_t(kBK), rows, cols / kBK};
+  cuuint64_t strides[2] = {ld * 2, uint64_t(kBK) * 2};
+  cuuint32_t box[3] = {uint32_t(kBK), box_rows, blocks};
+  cuuint32_t es[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 bool gemm_tcgen05_supported(int M, int N, int K) { return M > 0 && K % kBK == 0 && N % 128 == 0; }
@@ -806,6 +853,7 @@ namespace {
 __global__ void splitk_epilogue_kernel(const float* __restrict__ parts, int splits, int M, int N, int epilogue,
                                        bf16* out, int ld, float* sum_out) {
   allow_next();  // a dependent GEMM may request its weights meanwhile
+  wait_prior();
   const size_t pairs = size_t(M) * (N / 2);
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < pairs; i += size_t(gridDim.x) * blockDim.x) {
     const int m = int(i / (N / 2)), n = int(i % (N / 2)) * 2;
@@ -869,6 +917,17 @@ cudaError_t launch_gemm_tcgen05_parts(const GemmProblem& p, int splits, float* p
     if (!encode_2d(&a.map_b, p.w, uint64_t(p.N), uint64_t(p.K), uint64_t(p.K), uint32_t(BN)))
       return cudaErrorInvalidValue;
   }
+  // Two feature blocks per stage in the swapped form (32 rows): 256
+  // contiguous bytes of each weight row per request.  Measured on the batch-32
+  // decode step at 2K context: 6.56 -> 6.18 ms (four blocks: 6.19 ms, with
+  // only two 80 KB stages in flight).
+  int nb = swap && BN == 32 ? 2 : 1;
+  if (nb > 1 && ((p.K / kBK) % nb || p.K / kBK / nb < splits)) nb = 1;
+  if (nb > 1) {
+    if (!encode_3d(&a.map_a, p.w, uint64_t(p.N), uint64_t(p.K), uint64_t(p.K), kBM, uint32_t(nb)) ||
+        !encode_3d(&a.map_b, p.x, uint64_t(p.M), uint64_t(p.K), uint64_t(p.ldx), uint32_t(BN), uint32_t(nb)))
+      return cudaErrorInvalidValue;
+  }
   a.M = p.M;
   a.N = p.N;
   a.K = p.K;
@@ -878,8 +937,8 @@ cudaError_t launch_gemm_tcgen05_parts(const GemmProblem& p, int splits, float* p
   a.split = splits;
   a.partial = parts;
   a.partial_only = 1;
-  const int stage_bytes = (kBM + BN) * kBK * 2;
-  a.stages = std::min(8, (200 * 1024) / stage_bytes);
+  const int stage_bytes = (kBM + BN) * kBK * 2 * nb;
+  a.stages = std::min(kMaxStages, (224 * 1024) / stage_bytes);
   const size_t smem = size_t(a.stages) * stage_bytes + 1024;
   int sms = 148, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -900,18 +959,26 @@ cudaError_t launch_gemm_tcgen05_parts(const GemmProblem& p, int splits, float* p
     return cudaLaunchKernelEx(&cfg, kernel, a);
   };
   if (!swap) return go(gemm_tcgen05_kernel<128>);
-  if (BN == 32) return go(gemm_tcgen05_kernel<32, true>);
+  if (BN == 32) return nb == 2 ? go(gemm_tcgen05_kernel<32, true, false, 2>) : go(gemm_tcgen05_kernel<32, true>);
   if (BN == 64) return go(gemm_tcgen05_kernel<64, true>);
   return go(gemm_tcgen05_kernel<128, true>);
 }
 
 cudaError_t launch_gemm_splitk_epilogue(const float* parts, int splits, int M, int N, int epilogue, bf16* out,
-                                        int ld, float* sum_out, cudaStream_t stream) {
+                                        int ld, float* sum_out, cudaStream_t stream, bool pdl) {
   if (N % 2 || splits < 1 || (!out && !sum_out)) return cudaErrorInvalidValue;
   const size_t pairs = size_t(M) * (N / 2);
   const unsigned blocks = unsigned(std::min<size_t>((pairs + 255) / 256, 148 * 16));
-  splitk_epilogue_kernel<<<blocks, 256, 0, stream>>>(parts, splits, M, N, epilogue, out, ld, sum_out);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, splitk_epilogue_kernel, parts, splits, M, N, epilogue, out, ld, sum_out);
 }
 
 // CTA pairs that fit on the device at once (clusters of 2 at one CTA per SM).

@@ -60,6 +60,6 @@ int gemm_splitk_parts(int M, int N, int K, int sms);  // parts that fill the SMs
 cudaError_t launch_gemm_tcgen05_parts(const GemmProblem& p, int splits, float* parts, cudaStream_t stream,
                                       bool pdl = false);
 cudaError_t launch_gemm_splitk_epilogue(const float* parts, int splits, int M, int N, int epilogue, bf16* out,
-                                        int ld, float* sum_out, cudaStream_t stream);
+                                        int ld, float* sum_out, cudaStream_t stream, bool pdl = false);
 
 }  // namespace dl

@@ -158,7 +158,8 @@ Server::Server(const dl_model_config& cfg, int device, size_t batch, size_t capa
                o_hlocal = grab(tp_ > 1 ? B * Vp_ * 2 : 0), o_hgather = grab(tp_ > 1 ? size_t(tp_) * B * Vp_ * 2 : 0),
                o_xlast = grab(B * D_ * 2), o_vt = grab(size_t(hkv_) * d_ * vt_stride_ * 2),
                o_parts = grab(parts_floats_ * 4),
-               o_ws = grab(attention_decode_ws_floats(int(B), hq_, attn_splits_) * 4), o_tok = grab(R * 4),
+               o_ws = grab(attention_decode_ws_floats(int(B), hq_, attn_splits_) * 4),
+               o_tickets = grab(B * size_t(hkv_) * 4), o_tok = grab(R * 4),
                o_hist = grab(B * history_cap_ * 4), o_steps = grab(B * 4), o_pos = grab(8), o_err = grab(16),
                o_freq = grab(d_ / 2 * 4);
   check(cudaMalloc(&scratch_, so), "scratch");
@@ -179,6 +180,7 @@ Server::Server(const dl_model_config& cfg, int device, size_t batch, size_t capa
   vt_ = reinterpret_cast<bf16*>(sb + o_vt);
   parts_ = reinterpret_cast<float*>(sb + o_parts);
   attn_ws_ = reinterpret_cast<float*>(sb + o_ws);
+  attn_tickets_ = reinterpret_cast<int*>(sb + o_tickets);
   tokens_dev_ = reinterpret_cast<uint32_t*>(sb + o_tok);
   history_ = reinterpret_cast<uint32_t*>(sb + o_hist);
   steps_ = reinterpret_cast<int*>(sb + o_steps);
@@ -458,7 +460,8 @@ void Server::row_projection_out(const bf16* x, int ldx, const bf16* w, int M, in
   check(launch_gemm_tcgen05_parts(p, parts, parts_, stream_, decode), "gemm parts");
   ++launches_;
   if (tp_ == 1) {
-    check(launch_gemm_splitk_epilogue(parts_, parts, M, N, kGemmResidual, residual_, N, nullptr, stream_),
+    check(launch_gemm_splitk_epilogue(parts_, parts, M, N, kGemmResidual, residual_, N, nullptr, stream_,
+                                      decode && fused_step()),
           "splitk epilogue");
     ++launches_;
     return;
@@ -665,6 +668,16 @@ void Server::set_steering(int layer, size_t first, float strength, const float* 
   steer_source_pos_ = source_position;
 }
 
+void Server::set_step_fusion(bool on) {
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  if (on == fuse_) return;
+  fuse_ = on;
+  if (step_exec_) {
+    cudaGraphExecDestroy(step_exec_);
+    step_exec_ = nullptr;
+  }
+}
+
 float Server::steering_strength() {
   check(cudaSetDevice(device_), "cudaSetDevice");
   float b = 0.f;
@@ -675,12 +688,51 @@ float Server::steering_strength() {
   return b;
 }
 
-// One decode step for all B rows at the shared position.
+// o / down projection of the B decode rows into the residual, the block
+// output hooks of `layer` (none for o: layer < 0), then xn_ = RMSNorm of the
+// residual with norm_w.  Fused (one rank, no hook on this block): the GEMM
+// and one kernel that adds the split-K parts into the residual and normalises
+// the rows.
+void Server::decode_projection_norm(const bf16* x, int K, const bf16* w, int layer, const bf16* norm_w) {
+  const int B = int(batch_), D = int(D_);
+  const bool hooks = layer >= 0 && (layer == steer_layer_ || layer == capture_layer_);
+  if (fused_step() && tp_ == 1 && !hooks) {
+    GemmProblem p = {};
+    p.err = err_;
+    p.x = x;
+    p.ldx = K;
+    p.w = w;
+    p.M = B;
+    p.N = D;
+    p.K = K;
+    const int parts = gemm_splitk_parts(B, D, K, sms_);
+    check(launch_gemm_tcgen05_parts(p, parts, parts_, stream_, true), "gemm parts");
+    check(launch_residual_norm_rows(parts_, parts, B, D, residual_, norm_w, xn_, cfg_.epsilon, stream_, true),
+          "residual norm");
+    launches_ += 2;
+    return;
+  }
+  row_projection_out(x, K, w, B, K, true);
+  if (layer >= 0) block_output_hooks_decode(size_t(layer));
+  check(launch_rms_norm(residual_, norm_w, xn_, batch_, D, cfg_.epsilon, stream_, fused_step()), "rms_norm");
+  ++launches_;
+}
+
+// The fused decode step: split-K sums folded into the kernels that consume
+// them (QK-norm/RoPE/append, residual + RMSNorm), the attention splits merged
+// by their last CTA, and every kernel of the chain a programmatic dependent
+// launch.  Same arithmetic as the unfused step, bit for bit.
+bool Server::fused_step() const { return fuse_ && d_ == 128 && D_ > 128 && D_ % 8 == 0 && D_ <= 8192; }
+
+// One decode step for all B rows at the shared position.  xn_ holds the
+// normed input of block l at the top of each iteration.
 void Server::decode_body() {
   const int B = int(batch_), D = int(D_), Q = int(Ql_), G = int(Gl_), F = int(Fl_), d = int(d_);
+  const bool fused = fused_step();
+  check(launch_rms_norm(residual_, layers_[0].in_norm, xn_, batch_, D, cfg_.epsilon, stream_, fused), "rms_norm");
+  ++launches_;
   for (size_t l = 0; l < L_; ++l) {
     const Layer& y = layers_[l];
-    check(launch_rms_norm(residual_, y.in_norm, xn_, batch_, D, cfg_.epsilon, stream_), "rms_norm");
     GemmProblem p = {};
     p.err = err_;
     p.x = xn_;
@@ -693,27 +745,34 @@ void Server::decode_body() {
     // The split-K projections are programmatic dependent launches: their
     // weights stream in while the previous kernel finishes.
     check(launch_gemm_tcgen05_parts(p, parts, parts_, stream_, true), "qkv parts");
-    check(launch_gemm_splitk_epilogue(parts_, parts, B, p.N, kGemmStore, qkv_, p.N, nullptr, stream_), "qkv sum");
-    check(launch_norm_rope_append_rows(qkv_, Q + 2 * G, y.q_norm, y.k_norm, inv_freq_, q_rot_, planes(l), position_,
-                                       B, hq_, hkv_, d, cfg_.epsilon, stream_),
-          "norm rope append");
+    if (fused) {
+      check(launch_norm_rope_append_rows(nullptr, Q + 2 * G, y.q_norm, y.k_norm, inv_freq_, q_rot_, planes(l),
+                                         position_, B, hq_, hkv_, d, cfg_.epsilon, stream_, parts_, parts, true),
+            "qkv sum + norm rope append");
+      launches_ += 2;
+    } else {
+      check(launch_gemm_splitk_epilogue(parts_, parts, B, p.N, kGemmStore, qkv_, p.N, nullptr, stream_), "qkv sum");
+      check(launch_norm_rope_append_rows(qkv_, Q + 2 * G, y.q_norm, y.k_norm, inv_freq_, q_rot_, planes(l),
+                                         position_, B, hq_, hkv_, d, cfg_.epsilon, stream_),
+            "norm rope append");
+      launches_ += 3;
+    }
     check(launch_attention_decode_batched(q_rot_, planes(l), position_, B, hq_, hkv_, attn_splits_,
-                                          attention_scale(d), attn_ws_, att_, stream_),
+                                          attention_scale(d), attn_ws_, att_, stream_,
+                                          fused ? attn_tickets_ : nullptr, fused),
           "attention decode");
-    launches_ += 6;
-    row_projection_out(att_, Q, y.wo, B, Q, true);
-    check(launch_rms_norm(residual_, y.post_norm, xn_, batch_, D, cfg_.epsilon, stream_), "rms_norm");
+    launches_ += fused ? 1 : 2;
+    decode_projection_norm(att_, Q, y.wo, -1, y.post_norm);
     p.w = y.wgu;
     p.N = 2 * F;
     p.K = D;
     parts = gemm_splitk_parts(B, p.N, p.K, sms_);
     check(launch_gemm_tcgen05_parts(p, parts, parts_, stream_, true), "gate/up parts");
-    check(launch_gemm_splitk_epilogue(parts_, parts, B, p.N, kGemmSwiGLU, act_, F, nullptr, stream_), "swiglu");
-    launches_ += 3;
-    row_projection_out(act_, F, y.wd, B, F, true);
-    block_output_hooks_decode(l);
+    check(launch_gemm_splitk_epilogue(parts_, parts, B, p.N, kGemmSwiGLU, act_, F, nullptr, stream_, fused),
+          "swiglu");
+    launches_ += 2;
+    decode_projection_norm(act_, F, y.wd, int(l), l + 1 < L_ ? layers_[l + 1].in_norm : final_norm_);
   }
-  check(launch_rms_norm(residual_, final_norm_, xn_, batch_, D, cfg_.epsilon, stream_), "final norm");
   vocabulary_head(B);
   check(sampler_submit(sampler_, logits_, settings_, 0, true, stream_, V_), "sampler");
   check(sampler_feed(sampler_, history_, steps_, embed_, residual_, D, nullptr, stream_, history_cap_), "sampler feed");

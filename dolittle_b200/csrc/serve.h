@@ -61,6 +61,8 @@ class Server {
   void set_steering(int layer, size_t first, float strength, const float* direction, const uint8_t* mask,
                     long long source_sequence, size_t source_position);
   float steering_strength();
+  // Fused decode step on (default) or off; both give the same bits.
+  void set_step_fusion(bool on);
 
  private:
   struct Slice {
@@ -74,6 +76,8 @@ class Server {
   void gemm(const bf16* x, int ldx, const bf16* w, int M, int N, int K, int epi, int nseg, const int* n0s,
             bf16* const* outs, const int* lds);
   void row_projection_out(const bf16* x, int ldx, const bf16* w, int M, int K, bool decode);  // o / down
+  void decode_projection_norm(const bf16* x, int K, const bf16* w, int layer, const bf16* norm_w);
+  bool fused_step() const;
   void prefill_sequence(size_t b, const uint32_t* tokens, size_t n);
   void block_output_hooks(size_t l, size_t b, size_t c0, int rows);  // prompt chunk rows of sequence b
   void block_output_hooks_decode(size_t l);
@@ -112,6 +116,8 @@ class Server {
   bf16 *residual_, *xn_, *qkv_, *q_raw_, *k_raw_, *q_rot_, *att_, *act_, *logits_, *xlast_, *vt_;
   bf16 *head_local_ = nullptr, *head_gather_ = nullptr;  // tensor parallelism: [B][Vp], [tp][B][Vp]
   float *parts_, *attn_ws_;
+  int* attn_tickets_ = nullptr;  // [B][Hkv], zero between launches
+  bool fuse_ = true;             // fused decode step (set_step_fusion)
   size_t parts_floats_ = 0;
   uint32_t* tokens_dev_;
   uint32_t* history_;

@@ -23,33 +23,131 @@ __global__ void fill_normal_slice_kernel(bf16* out, size_t rows, size_t cols, si
 constexpr int kRopeWarps = 8;
 
 // Heads [0, Hq): queries; [Hq, Hq+Hkv): keys; [Hq+Hkv, Hq+2Hkv): values
-// (copied).  One warp per (row, head).
-__global__ void norm_rope_append_rows_kernel(const bf16* __restrict__ qkv, int ld, const bf16* __restrict__ qw,
+// (copied).  One warp per (row, head).  PARTS: the row is the split-K parts
+// [splits][M][ld] FP32 of the qkv projection, added in part order and
+// rounded to BF16 here (the split-K store epilogue's law), so the BF16 qkv
+// rows never go through global memory.
+template <bool PARTS>
+__global__ void norm_rope_append_rows_kernel(const bf16* __restrict__ qkv, const float* __restrict__ parts,
+                                             int splits, int M, int ld, const bf16* __restrict__ qw,
                                              const bf16* __restrict__ kw, const float* __restrict__ inv_freq,
                                              bf16* __restrict__ q_out, KvPlanes planes,
                                              const long long* __restrict__ position, int query_heads, int kv_heads,
                                              int width, float eps) {
   __shared__ float vals[kRopeWarps][128];
+  __shared__ __align__(16) bf16 staged[PARTS ? kRopeWarps : 1][128];
+  allow_next();
+  wait_prior();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x;
   const int head = blockIdx.y * kRopeWarps + warp;
   if (head >= query_heads + 2 * kv_heads) return;
   const int p = int(*position);
-  const bf16* row = qkv + size_t(b) * ld;
   const size_t G = size_t(kv_heads) * width;
+  const bf16* row = qkv + size_t(b) * ld;
+  const bf16* src = row + size_t(head) * width;  // q, k and v heads are consecutive
+  if constexpr (PARTS) {
+    // Lane l: columns 4l .. 4l + 3 of the head (width 128).
+    const size_t col = size_t(head) * width + 4 * lane;
+    float4 acc = *reinterpret_cast<const float4*>(parts + size_t(b) * ld + col);
+    for (int s = 1; s < splits; ++s) {
+      const float4 v = *reinterpret_cast<const float4*>(parts + (size_t(s) * M + b) * ld + col);
+      acc.x = __fadd_rn(acc.x, v.x);
+      acc.y = __fadd_rn(acc.y, v.y);
+      acc.z = __fadd_rn(acc.z, v.z);
+      acc.w = __fadd_rn(acc.w, v.w);
+    }
+    __nv_bfloat162* d = reinterpret_cast<__nv_bfloat162*>(staged[warp] + 4 * lane);
+    d[0] = __floats2bfloat162_rn(acc.x, acc.y);
+    d[1] = __floats2bfloat162_rn(acc.z, acc.w);
+    __syncwarp();
+    src = staged[warp];
+  }
   bf16* seq = planes.kv + size_t(b) * planes.seq_stride;
   if (head < query_heads) {
-    qk_norm_rope_warp(row + size_t(head) * width, qw, inv_freq, p,
-                      q_out + (size_t(b) * query_heads + head) * width, width, eps, vals[warp]);
+    qk_norm_rope_warp(src, qw, inv_freq, p, q_out + (size_t(b) * query_heads + head) * width, width, eps,
+                      vals[warp]);
   } else if (head < query_heads + kv_heads) {
     const int g = head - query_heads;
-    qk_norm_rope_warp(row + size_t(query_heads) * width + size_t(g) * width, kw, inv_freq, p,
-                      seq + planes.k_off + size_t(p) * G + size_t(g) * width, width, eps, vals[warp]);
+    qk_norm_rope_warp(src, kw, inv_freq, p, seq + planes.k_off + size_t(p) * G + size_t(g) * width, width, eps,
+                      vals[warp]);
   } else {
     const int g = head - query_heads - kv_heads;
-    const bf16* src = row + size_t(query_heads) * width + G + size_t(g) * width;
     bf16* dst = seq + planes.v_off + size_t(p) * G + size_t(g) * width;
     for (int f = lane; f < width; f += 32) dst[f] = src[f];
+  }
+}
+
+// Residual epilogue of a row-parallel projection and the next RMSNorm in
+// one pass: CTA m adds the split-K parts [splits][M][N] of row m in part
+// order, applies residual = round(residual + round(sum)) (the split-K
+// residual epilogue's law), keeps the new row as FP32 in shared memory and
+// writes xn = RMSNorm(row) * w with rms_norm_rows_kernel's law (staged
+// chains, width > 128).  Up to 1024 threads, PER float4 columns each, every
+// part's loads issued together.
+template <int PER>
+__global__ void __launch_bounds__(1024) residual_norm_rows_kernel(const float* __restrict__ parts, int splits, int M,
+                                                                  int N, bf16* __restrict__ residual,
+                                                                  const bf16* __restrict__ w, bf16* __restrict__ xn,
+                                                                  float eps) {
+  extern __shared__ float xs[];  // [N]
+  __shared__ float chains[129];
+  allow_next();
+  wait_prior();
+  const int m = blockIdx.x, n4 = N / 4;
+  bf16* res = residual + size_t(m) * N;
+  const float4* p0 = reinterpret_cast<const float4*>(parts) + size_t(m) * n4;
+  const size_t part_stride = size_t(M) * n4;
+  float4 acc[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int q = threadIdx.x + i * blockDim.x;
+    if (q < n4) acc[i] = __ldcg(p0 + q);
+  }
+#pragma unroll 4
+  for (int s = 1; s < splits; ++s) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int q = threadIdx.x + i * blockDim.x;
+      if (q < n4) {
+        const float4 v = __ldcg(p0 + size_t(s) * part_stride + q);
+        acc[i].x = __fadd_rn(acc[i].x, v.x);
+        acc[i].y = __fadd_rn(acc[i].y, v.y);
+        acc[i].z = __fadd_rn(acc[i].z, v.z);
+        acc[i].w = __fadd_rn(acc[i].w, v.w);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int q = threadIdx.x + i * blockDim.x;
+    if (q >= n4) continue;
+    __nv_bfloat162* r2 = reinterpret_cast<__nv_bfloat162*>(res + 4 * q);
+    const float2 a = __bfloat1622float2(r2[0]), b = __bfloat1622float2(r2[1]);
+    const __nv_bfloat162 n0 =
+        __floats2bfloat162_rn(__fadd_rn(a.x, round_bf16(acc[i].x)), __fadd_rn(a.y, round_bf16(acc[i].y)));
+    const __nv_bfloat162 n1 =
+        __floats2bfloat162_rn(__fadd_rn(b.x, round_bf16(acc[i].z)), __fadd_rn(b.y, round_bf16(acc[i].w)));
+    r2[0] = n0;
+    r2[1] = n1;
+    const float2 f0 = __bfloat1622float2(n0), f1 = __bfloat1622float2(n1);
+    *reinterpret_cast<float4*>(xs + 4 * q) = make_float4(f0.x, f0.y, f1.x, f1.y);
+  }
+  __syncthreads();
+  const float inv = rms_inverse_block(xs, N, eps, chains);
+  const uint4* wv = reinterpret_cast<const uint4*>(w);
+  uint4* dst = reinterpret_cast<uint4*>(xn + size_t(m) * N);
+  for (int q = threadIdx.x; q < N / 8; q += blockDim.x) {
+    const uint4 g = wv[q];
+    const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const bf16 lo = narrow(__fmul_rn(round_bf16(__fmul_rn(xs[8 * q + 2 * i], inv)), bf_lo(gw[i])));
+      const bf16 hi = narrow(__fmul_rn(round_bf16(__fmul_rn(xs[8 * q + 2 * i + 1], inv)), bf_hi(gw[i])));
+      o[i] = uint32_t(__bfloat16_as_ushort(lo)) | (uint32_t(__bfloat16_as_ushort(hi)) << 16);
+    }
+    dst[q] = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -103,9 +201,32 @@ __device__ __forceinline__ void ldsm_x2_trans(uint32_t& b0, uint32_t& b1, const 
 
 __device__ __forceinline__ uint32_t lds32(const bf16* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
+// Merge of the splits of one (sequence, query head) for output feature f:
+// the global max, then the rescaled sums in split order; w points at the
+// head's [splits][130] workspace (L2 reads: written by other CTAs).
+__device__ __forceinline__ float combine_splits(const float* w, int splits, int f) {
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, __ldcg(w + size_t(s) * kAdWs));
+  float L = 0.f, o = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float m = __ldcg(w + size_t(s) * kAdWs);
+    if (m == -INFINITY) continue;
+    const float e = expf(m - M);
+    L += __ldcg(w + size_t(s) * kAdWs + 1) * e;
+    o += __ldcg(w + size_t(s) * kAdWs + 2 + f) * e;
+  }
+  return o / L;
+}
+
+// tickets (optional, [B][Hkv] zeroed): the last split CTA of each (sequence,
+// KV head) to finish merges the group's splits into out itself (ticket reset
+// for the next launch) instead of a separate combine launch.  Under a
+// programmatic dependent launch the key tiles that end before the newest
+// position (written by the previous kernel) are requested before waiting.
 __global__ void __launch_bounds__(kAdThreads) attention_decode_split_kernel(
     const bf16* __restrict__ q, KvPlanes planes, const long long* __restrict__ position, int query_heads,
-    int kv_heads, int splits, float scale, float* __restrict__ ws) {
+    int kv_heads, int splits, float scale, float* __restrict__ ws, int* __restrict__ tickets,
+    bf16* __restrict__ out) {
   extern __shared__ __align__(16) unsigned char smem[];
   bf16* stage = reinterpret_cast<bf16*>(smem);
   bf16* ps = reinterpret_cast<bf16*>(smem + size_t(kAdStages) * kAdStageElems * 2);  // [16][72]
@@ -123,15 +244,7 @@ __global__ void __launch_bounds__(kAdThreads) attention_decode_split_kernel(
   const bf16* vbase = planes.kv + size_t(b) * planes.seq_stride + planes.v_off + size_t(g) * 128;
   // P rows >= group stay zero.
   for (int i = t; i < 16 * kAdPPitch / 2; i += kAdThreads) reinterpret_cast<uint32_t*>(ps)[i] = 0u;
-  // Q fragments of the 8 k-steps (rows r < group; rows 8..15 are zero).
-  uint32_t qa[8][2];
   const bool qrow = r < group;
-  const bf16* qh = q + (size_t(b) * query_heads + g * group + (qrow ? r : 0)) * 128;
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-    qa[kk][0] = qrow ? *reinterpret_cast<const uint32_t*>(qh + 16 * kk + c2) : 0u;
-    qa[kk][1] = qrow ? *reinterpret_cast<const uint32_t*>(qh + 16 * kk + 8 + c2) : 0u;
-  }
   auto load_tile = [&](int tile, int slot) {
     const int base = j0 + tile * kAdKeys;
     const int n = min(kAdKeys, j1 - base);
@@ -153,10 +266,26 @@ __global__ void __launch_bounds__(kAdThreads) attention_decode_split_kernel(
   float o[2][4] = {};                // this warp's 2 n-tiles (rows r and r + 8)
   float m_run = -INFINITY, l_run = 0.f;  // head r (identical in every warp)
   // Tiles t+1 and t+2 load while tile t is processed (one commit group per
-  // tile; an empty group keeps the count when fewer tiles remain).
-  for (int i = 0; i < kAdStages - 1; ++i) {
-    if (i < tiles) load_tile(i, i);
+  // tile; an empty group keeps the count when fewer tiles remain).  Tiles
+  // wholly before key count - 1 (appended by the previous kernel) go first.
+  int pre = 0;
+  for (; pre < kAdStages - 1 && pre < tiles; ++pre) {
+    if (j0 + pre * kAdKeys + min(kAdKeys, j1 - (j0 + pre * kAdKeys)) > count - 1) break;
+    load_tile(pre, pre);
+  }
+  allow_next();
+  wait_prior();
+  for (; pre < kAdStages - 1; ++pre) {
+    if (pre < tiles) load_tile(pre, pre);
     else asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  // Q fragments of the 8 k-steps (rows r < group; rows 8..15 are zero).
+  uint32_t qa[8][2];
+  const bf16* qh = q + (size_t(b) * query_heads + g * group + (qrow ? r : 0)) * 128;
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    qa[kk][0] = qrow ? *reinterpret_cast<const uint32_t*>(qh + 16 * kk + c2) : 0u;
+    qa[kk][1] = qrow ? *reinterpret_cast<const uint32_t*>(qh + 16 * kk + 8 + c2) : 0u;
   }
   for (int tile = 0; tile < tiles; ++tile) {
     const int slot = tile % kAdStages;
@@ -233,24 +362,29 @@ __global__ void __launch_bounds__(kAdThreads) attention_decode_split_kernel(
       w[3 + 16 * warp + 8 * j + c2] = o[j][1];
     }
   }
+  if (!tickets) return;
+  // Publish this split (every writer fences), then count it.
+  __shared__ int last_s;
+  __threadfence();
+  __syncthreads();
+  if (t == 0) last_s = atomicAdd(tickets + size_t(b) * kv_heads + g, 1) == splits - 1;
+  __syncthreads();
+  if (!last_s) return;
+  __threadfence();
+  for (int i = t; i < group * 128; i += kAdThreads) {
+    const int h = g * group + i / 128, f = i % 128;
+    out[(size_t(b) * query_heads + h) * 128 + f] =
+        narrow(combine_splits(ws + (size_t(b) * query_heads + h) * splits * kAdWs, splits, f));
+  }
+  if (t == 0) tickets[size_t(b) * kv_heads + g] = 0;
 }
 
 __global__ void attention_decode_combine_kernel(const float* __restrict__ ws, int query_heads, int splits,
                                                 bf16* __restrict__ out) {
   allow_next();  // the o projection may request its weights meanwhile
   const int h = blockIdx.x, b = blockIdx.y, f = threadIdx.x;
-  const float* w = ws + (size_t(b) * query_heads + h) * splits * kAdWs;
-  float M = -INFINITY;
-  for (int s = 0; s < splits; ++s) M = fmaxf(M, w[size_t(s) * kAdWs]);
-  float L = 0.f, o = 0.f;
-  for (int s = 0; s < splits; ++s) {
-    const float m = w[size_t(s) * kAdWs];
-    if (m == -INFINITY) continue;
-    const float e = expf(m - M);
-    L += w[size_t(s) * kAdWs + 1] * e;
-    o += w[size_t(s) * kAdWs + 2 + f] * e;
-  }
-  out[(size_t(b) * query_heads + h) * 128 + f] = narrow(o / L);
+  out[(size_t(b) * query_heads + h) * 128 + f] =
+      narrow(combine_splits(ws + (size_t(b) * query_heads + h) * splits * kAdWs, splits, f));
 }
 
 __global__ void add_fp32_residual_kernel(const float* __restrict__ sum, bf16* __restrict__ residual, size_t n) {
@@ -355,15 +489,55 @@ cudaError_t launch_fill_normal_slice(bf16* out, size_t rows, size_t cols, size_t
   return cudaGetLastError();
 }
 
+namespace {
+cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t stream, cudaLaunchAttribute* attr,
+                              bool pdl) {
+  cudaLaunchConfig_t c = {};
+  c.gridDim = grid;
+  c.blockDim = block;
+  c.dynamicSmemBytes = smem;
+  c.stream = stream;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  c.attrs = attr;
+  c.numAttrs = pdl ? 1 : 0;
+  return c;
+}
+}  // namespace
+
 cudaError_t launch_norm_rope_append_rows(const bf16* qkv, int ld, const bf16* q_norm_w, const bf16* k_norm_w,
                                          const float* inv_freq, bf16* q_out, KvPlanes planes,
                                          const long long* position, int batch, int query_heads, int kv_heads,
-                                         int width, float eps, cudaStream_t stream) {
+                                         int width, float eps, cudaStream_t stream, const float* parts, int splits,
+                                         bool pdl) {
   if (width > 128 || width % 2 || batch < 1) return cudaErrorInvalidValue;
+  if (parts && (width != 128 || ld % 4 || splits < 1 || reinterpret_cast<uintptr_t>(parts) % 16))
+    return cudaErrorInvalidValue;
+  if (!parts && !qkv) return cudaErrorInvalidValue;
   const int heads = query_heads + 2 * kv_heads;
-  norm_rope_append_rows_kernel<<<dim3(batch, (heads + kRopeWarps - 1) / kRopeWarps), 32 * kRopeWarps, 0, stream>>>(
-      qkv, ld, q_norm_w, k_norm_w, inv_freq, q_out, planes, position, query_heads, kv_heads, width, eps);
-  return cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  auto cfg = pdl_config(dim3(batch, (heads + kRopeWarps - 1) / kRopeWarps), dim3(32 * kRopeWarps), 0, stream, attr,
+                        pdl);
+  if (parts)
+    return cudaLaunchKernelEx(&cfg, norm_rope_append_rows_kernel<true>, qkv, parts, splits, batch, ld, q_norm_w,
+                              k_norm_w, inv_freq, q_out, planes, position, query_heads, kv_heads, width, eps);
+  return cudaLaunchKernelEx(&cfg, norm_rope_append_rows_kernel<false>, qkv, parts, splits, batch, ld, q_norm_w,
+                            k_norm_w, inv_freq, q_out, planes, position, query_heads, kv_heads, width, eps);
+}
+
+cudaError_t launch_residual_norm_rows(const float* parts, int splits, int M, int N, bf16* residual, const bf16* w,
+                                      bf16* xn, float eps, cudaStream_t stream, bool pdl) {
+  if (N <= 128 || N % 8 || N > 8192 || splits < 1 || M < 1 ||
+      (reinterpret_cast<uintptr_t>(parts) | reinterpret_cast<uintptr_t>(residual) | reinterpret_cast<uintptr_t>(w) |
+       reinterpret_cast<uintptr_t>(xn)) % 16)
+    return cudaErrorInvalidValue;
+  const int n4 = N / 4;
+  const int threads = std::max(128, std::min(1024, (n4 + 31) / 32 * 32));
+  cudaLaunchAttribute attr[1];
+  auto cfg = pdl_config(dim3(M), dim3(threads), size_t(N) * 4, stream, attr, pdl);
+  if (n4 <= threads)
+    return cudaLaunchKernelEx(&cfg, residual_norm_rows_kernel<1>, parts, splits, M, N, residual, w, xn, eps);
+  return cudaLaunchKernelEx(&cfg, residual_norm_rows_kernel<2>, parts, splits, M, N, residual, w, xn, eps);
 }
 
 size_t attention_decode_ws_floats(int batch, int query_heads, int splits) {
@@ -380,16 +554,17 @@ int attention_decode_splits(int batch, int kv_heads, int capacity, int sms) {
 
 cudaError_t launch_attention_decode_batched(const bf16* q, KvPlanes planes, const long long* position, int batch,
                                             int query_heads, int kv_heads, int splits, float scale, float* ws,
-                                            bf16* out, cudaStream_t stream) {
+                                            bf16* out, cudaStream_t stream, int* tickets, bool pdl) {
   if (query_heads % kv_heads || query_heads / kv_heads > kAdMaxGroup || splits < 1 || splits > 64 || batch < 1)
     return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(attention_decode_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        int(kAdSmem));
   if (e != cudaSuccess) return e;
-  attention_decode_split_kernel<<<dim3(kv_heads, splits, batch), kAdThreads, kAdSmem, stream>>>(
-      q, planes, position, query_heads, kv_heads, splits, scale, ws);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  cudaLaunchAttribute attr[1];
+  auto cfg = pdl_config(dim3(kv_heads, splits, batch), dim3(kAdThreads), kAdSmem, stream, attr, pdl);
+  e = cudaLaunchKernelEx(&cfg, attention_decode_split_kernel, q, planes, position, query_heads, kv_heads, splits,
+                         scale, ws, tickets, out);
+  if (e != cudaSuccess || tickets) return e;
   attention_decode_combine_kernel<<<dim3(query_heads, batch), 128, 0, stream>>>(ws, query_heads, splits, out);
   return cudaGetLastError();
 }

@@ -24,11 +24,22 @@ cudaError_t launch_fill_normal_slice(bf16* out, size_t rows, size_t cols, size_t
 // Batched decode: row b of qkv [B][Hq*d + 2*Hkv*d] (row stride ld) is
 // sequence b's token at the shared position *position.  Queries get QK-norm
 // + RoPE into q_out [B][Hq][d]; keys get QK-norm + RoPE and values are copied,
-// both into sequence b's cache at that position.
+// both into sequence b's cache at that position.  With `parts` (d = 128) the
+// rows are instead the projection's split-K parts [splits][B][ld] FP32,
+// added in part order and rounded to BF16 first (qkv unused).  pdl: launched
+// as a programmatic dependent of the previous kernel.
 cudaError_t launch_norm_rope_append_rows(const bf16* qkv, int ld, const bf16* q_norm_w, const bf16* k_norm_w,
                                          const float* inv_freq, bf16* q_out, KvPlanes planes,
                                          const long long* position, int batch, int query_heads, int kv_heads,
-                                         int width, float eps, cudaStream_t stream);
+                                         int width, float eps, cudaStream_t stream, const float* parts = nullptr,
+                                         int splits = 1, bool pdl = false);
+
+// residual[m] = round(residual[m] + round(sum of parts [splits][M][N] in part
+// order)), then xn[m] = RMSNorm(residual[m]) * w (the RMSNorm rows law, N >
+// 128, N % 8 == 0, N <= 8192): the row-parallel projection's residual
+// epilogue and the following norm as one launch of M CTAs.
+cudaError_t launch_residual_norm_rows(const float* parts, int splits, int M, int N, bf16* residual, const bf16* w,
+                                      bf16* xn, float eps, cudaStream_t stream, bool pdl);
 
 // Split-K flash decoding: for every sequence b and query head h, attention of
 // q [B][Hq][128] over keys 0 .. *position of b's cache, the keys cut into
@@ -37,9 +48,14 @@ cudaError_t launch_norm_rope_append_rows(const bf16* qkv, int ld, const bf16* q_
 // [B][Hq*128] BF16.  Online softmax: not the reference's reduction order.
 size_t attention_decode_ws_floats(int batch, int query_heads, int splits);
 int attention_decode_splits(int batch, int kv_heads, int capacity, int sms);
+// tickets ([B][Hkv] int, zeroed once; each launch leaves them zero): the
+// last split of each (sequence, KV head) merges the splits itself, no
+// combine launch.  pdl: programmatic dependent launch (the key tiles before
+// the newest position are requested before waiting for the previous kernel).
 cudaError_t launch_attention_decode_batched(const bf16* q, KvPlanes planes, const long long* position, int batch,
                                             int query_heads, int kv_heads, int splits, float scale, float* ws,
-                                            bf16* out, cudaStream_t stream);
+                                            bf16* out, cudaStream_t stream, int* tickets = nullptr,
+                                            bool pdl = false);
 
 // Vocabulary-split head: src [t][B][Vp] (rank r's logits of vocabulary rows
 // [r Vl, (r+1) Vl) in its first Vl columns) -> dst [B][t Vl].

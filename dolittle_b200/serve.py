@@ -107,6 +107,10 @@ class Server:
                                           mask.ctypes.data_as(C.POINTER(C.c_uint8)), source_sequence,
                                           source_position))
 
+    def set_step_fusion(self, on: bool) -> None:
+        """Fused decode step (default) or separate kernels; the same bits."""
+        check(lib().dl_serve_set_step_fusion(self._h, 1 if on else 0))
+
     def steering_strength(self) -> float:
         b = C.c_float()
         check(lib().dl_serve_steering_strength(self._h, C.byref(b)))

@@ -137,6 +137,41 @@ def test_server_matches_single_sequence_engine():
     assert agree >= B * (steps + 1) - 1, agree
 
 
+@pytest.mark.parametrize("capture_layer", [-1, 1])
+def test_fused_decode_step_gives_the_same_bits_as_separate_kernels(capture_layer):
+    """The fused step (split-K sums folded into QK-norm/RoPE/append and into
+    residual + RMSNorm, attention splits merged by their last CTA, chained
+    programmatic launches) against the step as separate kernels: tokens,
+    logits and the captured block output identical, with fewer launches.  A
+    captured block keeps its separate residual epilogue (the hook sits between
+    the residual add and the next norm)."""
+    cfg = _small_cfg(3)
+    B, P, steps = 3, 40, 6
+    prompts = np.stack([oracle.uniform_ids(P, 70 + b, 0, cfg.vocabulary) for b in range(B)])
+    runs = []
+    for fused in (True, False):
+        srv = Server(cfg, batch=B, capacity=64, chunk_rows=16)
+        srv.init_random(11, 0.02)
+        if capture_layer >= 0:
+            srv.set_capture(capture_layer)
+        srv.set_step_fusion(fused)
+        first = srv.prefill(prompts, dl.Settings(dl.SelectionMode.categorical, 0.9, 0, 0.95), seed=5)
+        res = srv.decode(steps, want_logits=True)
+        cap = [srv.read_capture(b, 0, P + steps) for b in range(B)] if capture_layer >= 0 else []
+        runs.append((first, res, cap))
+        srv.close()
+    (f1, r1, c1), (f0, r0, c0) = runs
+    assert np.array_equal(f1, f0)
+    assert np.array_equal(r1.tokens, r0.tokens)
+    assert np.array_equal(r1.logits, r0.logits)
+    for a, b in zip(c1, c0):
+        assert np.array_equal(a, b)
+    # 3 blocks: 4 launches fewer per block, 3 with the captured block.
+    saved = 4 * cfg.layers - (1 if capture_layer >= 0 else 0)
+    assert r0.kernels_per_decode_step - r1.kernels_per_decode_step == saved, (r0.kernels_per_decode_step,
+                                                                               r1.kernels_per_decode_step)
+
+
 def test_server_greedy_tokens_are_the_argmax_of_its_logits():
     cfg = _small_cfg(1)
     srv = Server(cfg, batch=2, capacity=48, chunk_rows=32)
