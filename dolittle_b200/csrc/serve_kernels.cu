@@ -545,11 +545,25 @@ size_t attention_decode_ws_floats(int batch, int query_heads, int splits) {
 }
 
 int attention_decode_splits(int batch, int kv_heads, int capacity, int sms) {
-  // About eight waves of two resident CTAs per SM, and at least 8 tiles of
-  // keys per split at full capacity.
-  const int units = std::max(1, batch * kv_heads);
-  const int want = (16 * sms + units - 1) / units;
-  return std::clamp(want, 1, std::clamp(capacity / (8 * kAdKeys), 1, 64));
+  // Splits of each (sequence, KV head)'s keys by estimated time: waves of
+  // two resident CTAs per SM x (64-key tiles per split + ~3 tiles of fixed
+  // cost per CTA: query load, pipeline fill, partial write).  Measured on the
+  // batch-32 step: one split per (sequence, KV head) at 1K and 2K context
+  // (5.36 -> 5.08 and 6.18 -> 5.92 ms per step against 2 and 4 splits),
+  // about even from 1 to 4 splits at 8K.
+  const long long units = std::max(1, batch * kv_heads), slots = 2ll * std::max(1, sms);
+  const int tiles = std::max(1, (capacity + kAdKeys - 1) / kAdKeys);
+  int best = 1;
+  long long best_cost = -1;
+  for (int s = 1; s <= std::min(64, tiles); ++s) {
+    const long long waves = (units * s + slots - 1) / slots;
+    const long long cost = waves * ((tiles + s - 1) / s + 3);
+    if (best_cost < 0 || cost < best_cost) {
+      best = s;
+      best_cost = cost;
+    }
+  }
+  return best;
 }
 
 cudaError_t launch_attention_decode_batched(const bf16* q, KvPlanes planes, const long long* position, int batch,
