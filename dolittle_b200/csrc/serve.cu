@@ -469,12 +469,9 @@ void Server::row_projection_out(const bf16* x, int ldx, const bf16* w, int M, in
   // Decode rows: one kernel sums the K parts, exchanges them over NVLink peer
   // memory and adds the residual (NCCL when DOLITTLE_TP_ALLREDUCE=nccl, and
   // for the prompt pass's large messages).
-  static const bool use_nccl = [] {
-    const char* v = std::getenv("DOLITTLE_TP_ALLREDUCE");
-    return v && std::string(v) == "nccl";
-  }();
-  if (decode && peers_ && !use_nccl && size_t(M) * N <= pb_.capacity) {
-    check(launch_peer_allreduce_residual(pb_, parts_, parts, residual_, size_t(M) * N, stream_), "peer all-reduce");
+  if (decode && peer_decode(M)) {
+    check(launch_peer_allreduce_residual(pb_, parts_, parts, M, N, residual_, nullptr, nullptr, 0.f, stream_, false),
+          "peer all-reduce");
     ++launches_;
     return;
   }
@@ -696,7 +693,8 @@ float Server::steering_strength() {
 void Server::decode_projection_norm(const bf16* x, int K, const bf16* w, int layer, const bf16* norm_w) {
   const int B = int(batch_), D = int(D_);
   const bool hooks = layer >= 0 && (layer == steer_layer_ || layer == capture_layer_);
-  if (fused_step() && tp_ == 1 && !hooks) {
+  const bool fold = fused_step() && !hooks;
+  if (fold && (tp_ == 1 || peer_decode(B))) {
     GemmProblem p = {};
     p.err = err_;
     p.x = x;
@@ -707,8 +705,13 @@ void Server::decode_projection_norm(const bf16* x, int K, const bf16* w, int lay
     p.K = K;
     const int parts = gemm_splitk_parts(B, D, K, sms_);
     check(launch_gemm_tcgen05_parts(p, parts, parts_, stream_, true), "gemm parts");
-    check(launch_residual_norm_rows(parts_, parts, B, D, residual_, norm_w, xn_, cfg_.epsilon, stream_, true),
-          "residual norm");
+    if (tp_ == 1)
+      check(launch_residual_norm_rows(parts_, parts, B, D, residual_, norm_w, xn_, cfg_.epsilon, stream_, true),
+            "residual norm");
+    else
+      check(launch_peer_allreduce_residual(pb_, parts_, parts, B, D, residual_, norm_w, xn_, cfg_.epsilon, stream_,
+                                           true),
+            "peer all-reduce + norm");
     launches_ += 2;
     return;
   }
@@ -722,6 +725,17 @@ void Server::decode_projection_norm(const bf16* x, int K, const bf16* w, int lay
 // them (QK-norm/RoPE/append, residual + RMSNorm), the attention splits merged
 // by their last CTA, and every kernel of the chain a programmatic dependent
 // launch.  Same arithmetic as the unfused step, bit for bit.
+// Decode all-reduces over NVLink peer memory (NCCL when
+// DOLITTLE_TP_ALLREDUCE=nccl): one CTA per row, so at most kPeerChunks rows.
+bool Server::peer_decode(int rows) const {
+  static const bool use_nccl = [] {
+    const char* v = std::getenv("DOLITTLE_TP_ALLREDUCE");
+    return v && std::string(v) == "nccl";
+  }();
+  return tp_ > 1 && peers_ && !use_nccl && rows <= kPeerChunks && size_t(rows) * D_ <= pb_.capacity &&
+         D_ % 8 == 0 && D_ > 128 && D_ <= 8192;
+}
+
 bool Server::fused_step() const { return fuse_ && d_ == 128 && D_ > 128 && D_ % 8 == 0 && D_ <= 8192; }
 
 // One decode step for all B rows at the shared position.  xn_ holds the

@@ -78,6 +78,7 @@ class Server {
   void row_projection_out(const bf16* x, int ldx, const bf16* w, int M, int K, bool decode);  // o / down
   void decode_projection_norm(const bf16* x, int K, const bf16* w, int layer, const bf16* norm_w);
   bool fused_step() const;
+  bool peer_decode(int rows) const;
   void prefill_sequence(size_t b, const uint32_t* tokens, size_t n);
   void block_output_hooks(size_t l, size_t b, size_t c0, int rows);  // prompt chunk rows of sequence b
   void block_output_hooks_decode(size_t l);

@@ -405,47 +405,58 @@ __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
 
 constexpr long long kPeerSpin = 1ll << 31;  // ~1 s of SM cycles
 
-__global__ void __launch_bounds__(256) peer_allreduce_residual_kernel(PeerBuffers pb, const float* __restrict__ parts,
-                                                                      int splits, bf16* __restrict__ residual,
-                                                                      size_t n) {
+// CTA `row` owns row `row` of the [M][N] output (M <= kPeerChunks): it sums
+// this rank's split-K parts of the row in part order, writes the FP32 row
+// into slot `rank` of every rank's buffer, raises flag (rank, row) on each,
+// waits (bounded) for every rank's flag on its own buffer, adds the slots in
+// rank order and applies the residual epilogue; with NORM it then writes
+// xn = RMSNorm(row) * w by the RMSNorm rows law (the row is in shared memory).
+template <bool NORM>
+__global__ void __launch_bounds__(1024) peer_allreduce_rows_kernel(PeerBuffers pb, const float* __restrict__ parts,
+                                                                   int splits, int M, int N,
+                                                                   bf16* __restrict__ residual,
+                                                                   const bf16* __restrict__ w, bf16* __restrict__ xn,
+                                                                   float eps) {
+  extern __shared__ float xs[];  // [N] (NORM)
+  __shared__ float chains[129];
   __shared__ unsigned epoch_s;
   __shared__ int ok_s;
-  const int i = blockIdx.x, R = pb.ranks;
-  // CTA i counts its own calls: every rank runs the same calls, so chunk i's
-  // epochs agree across ranks without any ordering between CTAs.
-  if (threadIdx.x == 0) epoch_s = pb.epoch[i] + 1;
+  allow_next();
+  wait_prior();
+  const int row = blockIdx.x, R = pb.ranks, n4 = N / 4;
+  // CTA `row` counts its own calls: every rank runs the same calls, so the
+  // epochs of row `row` agree across ranks without any ordering between CTAs.
+  if (threadIdx.x == 0) epoch_s = pb.epoch[row] + 1;
   __syncthreads();
   const unsigned epoch = epoch_s, par = epoch & 1u;
-  const size_t per = ((n + kPeerChunks - 1) / kPeerChunks + 3) / 4 * 4;
-  const size_t c0 = min(n, size_t(i) * per), c1 = min(n, c0 + per);
-  // 1. This rank's chunk i (its split-K parts summed in part order, the
-  // split-K epilogue's law) into slot `rank` of every rank's buffer (16-byte
-  // stores; n and the chunk bounds are multiples of 4 floats).
+  const size_t off4 = size_t(row) * n4, all4 = size_t(M) * n4;
+  // 1. This rank's row (split-K parts in part order) into slot `rank` of
+  // every rank's buffer.
   const float4* src = reinterpret_cast<const float4*>(parts);
-  for (size_t j = c0 / 4 + threadIdx.x; j < c1 / 4; j += blockDim.x) {
-    float4 acc = src[j];
+  for (int j = threadIdx.x; j < n4; j += blockDim.x) {
+    float4 acc = src[off4 + j];
     for (int s = 1; s < splits; ++s) {
-      const float4 v = src[size_t(s) * (n / 4) + j];
+      const float4 v = src[size_t(s) * all4 + off4 + j];
       acc.x = __fadd_rn(acc.x, v.x);
       acc.y = __fadd_rn(acc.y, v.y);
       acc.z = __fadd_rn(acc.z, v.z);
       acc.w = __fadd_rn(acc.w, v.w);
     }
     for (int p = 0; p < R; ++p)
-      reinterpret_cast<float4*>(pb.data[p] + (size_t(par) * R + pb.rank) * pb.capacity)[j] = acc;
+      reinterpret_cast<float4*>(pb.data[p] + (size_t(par) * R + pb.rank) * pb.capacity)[off4 + j] = acc;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence_system();
-    for (int p = 0; p < R; ++p) st_release_sys(pb.flags[p] + (size_t(par) * R + pb.rank) * kPeerChunks + i, epoch);
+    for (int p = 0; p < R; ++p) st_release_sys(pb.flags[p] + (size_t(par) * R + pb.rank) * kPeerChunks + row, epoch);
   }
-  // 2. Every rank's chunk i has arrived here (bounded wait).
+  // 2. Every rank's row has arrived here (bounded wait).
   if (threadIdx.x == 0) {
     int ok = 1;
     const unsigned* mine = pb.flags[pb.rank] + size_t(par) * R * kPeerChunks;
-    for (int src = 0; src < R && ok; ++src) {
+    for (int r = 0; r < R && ok; ++r) {
       const long long start = clock64();
-      while (ld_relaxed_sys(mine + src * kPeerChunks + i) != epoch) {
+      while (ld_relaxed_sys(mine + r * kPeerChunks + row) != epoch) {
         if (clock64() - start > kPeerSpin) {
           ok = 0;
           atomicOr(pb.err, kErrWaitFull);
@@ -458,24 +469,52 @@ __global__ void __launch_bounds__(256) peer_allreduce_residual_kernel(PeerBuffer
   }
   __syncthreads();
   // 3. Sum in rank order, residual add (the residual epilogue law).
-  if (ok_s) {
+  const bool ok = ok_s != 0;
+  if (ok) {
     const float* slots = pb.data[pb.rank] + size_t(par) * R * pb.capacity;
-    for (size_t j = c0 / 4 + threadIdx.x; j < c1 / 4; j += blockDim.x) {
-      float4 sum = __ldcv(reinterpret_cast<const float4*>(slots) + j);
-      for (int src = 1; src < R; ++src) {
-        const float4 v = __ldcv(reinterpret_cast<const float4*>(slots + size_t(src) * pb.capacity) + j);
+    for (int j = threadIdx.x; j < n4; j += blockDim.x) {
+      float4 sum = __ldcv(reinterpret_cast<const float4*>(slots) + off4 + j);
+      for (int r = 1; r < R; ++r) {
+        const float4 v = __ldcv(reinterpret_cast<const float4*>(slots + size_t(r) * pb.capacity) + off4 + j);
         sum.x = __fadd_rn(sum.x, v.x);
         sum.y = __fadd_rn(sum.y, v.y);
         sum.z = __fadd_rn(sum.z, v.z);
         sum.w = __fadd_rn(sum.w, v.w);
       }
-      __nv_bfloat162* r2 = reinterpret_cast<__nv_bfloat162*>(residual) + 2 * j;
+      __nv_bfloat162* r2 = reinterpret_cast<__nv_bfloat162*>(residual) + 2 * (off4 + j);
       const float2 a = __bfloat1622float2(r2[0]), b = __bfloat1622float2(r2[1]);
-      r2[0] = __floats2bfloat162_rn(__fadd_rn(a.x, round_bf16(sum.x)), __fadd_rn(a.y, round_bf16(sum.y)));
-      r2[1] = __floats2bfloat162_rn(__fadd_rn(b.x, round_bf16(sum.z)), __fadd_rn(b.y, round_bf16(sum.w)));
+      const __nv_bfloat162 n0 =
+          __floats2bfloat162_rn(__fadd_rn(a.x, round_bf16(sum.x)), __fadd_rn(a.y, round_bf16(sum.y)));
+      const __nv_bfloat162 n1 =
+          __floats2bfloat162_rn(__fadd_rn(b.x, round_bf16(sum.z)), __fadd_rn(b.y, round_bf16(sum.w)));
+      r2[0] = n0;
+      r2[1] = n1;
+      if constexpr (NORM) {
+        const float2 f0 = __bfloat1622float2(n0), f1 = __bfloat1622float2(n1);
+        *reinterpret_cast<float4*>(xs + 4 * j) = make_float4(f0.x, f0.y, f1.x, f1.y);
+      }
     }
   }
-  if (threadIdx.x == 0) pb.epoch[i] = epoch;
+  if (threadIdx.x == 0) pb.epoch[row] = epoch;
+  if constexpr (NORM) {
+    if (!ok) return;  // CTA-uniform
+    __syncthreads();
+    const float inv = rms_inverse_block(xs, N, eps, chains);
+    const uint4* wv = reinterpret_cast<const uint4*>(w);
+    uint4* dst = reinterpret_cast<uint4*>(xn + size_t(row) * N);
+    for (int q = threadIdx.x; q < N / 8; q += blockDim.x) {
+      const uint4 g = wv[q];
+      const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const bf16 lo = narrow(__fmul_rn(round_bf16(__fmul_rn(xs[8 * q + 2 * i], inv)), bf_lo(gw[i])));
+        const bf16 hi = narrow(__fmul_rn(round_bf16(__fmul_rn(xs[8 * q + 2 * i + 1], inv)), bf_hi(gw[i])));
+        o[i] = uint32_t(__bfloat16_as_ushort(lo)) | (uint32_t(__bfloat16_as_ushort(hi)) << 16);
+      }
+      dst[q] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
 }
 
 }  // namespace
@@ -587,12 +626,20 @@ size_t peer_buffer_bytes(int ranks, size_t capacity) {
   return size_t(2) * ranks * capacity * 4 + size_t(2) * ranks * kPeerChunks * 4;
 }
 
-cudaError_t launch_peer_allreduce_residual(const PeerBuffers& pb, const float* parts, int splits, bf16* residual,
-                                           size_t n, cudaStream_t stream) {
-  if (n > pb.capacity || n % 4 || splits < 1 || pb.ranks < 1 || pb.ranks > kPeerMaxRanks)
+cudaError_t launch_peer_allreduce_residual(const PeerBuffers& pb, const float* parts, int splits, int M, int N,
+                                           bf16* residual, const bf16* norm_w, bf16* xn, float eps,
+                                           cudaStream_t stream, bool pdl) {
+  if (M < 1 || M > kPeerChunks || N % 8 || size_t(M) * N > pb.capacity || splits < 1 || pb.ranks < 1 ||
+      pb.ranks > kPeerMaxRanks || (norm_w && (N <= 128 || N > 8192 || !xn)))
     return cudaErrorInvalidValue;
-  peer_allreduce_residual_kernel<<<kPeerChunks, 256, 0, stream>>>(pb, parts, splits, residual, n);
-  return cudaGetLastError();
+  const int threads = std::max(128, std::min(1024, (N / 4 + 31) / 32 * 32));
+  cudaLaunchAttribute attr[1];
+  auto cfg = pdl_config(dim3(M), dim3(threads), norm_w ? size_t(N) * 4 : 0, stream, attr, pdl);
+  if (norm_w)
+    return cudaLaunchKernelEx(&cfg, peer_allreduce_rows_kernel<true>, pb, parts, splits, M, N, residual, norm_w, xn,
+                              eps);
+  return cudaLaunchKernelEx(&cfg, peer_allreduce_rows_kernel<false>, pb, parts, splits, M, N, residual, norm_w, xn,
+                            eps);
 }
 
 __global__ void gather_vocab_slices_kernel(const bf16* src, bf16* dst, int ranks, int batch, int vl, int vp) {

@@ -67,16 +67,18 @@ cudaError_t launch_gather_vocab_slices(const bf16* src, bf16* dst, int ranks, in
 cudaError_t launch_add_fp32_residual(const float* sum, bf16* residual, size_t n, cudaStream_t stream);
 
 // Tensor-parallel all-reduce of the row-parallel projections over NVLink peer
-// memory, fused with the split-K sum and the residual add: every rank sums
-// its split-K parts [splits][n] in part order and writes the FP32 partial sum
-// [n] (chunk i per CTA) into slot `rank` of every rank's buffer (peer
-// pointers from CUDA IPC), raises flag (rank, i) on each with the call's
-// epoch, waits (bounded) for every rank's flag i on its own buffer, then adds
-// the slots in rank order (the same sum on every rank) and applies
-// residual = round(residual + round(sum)).  Buffers alternate by epoch parity
-// so a rank running one call ahead never overwrites a slot still being read.
+// memory, fused with the split-K sum, the residual add and (norm_w) the next
+// RMSNorm: CTA `row` sums this rank's split-K parts of its row [splits][M][N]
+// in part order and writes the FP32 row into slot `rank` of every rank's
+// buffer (peer pointers from CUDA IPC), raises flag (rank, row) on each with
+// the call's epoch, waits (bounded) for every rank's flag `row` on its own
+// buffer, then adds the slots in rank order (the same sum on every rank) and
+// applies residual = round(residual + round(sum)); with norm_w it writes xn =
+// RMSNorm(residual row) * norm_w (the RMSNorm rows law).  Buffers alternate by
+// epoch parity so a rank running one call ahead never overwrites a slot still
+// being read.  M <= kPeerChunks; pdl: programmatic dependent launch.
 constexpr int kPeerMaxRanks = 8;
-constexpr int kPeerChunks = 128;  // CTAs per call
+constexpr int kPeerChunks = 128;  // rows per call (one CTA each)
 struct PeerBuffers {
   float* data[kPeerMaxRanks];       // [2][ranks][capacity] FP32 on each rank
   unsigned* flags[kPeerMaxRanks];   // [2][ranks][kPeerChunks] on each rank
@@ -86,7 +88,8 @@ struct PeerBuffers {
   size_t capacity;                  // floats per slot
 };
 size_t peer_buffer_bytes(int ranks, size_t capacity);  // data + flags, one rank
-cudaError_t launch_peer_allreduce_residual(const PeerBuffers& pb, const float* parts, int splits, bf16* residual,
-                                           size_t n, cudaStream_t stream);
+cudaError_t launch_peer_allreduce_residual(const PeerBuffers& pb, const float* parts, int splits, int M, int N,
+                                           bf16* residual, const bf16* norm_w, bf16* xn, float eps,
+                                           cudaStream_t stream, bool pdl);
 
 }  // namespace dl
