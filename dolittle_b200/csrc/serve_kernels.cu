@@ -350,6 +350,17 @@ __global__ void __launch_bounds__(kAdThreads) attention_decode_split_kernel(
       }
     }
   }
+  if (splits == 1 && tickets) {
+    // One split: merging is the identity (weight expf(0) = 1), so the output
+    // is O / l directly, with no workspace round trip.
+    if (qrow) {
+      bf16* orow = out + (size_t(b) * query_heads + g * group + r) * 128 + 16 * warp + c2;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        *reinterpret_cast<__nv_bfloat162*>(orow + 8 * j) = __floats2bfloat162_rn(o[j][0] / l_run, o[j][1] / l_run);
+    }
+    return;
+  }
   if (qrow) {
     float* w = ws + ((size_t(b) * query_heads + g * group + r) * splits + s) * kAdWs;
     if (warp == 0 && (lane & 3) == 0) {
