@@ -760,22 +760,23 @@ void Server::decode_body() {
     // weights stream in while the previous kernel finishes.
     check(launch_gemm_tcgen05_parts(p, parts, parts_, stream_, true), "qkv parts");
     if (fused) {
-      check(launch_norm_rope_append_rows(nullptr, Q + 2 * G, y.q_norm, y.k_norm, inv_freq_, q_rot_, planes(l),
-                                         position_, B, hq_, hkv_, d, cfg_.epsilon, stream_, parts_, parts, true),
-            "qkv sum + norm rope append");
+      // The attention kernel builds the queries and appends the new key and
+      // value from the qkv parts itself.
+      const AttnQkvIn qi{parts_, parts, B, Q + 2 * G, y.q_norm, y.k_norm, inv_freq_, cfg_.epsilon};
+      check(launch_attention_decode_batched(q_rot_, planes(l), position_, B, hq_, hkv_, attn_splits_,
+                                            attention_scale(d), attn_ws_, att_, stream_, attn_tickets_, true, &qi),
+            "qkv parts + attention decode");
       launches_ += 2;
     } else {
       check(launch_gemm_splitk_epilogue(parts_, parts, B, p.N, kGemmStore, qkv_, p.N, nullptr, stream_), "qkv sum");
       check(launch_norm_rope_append_rows(qkv_, Q + 2 * G, y.q_norm, y.k_norm, inv_freq_, q_rot_, planes(l),
                                          position_, B, hq_, hkv_, d, cfg_.epsilon, stream_),
             "norm rope append");
-      launches_ += 3;
+      check(launch_attention_decode_batched(q_rot_, planes(l), position_, B, hq_, hkv_, attn_splits_,
+                                            attention_scale(d), attn_ws_, att_, stream_),
+            "attention decode");
+      launches_ += 5;
     }
-    check(launch_attention_decode_batched(q_rot_, planes(l), position_, B, hq_, hkv_, attn_splits_,
-                                          attention_scale(d), attn_ws_, att_, stream_,
-                                          fused ? attn_tickets_ : nullptr, fused),
-          "attention decode");
-    launches_ += fused ? 1 : 2;
     decode_projection_norm(att_, Q, y.wo, -1, y.post_norm);
     p.w = y.wgu;
     p.N = 2 * F;

@@ -223,10 +223,12 @@ __device__ __forceinline__ float combine_splits(const float* w, int splits, int 
 // for the next launch) instead of a separate combine launch.  Under a
 // programmatic dependent launch the key tiles that end before the newest
 // position (written by the previous kernel) are requested before waiting.
+// qi.parts (optional): the queries, the new key and the new value come from
+// the qkv projection's split-K parts instead (see AttnQkvIn).
 __global__ void __launch_bounds__(kAdThreads) attention_decode_split_kernel(
     const bf16* __restrict__ q, KvPlanes planes, const long long* __restrict__ position, int query_heads,
     int kv_heads, int splits, float scale, float* __restrict__ ws, int* __restrict__ tickets,
-    bf16* __restrict__ out) {
+    bf16* __restrict__ out, AttnQkvIn qi) {
   extern __shared__ __align__(16) unsigned char smem[];
   bf16* stage = reinterpret_cast<bf16*>(smem);
   bf16* ps = reinterpret_cast<bf16*>(smem + size_t(kAdStages) * kAdStageElems * 2);  // [16][72]
@@ -275,18 +277,64 @@ __global__ void __launch_bounds__(kAdThreads) attention_decode_split_kernel(
   }
   allow_next();
   wait_prior();
+  // The third ring slot is not loaded before the main loop: scratch for the
+  // queries built from the qkv parts ([8][128] BF16 rotated queries, [8][128]
+  // BF16 staged sums, [8][128] FP32 norm values).
+  bf16* qsm = stage + 2 * kAdStageElems;
+  if (qi.parts) {
+    bf16* staged = qsm + 8 * 128;
+    float* vals = reinterpret_cast<float*>(staged + 8 * 128);
+    const int p = count - 1;
+    const bool owns = j0 <= p && p < j1;  // this split holds the newest key
+    const int Qw = query_heads * 128;
+    // Jobs: query heads 0 .. group-1 of the group, then its key and value
+    // (only for the split holding them); warp w takes jobs w and w + 8.
+    for (int job = warp; job < group + 2; job += kAdThreads / 32) {
+      if (job >= group && !owns) continue;
+      const int col = job < group ? (g * group + job) * 128 : Qw + (job - group) * int(G) + g * 128;
+      const float* src = qi.parts + size_t(b) * qi.ld + col + 4 * lane;
+      float4 acc = *reinterpret_cast<const float4*>(src);
+      for (int sp = 1; sp < qi.splits; ++sp) {
+        const float4 v = *reinterpret_cast<const float4*>(src + size_t(sp) * qi.M * qi.ld);
+        acc.x = __fadd_rn(acc.x, v.x);
+        acc.y = __fadd_rn(acc.y, v.y);
+        acc.z = __fadd_rn(acc.z, v.z);
+        acc.w = __fadd_rn(acc.w, v.w);
+      }
+      bf16* st = staged + (job & 7) * 128;
+      __nv_bfloat162* d2 = reinterpret_cast<__nv_bfloat162*>(st + 4 * lane);
+      d2[0] = __floats2bfloat162_rn(acc.x, acc.y);
+      d2[1] = __floats2bfloat162_rn(acc.z, acc.w);
+      __syncwarp();
+      bf16* seq = planes.kv + size_t(b) * planes.seq_stride;
+      if (job < group) {
+        qk_norm_rope_warp(st, qi.q_norm, qi.inv_freq, p, qsm + job * 128, 128, qi.eps, vals + (job & 7) * 128);
+      } else if (job == group) {
+        qk_norm_rope_warp(st, qi.k_norm, qi.inv_freq, p, seq + planes.k_off + size_t(p) * G + size_t(g) * 128, 128,
+                          qi.eps, vals + (job & 7) * 128);
+      } else {
+        bf16* dst = seq + planes.v_off + size_t(p) * G + size_t(g) * 128;
+        reinterpret_cast<uint2*>(dst)[lane] = reinterpret_cast<const uint2*>(st)[lane];
+      }
+      __syncwarp();
+    }
+    __threadfence();  // the new K / V row is read back through the cache loads below
+    __syncthreads();
+  }
   for (; pre < kAdStages - 1; ++pre) {
     if (pre < tiles) load_tile(pre, pre);
     else asm volatile("cp.async.commit_group;" ::: "memory");
   }
   // Q fragments of the 8 k-steps (rows r < group; rows 8..15 are zero).
   uint32_t qa[8][2];
-  const bf16* qh = q + (size_t(b) * query_heads + g * group + (qrow ? r : 0)) * 128;
+  const bf16* qh = qi.parts ? qsm + (qrow ? r : 0) * 128
+                            : q + (size_t(b) * query_heads + g * group + (qrow ? r : 0)) * 128;
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk) {
     qa[kk][0] = qrow ? *reinterpret_cast<const uint32_t*>(qh + 16 * kk + c2) : 0u;
     qa[kk][1] = qrow ? *reinterpret_cast<const uint32_t*>(qh + 16 * kk + 8 + c2) : 0u;
   }
+  if (qi.parts) __syncthreads();  // every fragment read before slot 2 is loaded
   for (int tile = 0; tile < tiles; ++tile) {
     const int slot = tile % kAdStages;
     asm volatile("cp.async.wait_group %0;" ::"n"(kAdStages - 2) : "memory");
@@ -618,16 +666,24 @@ int attention_decode_splits(int batch, int kv_heads, int capacity, int sms) {
 
 cudaError_t launch_attention_decode_batched(const bf16* q, KvPlanes planes, const long long* position, int batch,
                                             int query_heads, int kv_heads, int splits, float scale, float* ws,
-                                            bf16* out, cudaStream_t stream, int* tickets, bool pdl) {
+                                            bf16* out, cudaStream_t stream, int* tickets, bool pdl,
+                                            const AttnQkvIn* qkv) {
   if (query_heads % kv_heads || query_heads / kv_heads > kAdMaxGroup || splits < 1 || splits > 64 || batch < 1)
     return cudaErrorInvalidValue;
+  AttnQkvIn qi = {};
+  if (qkv) {
+    qi = *qkv;
+    if (!qi.parts || qi.splits < 1 || qi.M < batch || qi.ld % 4 || qi.ld != (query_heads + 2 * kv_heads) * 128 ||
+        reinterpret_cast<uintptr_t>(qi.parts) % 16)
+      return cudaErrorInvalidValue;
+  }
   cudaError_t e = cudaFuncSetAttribute(attention_decode_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        int(kAdSmem));
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[1];
   auto cfg = pdl_config(dim3(kv_heads, splits, batch), dim3(kAdThreads), kAdSmem, stream, attr, pdl);
   e = cudaLaunchKernelEx(&cfg, attention_decode_split_kernel, q, planes, position, query_heads, kv_heads, splits,
-                         scale, ws, tickets, out);
+                         scale, ws, tickets, out, qi);
   if (e != cudaSuccess || tickets) return e;
   attention_decode_combine_kernel<<<dim3(query_heads, batch), 128, 0, stream>>>(ws, query_heads, splits, out);
   return cudaGetLastError();

@@ -52,10 +52,24 @@ int attention_decode_splits(int batch, int kv_heads, int capacity, int sms);
 // last split of each (sequence, KV head) merges the splits itself, no
 // combine launch.  pdl: programmatic dependent launch (the key tiles before
 // the newest position are requested before waiting for the previous kernel).
+// qkv (optional): the batch's qkv projection as split-K parts [splits][M][ld]
+// FP32 (ld = (Hq + 2 Hkv) * 128).  Each CTA then builds its group's queries
+// itself (parts summed in part order and rounded to BF16, QK-norm + RoPE: the
+// law of launch_norm_rope_append_rows with parts), and the split that holds
+// the newest position appends that position's key (QK-norm + RoPE) and value
+// to the cache before reading it; q is not read.
+struct AttnQkvIn {
+  const float* parts;
+  int splits, M, ld;
+  const bf16* q_norm;
+  const bf16* k_norm;
+  const float* inv_freq;
+  float eps;
+};
 cudaError_t launch_attention_decode_batched(const bf16* q, KvPlanes planes, const long long* position, int batch,
                                             int query_heads, int kv_heads, int splits, float scale, float* ws,
                                             bf16* out, cudaStream_t stream, int* tickets = nullptr,
-                                            bool pdl = false);
+                                            bool pdl = false, const AttnQkvIn* qkv = nullptr);
 
 // Vocabulary-split head: src [t][B][Vp] (rank r's logits of vocabulary rows
 // [r Vl, (r+1) Vl) in its first Vl columns) -> dst [B][t Vl].
