@@ -429,11 +429,12 @@ DL_API dl_status dl_serve_set_steering(dl_serve* s, int layer, size_t first_posi
 /* The beta the steering edit used (host read). */
 DL_API dl_status dl_serve_steering_strength(dl_serve* s, float* beta);
 /* Decode step form: 1 (default) folds the split-K sums into the kernels that
- * consume them (QK-norm/RoPE/KV append; residual add + RMSNorm), merges the
- * attention splits in their last CTA and chains the kernels as programmatic
- * dependent launches; 0 runs every step as separate kernels.  Both give the
- * same bits; the switch exists to check that.  Takes effect at the next
- * decode call. */
+ * consume them (the attention kernel builds its queries and appends the new
+ * key/value from the qkv parts and merges its own splits; the o / down parts
+ * go through residual add + RMSNorm, over NVLink peer memory under tensor
+ * parallelism) and chains the kernels as programmatic dependent launches;
+ * 0 runs every step as separate kernels.  Both give the same bits; the
+ * switch exists to check that.  Takes effect at the next decode call. */
 DL_API dl_status dl_serve_set_step_fusion(dl_serve* s, int on);
 
 /* Split-K GEMM for few rows: Y = epilogue(X W^T) as dl_gemm_bf16, the K
