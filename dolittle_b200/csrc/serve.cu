@@ -725,15 +725,23 @@ void Server::decode_projection_norm(const bf16* x, int K, const bf16* w, int lay
 // them (QK-norm/RoPE/append, residual + RMSNorm), the attention splits merged
 // by their last CTA, and every kernel of the chain a programmatic dependent
 // launch.  Same arithmetic as the unfused step, bit for bit.
-// Decode all-reduces over NVLink peer memory (NCCL when
-// DOLITTLE_TP_ALLREDUCE=nccl): one CTA per row, so at most kPeerChunks rows.
+// Decode all-reduces over NVLink peer memory for two ranks, NCCL for more:
+// every rank writes its whole partial to every other rank, so the bytes a
+// rank sends grow with t - 1 while NCCL's in-switch and tree reductions do
+// not.  Measured at batch 32, 2K context: peer 4.73 / NCCL 4.55 ms per step at
+// four ranks, 5.70 / 4.74 ms at eight; even at two (where the peer kernel also
+// applies the next RMSNorm).  DOLITTLE_TP_ALLREDUCE=nccl or =peer overrides.
+// One CTA per row, so at most kPeerChunks rows.
 bool Server::peer_decode(int rows) const {
-  static const bool use_nccl = [] {
+  static const int mode = [] {
     const char* v = std::getenv("DOLITTLE_TP_ALLREDUCE");
-    return v && std::string(v) == "nccl";
+    if (v && std::string(v) == "nccl") return 1;
+    if (v && std::string(v) == "peer") return 2;
+    return 0;
   }();
-  return tp_ > 1 && peers_ && !use_nccl && rows <= kPeerChunks && size_t(rows) * D_ <= pb_.capacity &&
-         D_ % 8 == 0 && D_ > 128 && D_ <= 8192;
+  const bool peer = mode == 2 || (mode == 0 && tp_ == 2);
+  return tp_ > 1 && peers_ && peer && rows <= kPeerChunks && size_t(rows) * D_ <= pb_.capacity && D_ % 8 == 0 &&
+         D_ > 128 && D_ <= 8192;
 }
 
 bool Server::fused_step() const { return fuse_ && d_ == 128 && D_ > 128 && D_ % 8 == 0 && D_ <= 8192; }
