@@ -715,16 +715,35 @@ void Server::decode_projection_norm(const bf16* x, int K, const bf16* w, int lay
     launches_ += 2;
     return;
   }
+  if (fold && tp_ > 1) {
+    // NCCL: the parts summed in part order, the all-reduce, then one kernel
+    // for the residual add and the norm (the parts kernel with one part).
+    GemmProblem p = {};
+    p.err = err_;
+    p.x = x;
+    p.ldx = K;
+    p.w = w;
+    p.M = B;
+    p.N = D;
+    p.K = K;
+    const int parts = gemm_splitk_parts(B, D, K, sms_);
+    check(launch_gemm_tcgen05_parts(p, parts, parts_, stream_, true), "gemm parts");
+    if (parts > 1) {
+      check(launch_gemm_splitk_epilogue(parts_, parts, B, D, kGemmStore, nullptr, D, parts_, stream_), "splitk sum");
+      ++launches_;
+    }
+    all_reduce(parts_, size_t(B) * D);
+    check(launch_residual_norm_rows(parts_, 1, B, D, residual_, norm_w, xn_, cfg_.epsilon, stream_, false),
+          "residual norm");
+    launches_ += 3;
+    return;
+  }
   row_projection_out(x, K, w, B, K, true);
   if (layer >= 0) block_output_hooks_decode(size_t(layer));
   check(launch_rms_norm(residual_, norm_w, xn_, batch_, D, cfg_.epsilon, stream_, fused_step()), "rms_norm");
   ++launches_;
 }
 
-// The fused decode step: split-K sums folded into the kernels that consume
-// them (QK-norm/RoPE/append, residual + RMSNorm), the attention splits merged
-// by their last CTA, and every kernel of the chain a programmatic dependent
-// launch.  Same arithmetic as the unfused step, bit for bit.
 // Decode all-reduces over NVLink peer memory for two ranks, NCCL for more:
 // every rank writes its whole partial to every other rank, so the bytes a
 // rank sends grow with t - 1 while NCCL's in-switch and tree reductions do
@@ -744,6 +763,10 @@ bool Server::peer_decode(int rows) const {
          D_ > 128 && D_ <= 8192;
 }
 
+// The fused decode step: split-K sums folded into the kernels that consume
+// them (the attention kernel, residual + RMSNorm), the attention splits
+// merged by their last CTA, and every kernel of the chain a programmatic
+// dependent launch.  Same arithmetic as the unfused step, bit for bit.
 bool Server::fused_step() const { return fuse_ && d_ == 128 && D_ > 128 && D_ % 8 == 0 && D_ <= 8192; }
 
 // One decode step for all B rows at the shared position.  xn_ holds the
