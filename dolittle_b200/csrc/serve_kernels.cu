@@ -23,19 +23,13 @@ __global__ void fill_normal_slice_kernel(bf16* out, size_t rows, size_t cols, si
 constexpr int kRopeWarps = 8;
 
 // Heads [0, Hq): queries; [Hq, Hq+Hkv): keys; [Hq+Hkv, Hq+2Hkv): values
-// (copied).  One warp per (row, head).  PARTS: the row is the split-K parts
-// [splits][M][ld] FP32 of the qkv projection, added in part order and
-// rounded to BF16 here (the split-K store epilogue's law), so the BF16 qkv
-// rows never go through global memory.
-template <bool PARTS>
-__global__ void norm_rope_append_rows_kernel(const bf16* __restrict__ qkv, const float* __restrict__ parts,
-                                             int splits, int M, int ld, const bf16* __restrict__ qw,
+// (copied).  One warp per (row, head).
+__global__ void norm_rope_append_rows_kernel(const bf16* __restrict__ qkv, int ld, const bf16* __restrict__ qw,
                                              const bf16* __restrict__ kw, const float* __restrict__ inv_freq,
                                              bf16* __restrict__ q_out, KvPlanes planes,
                                              const long long* __restrict__ position, int query_heads, int kv_heads,
                                              int width, float eps) {
   __shared__ float vals[kRopeWarps][128];
-  __shared__ __align__(16) bf16 staged[PARTS ? kRopeWarps : 1][128];
   allow_next();
   wait_prior();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -44,25 +38,7 @@ __global__ void norm_rope_append_rows_kernel(const bf16* __restrict__ qkv, const
   if (head >= query_heads + 2 * kv_heads) return;
   const int p = int(*position);
   const size_t G = size_t(kv_heads) * width;
-  const bf16* row = qkv + size_t(b) * ld;
-  const bf16* src = row + size_t(head) * width;  // q, k and v heads are consecutive
-  if constexpr (PARTS) {
-    // Lane l: columns 4l .. 4l + 3 of the head (width 128).
-    const size_t col = size_t(head) * width + 4 * lane;
-    float4 acc = *reinterpret_cast<const float4*>(parts + size_t(b) * ld + col);
-    for (int s = 1; s < splits; ++s) {
-      const float4 v = *reinterpret_cast<const float4*>(parts + (size_t(s) * M + b) * ld + col);
-      acc.x = __fadd_rn(acc.x, v.x);
-      acc.y = __fadd_rn(acc.y, v.y);
-      acc.z = __fadd_rn(acc.z, v.z);
-      acc.w = __fadd_rn(acc.w, v.w);
-    }
-    __nv_bfloat162* d = reinterpret_cast<__nv_bfloat162*>(staged[warp] + 4 * lane);
-    d[0] = __floats2bfloat162_rn(acc.x, acc.y);
-    d[1] = __floats2bfloat162_rn(acc.z, acc.w);
-    __syncwarp();
-    src = staged[warp];
-  }
+  const bf16* src = qkv + size_t(b) * ld + size_t(head) * width;  // q, k and v heads are consecutive
   bf16* seq = planes.kv + size_t(b) * planes.seq_stride;
   if (head < query_heads) {
     qk_norm_rope_warp(src, qw, inv_freq, p, q_out + (size_t(b) * query_heads + head) * width, width, eps,
@@ -606,21 +582,14 @@ cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t s
 cudaError_t launch_norm_rope_append_rows(const bf16* qkv, int ld, const bf16* q_norm_w, const bf16* k_norm_w,
                                          const float* inv_freq, bf16* q_out, KvPlanes planes,
                                          const long long* position, int batch, int query_heads, int kv_heads,
-                                         int width, float eps, cudaStream_t stream, const float* parts, int splits,
-                                         bool pdl) {
-  if (width > 128 || width % 2 || batch < 1) return cudaErrorInvalidValue;
-  if (parts && (width != 128 || ld % 4 || splits < 1 || reinterpret_cast<uintptr_t>(parts) % 16))
-    return cudaErrorInvalidValue;
-  if (!parts && !qkv) return cudaErrorInvalidValue;
+                                         int width, float eps, cudaStream_t stream, bool pdl) {
+  if (width > 128 || width % 2 || batch < 1 || !qkv) return cudaErrorInvalidValue;
   const int heads = query_heads + 2 * kv_heads;
   cudaLaunchAttribute attr[1];
   auto cfg = pdl_config(dim3(batch, (heads + kRopeWarps - 1) / kRopeWarps), dim3(32 * kRopeWarps), 0, stream, attr,
                         pdl);
-  if (parts)
-    return cudaLaunchKernelEx(&cfg, norm_rope_append_rows_kernel<true>, qkv, parts, splits, batch, ld, q_norm_w,
-                              k_norm_w, inv_freq, q_out, planes, position, query_heads, kv_heads, width, eps);
-  return cudaLaunchKernelEx(&cfg, norm_rope_append_rows_kernel<false>, qkv, parts, splits, batch, ld, q_norm_w,
-                            k_norm_w, inv_freq, q_out, planes, position, query_heads, kv_heads, width, eps);
+  return cudaLaunchKernelEx(&cfg, norm_rope_append_rows_kernel, qkv, ld, q_norm_w, k_norm_w, inv_freq, q_out, planes,
+                            position, query_heads, kv_heads, width, eps);
 }
 
 cudaError_t launch_residual_norm_rows(const float* parts, int splits, int M, int N, bf16* residual, const bf16* w,

@@ -24,15 +24,12 @@ cudaError_t launch_fill_normal_slice(bf16* out, size_t rows, size_t cols, size_t
 // Batched decode: row b of qkv [B][Hq*d + 2*Hkv*d] (row stride ld) is
 // sequence b's token at the shared position *position.  Queries get QK-norm
 // + RoPE into q_out [B][Hq][d]; keys get QK-norm + RoPE and values are copied,
-// both into sequence b's cache at that position.  With `parts` (d = 128) the
-// rows are instead the projection's split-K parts [splits][B][ld] FP32,
-// added in part order and rounded to BF16 first (qkv unused).  pdl: launched
-// as a programmatic dependent of the previous kernel.
+// both into sequence b's cache at that position.  pdl: launched as a
+// programmatic dependent of the previous kernel.
 cudaError_t launch_norm_rope_append_rows(const bf16* qkv, int ld, const bf16* q_norm_w, const bf16* k_norm_w,
                                          const float* inv_freq, bf16* q_out, KvPlanes planes,
                                          const long long* position, int batch, int query_heads, int kv_heads,
-                                         int width, float eps, cudaStream_t stream, const float* parts = nullptr,
-                                         int splits = 1, bool pdl = false);
+                                         int width, float eps, cudaStream_t stream, bool pdl = false);
 
 // residual[m] = round(residual[m] + round(sum of parts [splits][M][N] in part
 // order)), then xn[m] = RMSNorm(residual[m]) * w (the RMSNorm rows law, N >
