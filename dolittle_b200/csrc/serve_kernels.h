@@ -40,21 +40,23 @@ cudaError_t launch_residual_norm_rows(const float* parts, int splits, int M, int
 
 // Split-K flash decoding: for every sequence b and query head h, attention of
 // q [B][Hq][128] over keys 0 .. *position of b's cache, the keys cut into
-// `splits` ranges whose (max, sum, unnormalised output) go to ws
-// [B][Hq][splits][130] FP32; the combine kernel merges them into out
-// [B][Hq*128] BF16.  Online softmax: not the reference's reduction order.
+// `splits` ranges (attention_decode_splits: a wave-cost model) whose (max,
+// sum, unnormalised output) go to ws [B][Hq][splits][130] FP32, merged into
+// out [B][Hq*128] BF16 by the combine kernel.  Online softmax: not the
+// reference's reduction order.
 size_t attention_decode_ws_floats(int batch, int query_heads, int splits);
 int attention_decode_splits(int batch, int kv_heads, int capacity, int sms);
 // tickets ([B][Hkv] int, zeroed once; each launch leaves them zero): the
 // last split of each (sequence, KV head) merges the splits itself, no
-// combine launch.  pdl: programmatic dependent launch (the key tiles before
-// the newest position are requested before waiting for the previous kernel).
+// combine launch (with one split the CTA writes O / l directly).  pdl:
+// programmatic dependent launch (the key tiles before the newest position
+// are requested before waiting for the previous kernel).
 // qkv (optional): the batch's qkv projection as split-K parts [splits][M][ld]
 // FP32 (ld = (Hq + 2 Hkv) * 128).  Each CTA then builds its group's queries
-// itself (parts summed in part order and rounded to BF16, QK-norm + RoPE: the
-// law of launch_norm_rope_append_rows with parts), and the split that holds
-// the newest position appends that position's key (QK-norm + RoPE) and value
-// to the cache before reading it; q is not read.
+// itself (parts summed in part order and rounded to BF16, QK-norm + RoPE with
+// the same warp routine as launch_norm_rope_append_rows), and the split that
+// holds the newest position appends that position's key (QK-norm + RoPE) and
+// value to the cache before reading it; q is not read.
 struct AttnQkvIn {
   const float* parts;
   int splits, M, ld;
