@@ -219,6 +219,15 @@ __global__ void greedy_kernel(const void* row, bool bf16_in, unsigned n, uint4* 
   result[0] = result[1] ? 0u : bid;
 }
 
+// result[0..1] of every row back to zero before a selection.
+__global__ void clear_results_kernel(unsigned* result, size_t stride, unsigned rows) {
+  const unsigned row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  unsigned* r = reinterpret_cast<unsigned*>(reinterpret_cast<unsigned char*>(result) + row * stride);
+  r[0] = 0;
+  r[1] = 0;
+}
+
 // ---- categorical -------------------------------------------------------------
 __global__ void keys_kernel(const void* row, bool bf16_in, unsigned n, uint2* keys, unsigned* result, size_t stride,
                             size_t row_bytes) {
@@ -243,18 +252,29 @@ __device__ __forceinline__ void block_digit_ranks(unsigned digit, bool live, uns
   __syncthreads();
 }
 
+// Radix blocks of kRadixPer consecutive 256-key tiles: fewer, longer CTAs
+// (and fewer per-block counts to scan) than one tile per CTA.
+constexpr unsigned kRadixPer = 8;
+constexpr unsigned kRadixBlock = kW * kRadixPer;
+
 __global__ void histogram_kernel(const uint2* keys, unsigned n, unsigned shift, unsigned* counts, size_t stride) {
-  __shared__ unsigned bins[kWarps][kW];
+  __shared__ unsigned bins[kW];
   keys = at_row(keys, stride);
   counts = at_row(counts, stride);
-  const unsigned i = blockIdx.x * kW + threadIdx.x;
-  const bool live = i < n;
-  const unsigned digit = live ? (keys[i].x >> shift) & 0xffu : 0u;
-  unsigned peers;
-  block_digit_ranks(digit, live, bins, peers);
-  unsigned total = 0;
-  for (unsigned w = 0; w < kWarps; ++w) total += bins[w][threadIdx.x];
-  counts[blockIdx.x * kW + threadIdx.x] = total;
+  const unsigned lane = threadIdx.x & 31;
+  bins[threadIdx.x] = 0;
+  __syncthreads();
+#pragma unroll
+  for (unsigned e = 0; e < kRadixPer; ++e) {
+    const unsigned i = blockIdx.x * kRadixBlock + e * kW + threadIdx.x;
+    const bool live = i < n;
+    const unsigned digit = live ? (keys[i].x >> shift) & 0xffu : 0x100u;
+    // One shared-memory add per distinct digit of the warp.
+    const unsigned peers = __match_any_sync(0xffffffffu, digit);
+    if (live && lane == unsigned(__ffs(int(peers)) - 1)) atomicAdd(&bins[digit], unsigned(__popc(peers)));
+  }
+  __syncthreads();
+  counts[blockIdx.x * kW + threadIdx.x] = bins[threadIdx.x];
 }
 
 // Radix offsets, in two halves.  This kernel turns each digit column of the
@@ -306,6 +326,7 @@ __global__ void scatter_kernel(const uint2* in, uint2* out, unsigned n, unsigned
   __shared__ unsigned bins[kWarps][kW];
   __shared__ unsigned digit_base[kW];
   __shared__ unsigned warp_sum[kWarps];
+  __shared__ unsigned running[kW], block_offset[kW];
   in = at_row(in, stride);
   out = at_row(out, stride);
   offsets = at_row(offsets, stride);
@@ -325,18 +346,31 @@ __global__ void scatter_kernel(const uint2* in, uint2* out, unsigned n, unsigned
     for (unsigned k = 0; k < wp; ++k) before += warp_sum[k];
     digit_base[threadIdx.x] = before + v - t;
   }
-  // (block_digit_ranks starts with a CTA barrier, which publishes digit_base.)
-  const unsigned i = blockIdx.x * kW + threadIdx.x;
-  const bool live = i < n;
-  const uint2 k = live ? in[i] : make_uint2(0, 0);
-  const unsigned digit = (k.x >> shift) & 0xffu;
-  unsigned peers;
-  block_digit_ranks(digit, live, bins, peers);
-  if (!live) return;
+  // The block's tiles in key order; running[d] = keys with digit d in the
+  // tiles before (block_digit_ranks starts with a CTA barrier, which
+  // publishes digit_base and running).
+  running[threadIdx.x] = 0;
   const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  unsigned rank = __popc(peers & ((1u << lane) - 1u));
-  for (unsigned w = 0; w < warp; ++w) rank += bins[w][digit];
-  out[digit_base[digit] + offsets[blockIdx.x * kW + digit] + rank] = k;
+  const unsigned base = offsets[blockIdx.x * kW + threadIdx.x];  // thread = digit
+  block_offset[threadIdx.x] = base;
+  for (unsigned e = 0; e < kRadixPer; ++e) {
+    const unsigned i = blockIdx.x * kRadixBlock + e * kW + threadIdx.x;
+    const bool live = i < n;
+    const uint2 k = live ? in[i] : make_uint2(0, 0);
+    const unsigned digit = (k.x >> shift) & 0xffu;
+    unsigned peers;
+    block_digit_ranks(digit, live, bins, peers);
+    if (live) {
+      unsigned rank = running[digit] + __popc(peers & ((1u << lane) - 1u));
+      for (unsigned w = 0; w < warp; ++w) rank += bins[w][digit];
+      out[digit_base[digit] + block_offset[digit] + rank] = k;
+    }
+    __syncthreads();  // ranks read running and bins
+    unsigned add = 0;
+    for (unsigned w = 0; w < kWarps; ++w) add += bins[w][threadIdx.x];
+    running[threadIdx.x] += add;
+    __syncthreads();  // running complete; bins free
+  }
 }
 
 __global__ void weights_kernel(const void* row, bool bf16_in, const uint2* sorted, unsigned keep,
@@ -533,9 +567,7 @@ cudaError_t sampler_submit(Sampler& s, const void* row, const dl_sampling& st, u
   const Layout L = layout(s.arena, s.vocabulary);
   const unsigned n = unsigned(s.vocabulary), blocks = (n + kW - 1) / kW, R = s.rows;
   const size_t S = s.stride, row_bytes = row_stride * (s.bf16_input ? 2 : 4);
-  cudaError_t e = cudaSuccess;
-  for (unsigned r = 0; r < R && e == cudaSuccess; ++r) e = cudaMemsetAsync(L.result + r * S / 4, 0, 8, stream);
-  if (e != cudaSuccess) return e;
+  clear_results_kernel<<<(R + 255) / 256, 256, 0, stream>>>(L.result, S, R);
   const bool greedy = st.mode == 0;
   if (owned) next_random_kernel<<<dim3(1, R), 1, 0, stream>>>(L.state, greedy, S);
   if (greedy) {
@@ -544,10 +576,12 @@ cudaError_t sampler_submit(Sampler& s, const void* row, const dl_sampling& st, u
     keys_kernel<<<dim3(blocks, R), kW, 0, stream>>>(row, s.bf16_input, n, L.keys_a, L.result, S, row_bytes);
     uint2* in = L.keys_a;
     uint2* out = L.keys_b;
+    const unsigned radix_blocks = (n + kRadixBlock - 1) / kRadixBlock;
     for (unsigned shift = s.bf16_input ? 16 : 0; shift < 32; shift += 8) {
-      histogram_kernel<<<dim3(blocks, R), kW, 0, stream>>>(in, n, shift, L.counts, S);
-      digit_offsets_kernel<<<dim3(kW / 32, R), 32 * kOffsetWarps, 0, stream>>>(L.counts, L.digit_totals, blocks, S);
-      scatter_kernel<<<dim3(blocks, R), kW, 0, stream>>>(in, out, n, shift, L.counts, L.digit_totals, S);
+      histogram_kernel<<<dim3(radix_blocks, R), kW, 0, stream>>>(in, n, shift, L.counts, S);
+      digit_offsets_kernel<<<dim3(kW / 32, R), 32 * kOffsetWarps, 0, stream>>>(L.counts, L.digit_totals,
+                                                                                 radix_blocks, S);
+      scatter_kernel<<<dim3(radix_blocks, R), kW, 0, stream>>>(in, out, n, shift, L.counts, L.digit_totals, S);
       uint2* t = in;
       in = out;
       out = t;
@@ -571,7 +605,7 @@ cudaError_t sampler_submit(Sampler& s, const void* row, const dl_sampling& st, u
 int sampler_launch_count(const Sampler& s, const dl_sampling& st, bool owned) {
   const int radix_passes = s.bf16_input ? 2 : 4;
   const int body = st.mode == 0 ? 1 : 1 + 3 * radix_passes + 5;
-  return body + (owned ? 2 : 0);
+  return 1 + body + (owned ? 2 : 0);  // the result clear, the selection, the draw and commit
 }
 
 unsigned* sampler_result(const Sampler& s, unsigned row) {
