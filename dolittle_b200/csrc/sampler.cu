@@ -256,6 +256,7 @@ __device__ __forceinline__ void block_digit_ranks(unsigned digit, bool live, uns
 // (and fewer per-block counts to scan) than one tile per CTA.
 constexpr unsigned kRadixPer = 8;
 constexpr unsigned kRadixBlock = kW * kRadixPer;
+static_assert(kRadixPer == kWarps, "weights_kernel scans tile w with warp w");
 
 __global__ void histogram_kernel(const uint2* keys, unsigned n, unsigned shift, unsigned* counts, size_t stride) {
   __shared__ unsigned bins[kW];
@@ -373,33 +374,45 @@ __global__ void scatter_kernel(const uint2* in, uint2* out, unsigned n, unsigned
   }
 }
 
+// kRadixPer tiles of 256 sorted keys per CTA: the weights of every key, then
+// each tile's serial FP64 prefix (the law's order) by one lane per tile, the
+// tiles side by side.
 __global__ void weights_kernel(const void* row, bool bf16_in, const uint2* sorted, unsigned keep,
                                double temperature, double* prefix, double* tile_totals, size_t stride,
                                size_t row_bytes) {
-  __shared__ double tile[kW];
+  __shared__ double tile[kRadixPer][kW];
   row = static_cast<const unsigned char*>(row) + blockIdx.y * row_bytes;
   sorted = at_row(sorted, stride);
   prefix = at_row(prefix, stride);
   tile_totals = at_row(tile_totals, stride);
-  const unsigned i = blockIdx.x * kW + threadIdx.x;
-  double w = 0.0;
-  if (i < keep) {
-    const double best = static_cast<double>(load_logit(row, sorted[0].y, bf16_in));
-    const double v = static_cast<double>(load_logit(row, sorted[i].y, bf16_in));
-    if (isfinite(v)) w = exp((v - best) / temperature);
+  const double best = static_cast<double>(load_logit(row, sorted[0].y, bf16_in));
+#pragma unroll
+  for (unsigned e = 0; e < kRadixPer; ++e) {
+    const unsigned i = blockIdx.x * kRadixBlock + e * kW + threadIdx.x;
+    double w = 0.0;
+    if (i < keep) {
+      const double v = static_cast<double>(load_logit(row, sorted[i].y, bf16_in));
+      if (isfinite(v)) w = exp((v - best) / temperature);
+    }
+    tile[e][threadIdx.x] = w;
   }
-  tile[threadIdx.x] = w;
   __syncthreads();
-  if (threadIdx.x == 0) {
+  const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;  // kWarps == kRadixPer
+  const unsigned t = blockIdx.x * kRadixPer + warp;                // this warp's tile
+  if (lane == 0 && t * kW < keep) {
     double sum = 0.0;
     for (unsigned j = 0; j < kW; ++j) {
-      sum += tile[j];
-      tile[j] = sum;
+      sum += tile[warp][j];
+      tile[warp][j] = sum;
     }
-    tile_totals[blockIdx.x] = sum;
+    tile_totals[t] = sum;
   }
   __syncthreads();
-  if (i < keep) prefix[i] = tile[threadIdx.x];
+#pragma unroll
+  for (unsigned e = 0; e < kRadixPer; ++e) {
+    const unsigned i = blockIdx.x * kRadixBlock + e * kW + threadIdx.x;
+    if (i < keep) prefix[i] = tile[e][threadIdx.x];
+  }
 }
 
 // Serial exclusive scan of the tile totals (the law's FP64 order), on a
@@ -444,9 +457,12 @@ __global__ void cutoff_kernel(const double* prefix, const double* offsets, unsig
   prefix = at_row(prefix, stride);
   offsets = at_row(offsets, stride);
   scan = at_row(scan, stride);
-  const unsigned i = blockIdx.x * kW + threadIdx.x;
   unsigned c = 0xffffffffu;
-  if (i < keep && (offsets[blockIdx.x] + prefix[i]) / scan->total >= top_p) c = i;
+  const double total = scan->total;
+  for (unsigned e = 0; e < kRadixPer && c == 0xffffffffu; ++e) {
+    const unsigned t = blockIdx.x * kRadixPer + e, i = t * kW + threadIdx.x;
+    if (i < keep && (offsets[t] + prefix[i]) / total >= top_p) c = i;
+  }
   const unsigned first = block_min(c);
   if (threadIdx.x == 0 && first != 0xffffffffu) atomicMin(&scan->cutoff, first);
 }
@@ -457,12 +473,14 @@ __global__ void select_kernel(const double* prefix, const double* offsets, unsig
   offsets = at_row(offsets, stride);
   state = at_row(state, stride);
   scan = at_row(scan, stride);
-  const unsigned i = blockIdx.x * kW + threadIdx.x;
   const unsigned last = scan->cutoff;
   const double retained = offsets[last / kW] + prefix[last];
   const double u = state ? state->draw : draw;
   unsigned c = 0xffffffffu;
-  if (i <= last && i < keep && u < (offsets[blockIdx.x] + prefix[i]) / retained) c = i;
+  for (unsigned e = 0; e < kRadixPer && c == 0xffffffffu; ++e) {
+    const unsigned t = blockIdx.x * kRadixPer + e, i = t * kW + threadIdx.x;
+    if (i <= last && i < keep && u < (offsets[t] + prefix[i]) / retained) c = i;
+  }
   const unsigned first = block_min(c);
   if (threadIdx.x == 0 && first != 0xffffffffu) atomicMin(&scan->selected, first);
 }
@@ -587,11 +605,11 @@ cudaError_t sampler_submit(Sampler& s, const void* row, const dl_sampling& st, u
       out = t;
     }
     const unsigned keep = st.top_k ? unsigned(st.top_k) : n;
-    const unsigned kept_blocks = (keep + kW - 1) / kW;
+    const unsigned kept_tiles = (keep + kW - 1) / kW, kept_blocks = (keep + kRadixBlock - 1) / kRadixBlock;
     weights_kernel<<<dim3(kept_blocks, R), kW, 0, stream>>>(row, s.bf16_input, in, keep, st.temperature, L.prefix,
                                                             L.tile_totals, S, row_bytes);
-    scan_tiles_kernel<<<dim3(1, R), kW, kept_blocks * sizeof(double), stream>>>(L.tile_totals, keep, L.scan, L.result,
-                                                                                 S);
+    scan_tiles_kernel<<<dim3(1, R), kW, kept_tiles * sizeof(double), stream>>>(L.tile_totals, keep, L.scan, L.result,
+                                                                                S);
     cutoff_kernel<<<dim3(kept_blocks, R), kW, 0, stream>>>(L.prefix, L.tile_totals, keep, st.top_p, L.scan, S);
     const double draw = static_cast<double>(bits >> 11) * 0x1.0p-53;
     select_kernel<<<dim3(kept_blocks, R), kW, 0, stream>>>(L.prefix, L.tile_totals, keep, draw,
