@@ -286,7 +286,7 @@ __global__ void rms_norm_kernel(const bf16* x, const bf16* w, bf16* out, size_t 
 __global__ void rms_norm_rows_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w, bf16* __restrict__ out,
                                      int width, float eps) {
   extern __shared__ float xs[];  // [width]
-  __shared__ float chains[128];
+  __shared__ float chains[129];
   __shared__ float inv_s;
   allow_next();
   wait_prior();
@@ -307,17 +307,8 @@ __global__ void rms_norm_rows_kernel(const bf16* __restrict__ x, const bf16* __r
     // The staged law's component sums run as 128 independent chains, one
     // per thread (chain t = 4 * lane + c sums columns t, t + 128, ...); warp
     // 0 then adds each lane's four in order and runs the shuffle tree.
-    float chain = 0.f;
-    for (int col = threadIdx.x; col < width; col += 128) chain = __fadd_rn(chain, __fmul_rn(xs[col], xs[col]));
-    chains[threadIdx.x] = chain;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-      const float* c4 = chains + 4 * threadIdx.x;
-      float sum = __fadd_rn(__fadd_rn(__fadd_rn(c4[0], c4[1]), c4[2]), c4[3]);
-      sum = shuffle_down_tree32(sum);
-      const float total = __shfl_sync(0xffffffffu, sum, 0);
-      if (threadIdx.x == 0) inv_s = rsqrtf(__fadd_rn(__fmul_rn(total, 1.0f / static_cast<float>(width)), eps));
-    }
+    const float inv = rms_inverse_block(xs, width, eps, chains);
+    if (threadIdx.x == 0) inv_s = inv;
   } else if (threadIdx.x < 32) {
     const float inv = rms_inverse_warp(xs, width, eps);
     if (threadIdx.x == 0) inv_s = inv;

@@ -68,6 +68,14 @@ __global__ void __launch_bounds__(1024) residual_norm_rows_kernel(const float* _
                                                                   float eps) {
   extern __shared__ float xs[];  // [N]
   __shared__ float chains[129];
+  // The norm weight is constant: its loads start before waiting for the parts.
+  const uint4* wv = reinterpret_cast<const uint4*>(w);
+  uint4 wq[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int q = threadIdx.x + i * blockDim.x;
+    wq[i] = q < N / 8 ? wv[q] : make_uint4(0, 0, 0, 0);
+  }
   allow_next();
   wait_prior();
   const int m = blockIdx.x, n4 = N / 4;
@@ -111,10 +119,12 @@ __global__ void __launch_bounds__(1024) residual_norm_rows_kernel(const float* _
   }
   __syncthreads();
   const float inv = rms_inverse_block(xs, N, eps, chains);
-  const uint4* wv = reinterpret_cast<const uint4*>(w);
   uint4* dst = reinterpret_cast<uint4*>(xn + size_t(m) * N);
-  for (int q = threadIdx.x; q < N / 8; q += blockDim.x) {
-    const uint4 g = wv[q];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int q = threadIdx.x + j * blockDim.x;
+    if (q >= N / 8) continue;
+    const uint4 g = wq[j];
     const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
     uint32_t o[4];
 #pragma unroll
