@@ -233,6 +233,16 @@ void Server::connect(const unsigned char* id128) {
   ncclUniqueId id;
   std::memcpy(&id, id128, sizeof(id));
   check_nccl(nccl().comm_init_rank(&comm_, tp_, id, rank_), "ncclCommInitRank");
+  // NCCL sets up the connections of an algorithm the first time a message
+  // needs it, blocking the host for a second or more.  Run each collective
+  // once here, at the sizes the server uses (a prompt chunk's and a decode
+  // step's all-reduce, the logits all-gather; the buffers are scratch), so
+  // that cost belongs to connecting and not to the first prompt pass.
+  all_reduce(parts_, chunk_ * D_);
+  all_reduce(parts_, batch_ * D_);
+  check_nccl(nccl().all_gather(head_local_, head_gather_, batch_ * Vp_, ncclBfloat16, comm_, stream_),
+             "ncclAllGather");
+  check(cudaStreamSynchronize(stream_), "connect sync");
 }
 
 void Server::ipc_handle(unsigned char* out64) {
