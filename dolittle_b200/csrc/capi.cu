@@ -763,8 +763,8 @@ DL_API size_t dl_attention_decode_batched_workspace_bytes(size_t batch, size_t q
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int splits = dl::attention_decode_splits(int(batch), int(kv_heads), int(capacity), sms);
-  return dl::attention_decode_ws_floats(int(batch), int(query_heads), splits) * 4;
+  const dl::AttnPlan plan = dl::attention_decode_plan(int(batch), int(kv_heads), int(capacity), sms);
+  return dl::attention_decode_ws_floats(int(batch), int(query_heads), plan.splits) * 4;
 }
 
 DL_API dl_status dl_attention_decode_batched(const void* query, const void* kv, size_t seq_stride,
@@ -779,12 +779,13 @@ DL_API dl_status dl_attention_decode_batched(const void* query, const void* kv, 
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int splits = dl::attention_decode_splits(int(batch), int(kv_heads), int(capacity), sms);
+  const dl::AttnPlan plan = dl::attention_decode_plan(int(batch), int(kv_heads), int(capacity), sms);
   const dl::KvPlanes planes{static_cast<bf16*>(const_cast<void*>(kv)), seq_stride, k_offset, v_offset};
   return cuda_status(dl::launch_attention_decode_batched(static_cast<const bf16*>(query), planes,
                                                          reinterpret_cast<const long long*>(position), int(batch),
-                                                         int(query_heads), int(kv_heads), splits,
-                                                         dl::attention_scale(128), static_cast<float*>(workspace),
+                                                         int(query_heads), int(kv_heads), plan.splits,
+                                                         plan.lead_q10, dl::attention_scale(128),
+                                                         static_cast<float*>(workspace),
                                                          static_cast<bf16*>(output), st(stream)),
                      "attention decode batched");
 }

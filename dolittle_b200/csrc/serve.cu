@@ -137,7 +137,13 @@ Server::Server(const dl_model_config& cfg, int device, size_t batch, size_t capa
   // ---- scratch ----
   const size_t R = std::max(chunk_rows, batch), B = batch;
   history_cap_ = capacity + 1;
-  attn_splits_ = attention_decode_splits(int(B), hkv_, int(capacity), sms_);
+  // DOLITTLE_ATTN_PLAN=even keeps even key ranges (a tuning override).
+  static const bool even_ranges = [] {
+    const char* v = std::getenv("DOLITTLE_ATTN_PLAN");
+    return v && std::string(v) == "even";
+  }();
+  attn_plan_ = even_ranges ? AttnPlan{attention_decode_splits(int(B), hkv_, int(capacity), sms_), 0}
+                           : attention_decode_plan(int(B), hkv_, int(capacity), sms_);
   // Split-K partials of the decode projections (and the FP32 sums of the
   // row-sliced projections under tensor parallelism).
   const int Ns[4] = {int(Ql_ + 2 * Gl_), int(D_), int(2 * Fl_), int(D_)};
@@ -158,7 +164,7 @@ Server::Server(const dl_model_config& cfg, int device, size_t batch, size_t capa
                o_hlocal = grab(tp_ > 1 ? B * Vp_ * 2 : 0), o_hgather = grab(tp_ > 1 ? size_t(tp_) * B * Vp_ * 2 : 0),
                o_xlast = grab(B * D_ * 2), o_vt = grab(size_t(hkv_) * d_ * vt_stride_ * 2),
                o_parts = grab(parts_floats_ * 4),
-               o_ws = grab(attention_decode_ws_floats(int(B), hq_, attn_splits_) * 4),
+               o_ws = grab(attention_decode_ws_floats(int(B), hq_, attn_plan_.splits) * 4),
                o_tickets = grab(B * size_t(hkv_) * 4), o_tok = grab(R * 4),
                o_hist = grab(B * history_cap_ * 4), o_steps = grab(B * 4), o_pos = grab(8), o_err = grab(16),
                o_freq = grab(d_ / 2 * 4);
@@ -804,8 +810,9 @@ void Server::decode_body() {
       // The attention kernel builds the queries and appends the new key and
       // value from the qkv parts itself.
       const AttnQkvIn qi{parts_, parts, B, Q + 2 * G, y.q_norm, y.k_norm, inv_freq_, cfg_.epsilon};
-      check(launch_attention_decode_batched(q_rot_, planes(l), position_, B, hq_, hkv_, attn_splits_,
-                                            attention_scale(d), attn_ws_, att_, stream_, attn_tickets_, true, &qi),
+      check(launch_attention_decode_batched(q_rot_, planes(l), position_, B, hq_, hkv_, attn_plan_.splits,
+                                            attn_plan_.lead_q10, attention_scale(d), attn_ws_, att_, stream_,
+                                            attn_tickets_, true, &qi),
             "qkv parts + attention decode");
       launches_ += 2;
     } else {
@@ -813,8 +820,8 @@ void Server::decode_body() {
       check(launch_norm_rope_append_rows(qkv_, Q + 2 * G, y.q_norm, y.k_norm, inv_freq_, q_rot_, planes(l),
                                          position_, B, hq_, hkv_, d, cfg_.epsilon, stream_),
             "norm rope append");
-      check(launch_attention_decode_batched(q_rot_, planes(l), position_, B, hq_, hkv_, attn_splits_,
-                                            attention_scale(d), attn_ws_, att_, stream_),
+      check(launch_attention_decode_batched(q_rot_, planes(l), position_, B, hq_, hkv_, attn_plan_.splits,
+                                            attn_plan_.lead_q10, attention_scale(d), attn_ws_, att_, stream_),
             "attention decode");
       launches_ += 5;
     }

@@ -127,7 +127,7 @@ class Server {
   unsigned* err_;
   size_t history_cap_ = 0;
   int vt_stride_ = 0;
-  int attn_splits_ = 1;
+  AttnPlan attn_plan_{1, 0};  // key ranges of the decode attention
   std::vector<AttnTcMaps*> attn_maps_;
   Sampler sampler_;  // one row per sequence
   dl_sampling settings_ = {0, 1.0, 0, 1.0};

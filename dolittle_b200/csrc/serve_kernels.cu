@@ -213,20 +213,36 @@ __device__ __forceinline__ float combine_splits(const float* w, int splits, int 
 // the qkv projection's split-K parts instead (see AttnQkvIn).
 __global__ void __launch_bounds__(kAdThreads) attention_decode_split_kernel(
     const bf16* __restrict__ q, KvPlanes planes, const long long* __restrict__ position, int query_heads,
-    int kv_heads, int splits, float scale, float* __restrict__ ws, int* __restrict__ tickets,
+    int kv_heads, int splits, int lead_q10, float scale, float* __restrict__ ws, int* __restrict__ tickets,
     bf16* __restrict__ out, AttnQkvIn qi) {
   extern __shared__ __align__(16) unsigned char smem[];
   bf16* stage = reinterpret_cast<bf16*>(smem);
   bf16* ps = reinterpret_cast<bf16*>(smem + size_t(kAdStages) * kAdStageElems * 2);  // [16][72]
   float* wred = reinterpret_cast<float*>(ps + 16 * kAdPPitch);                          // [2][8 warps][8 heads]
   // KV head fastest: the heads of one (sequence, split) run side by side and
-  // together read whole cache rows (Hkv x 256 bytes per position).
-  const int g = blockIdx.x, s = blockIdx.y, b = blockIdx.z, t = threadIdx.x;
+  // together read whole cache rows (Hkv x 256 bytes per position).  Even
+  // ranges: grid (KV head, split, sequence).  A leading range (lead_q10 > 0,
+  // two splits): grid (KV head, sequence, split), so every sequence's long
+  // first range is launched before any short second one.
+  const bool lead = lead_q10 > 0;
+  const int g = blockIdx.x, s = lead ? blockIdx.z : blockIdx.y, b = lead ? blockIdx.y : blockIdx.z, t = threadIdx.x;
   const int warp = t >> 5, lane = t & 31, r = lane >> 2, c2 = (lane & 3) * 2;
   const int group = query_heads / kv_heads;
   const int count = int(*position) + 1;
-  const int per = ((count + splits - 1) / splits + kAdKeys - 1) / kAdKeys * kAdKeys;
-  const int j0 = min(count, s * per), j1 = min(count, j0 + per);
+  int j0, j1;
+  if (lead) {
+    // The first range holds lead_q10 / 1024 of the keys, rounded up to whole
+    // tiles; the second range the rest (empty when that covers them all).
+    const long long c = (static_cast<long long>(count) * lead_q10 + 1023) >> 10;
+    const long long up = (c + kAdKeys - 1) / kAdKeys * kAdKeys;
+    const int cut = up < count ? int(up) : count;
+    j0 = s == 0 ? 0 : cut;
+    j1 = s == 0 ? cut : count;
+  } else {
+    const int per = ((count + splits - 1) / splits + kAdKeys - 1) / kAdKeys * kAdKeys;
+    j0 = min(count, s * per);
+    j1 = min(count, j0 + per);
+  }
   const size_t G = size_t(kv_heads) * 128;
   const bf16* kbase = planes.kv + size_t(b) * planes.seq_stride + planes.k_off + size_t(g) * 128;
   const bf16* vbase = planes.kv + size_t(b) * planes.seq_stride + planes.v_off + size_t(g) * 128;
@@ -621,20 +637,24 @@ size_t attention_decode_ws_floats(int batch, int query_heads, int splits) {
   return size_t(batch) * query_heads * splits * kAdWs;
 }
 
+// Estimated time of `s` even splits per (sequence, KV head), in 64-key tiles:
+// waves of two resident CTAs per SM x (tiles per split + ~3 tiles of fixed
+// cost per CTA: query load, pipeline fill, partial write).
+static long long even_split_cost(long long units, long long slots, int tiles, int s) {
+  const long long waves = (units * s + slots - 1) / slots;
+  return waves * ((tiles + s - 1) / s + 3);
+}
+
 int attention_decode_splits(int batch, int kv_heads, int capacity, int sms) {
-  // Splits of each (sequence, KV head)'s keys by estimated time: waves of
-  // two resident CTAs per SM x (64-key tiles per split + ~3 tiles of fixed
-  // cost per CTA: query load, pipeline fill, partial write).  Measured on the
-  // batch-32 step: one split per (sequence, KV head) at 1K and 2K context
-  // (5.36 -> 5.08 and 6.18 -> 5.92 ms per step against 2 and 4 splits),
-  // about even from 1 to 4 splits at 8K.
+  // Measured on the batch-32 step: one split per (sequence, KV head) at 1K
+  // and 2K context (5.36 -> 5.08 and 6.18 -> 5.92 ms per step against 2 and
+  // 4 splits), about even from 1 to 4 splits at 8K.
   const long long units = std::max(1, batch * kv_heads), slots = 2ll * std::max(1, sms);
   const int tiles = std::max(1, (capacity + kAdKeys - 1) / kAdKeys);
   int best = 1;
   long long best_cost = -1;
   for (int s = 1; s <= std::min(64, tiles); ++s) {
-    const long long waves = (units * s + slots - 1) / slots;
-    const long long cost = waves * ((tiles + s - 1) / s + 3);
+    const long long cost = even_split_cost(units, slots, tiles, s);
     if (best_cost < 0 || cost < best_cost) {
       best = s;
       best_cost = cost;
@@ -643,11 +663,34 @@ int attention_decode_splits(int batch, int kv_heads, int capacity, int sms) {
   return best;
 }
 
+AttnPlan attention_decode_plan(int batch, int kv_heads, int capacity, int sms) {
+  AttnPlan plan{attention_decode_splits(batch, kv_heads, capacity, sms), 0};
+  const long long units = std::max(1, batch * kv_heads), slots = 2ll * std::max(1, sms);
+  const int tiles = std::max(1, (capacity + kAdKeys - 1) / kAdKeys);
+  if (units >= slots || tiles < 2) return plan;
+  // Fewer (sequence, KV head) units than slots: a long first range per unit
+  // keeps `units` slots busy for the whole launch while the spare slots run
+  // the short second ranges one after another (ceil(units / spare) each);
+  // +2 tiles for merging the two ranges.
+  long long best = even_split_cost(units, slots, tiles, plan.splits);
+  const long long spare = slots - units, chain = (units + spare - 1) / spare;
+  for (int first = 1; first < tiles; ++first) {
+    const long long cost = std::max<long long>(first + 3, chain * (tiles - first + 3)) + 2;
+    if (cost < best) {
+      best = cost;
+      plan.splits = 2;
+      plan.lead_q10 = int(std::min<long long>(1023, std::max<long long>(1, (first * 1024ll + tiles / 2) / tiles)));
+    }
+  }
+  return plan;
+}
+
 cudaError_t launch_attention_decode_batched(const bf16* q, KvPlanes planes, const long long* position, int batch,
-                                            int query_heads, int kv_heads, int splits, float scale, float* ws,
-                                            bf16* out, cudaStream_t stream, int* tickets, bool pdl,
+                                            int query_heads, int kv_heads, int splits, int lead_q10, float scale,
+                                            float* ws, bf16* out, cudaStream_t stream, int* tickets, bool pdl,
                                             const AttnQkvIn* qkv) {
-  if (query_heads % kv_heads || query_heads / kv_heads > kAdMaxGroup || splits < 1 || splits > 64 || batch < 1)
+  if (query_heads % kv_heads || query_heads / kv_heads > kAdMaxGroup || splits < 1 || splits > 64 || batch < 1 ||
+      lead_q10 < 0 || lead_q10 > 1023 || (lead_q10 > 0 && splits != 2) || batch > 65535)
     return cudaErrorInvalidValue;
   AttnQkvIn qi = {};
   if (qkv) {
@@ -660,9 +703,10 @@ cudaError_t launch_attention_decode_batched(const bf16* q, KvPlanes planes, cons
                                        int(kAdSmem));
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[1];
-  auto cfg = pdl_config(dim3(kv_heads, splits, batch), dim3(kAdThreads), kAdSmem, stream, attr, pdl);
+  const dim3 grid = lead_q10 > 0 ? dim3(kv_heads, batch, 2) : dim3(kv_heads, splits, batch);
+  auto cfg = pdl_config(grid, dim3(kAdThreads), kAdSmem, stream, attr, pdl);
   e = cudaLaunchKernelEx(&cfg, attention_decode_split_kernel, q, planes, position, query_heads, kv_heads, splits,
-                         scale, ws, tickets, out, qi);
+                         lead_q10, scale, ws, tickets, out, qi);
   if (e != cudaSuccess || tickets) return e;
   attention_decode_combine_kernel<<<dim3(query_heads, batch), 128, 0, stream>>>(ws, query_heads, splits, out);
   return cudaGetLastError();

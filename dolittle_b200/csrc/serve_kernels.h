@@ -40,12 +40,21 @@ cudaError_t launch_residual_norm_rows(const float* parts, int splits, int M, int
 
 // Split-K flash decoding: for every sequence b and query head h, attention of
 // q [B][Hq][128] over keys 0 .. *position of b's cache, the keys cut into
-// `splits` ranges (attention_decode_splits: a wave-cost model) whose (max,
-// sum, unnormalised output) go to ws [B][Hq][splits][130] FP32, merged into
-// out [B][Hq*128] BF16 by the combine kernel.  Online softmax: not the
-// reference's reduction order.
+// `splits` ranges whose (max, sum, unnormalised output) go to ws
+// [B][Hq][splits][130] FP32, merged into out [B][Hq*128] BF16 by the combine
+// kernel.  Online softmax: not the reference's reduction order.  The ranges
+// are even, or (lead_q10 > 0, two splits) a first range of lead_q10 / 1024
+// of the keys (rounded up to 64-key tiles) and the rest.
 size_t attention_decode_ws_floats(int batch, int query_heads, int splits);
+// Even splits by a wave-cost model (two resident CTAs per SM).
 int attention_decode_splits(int batch, int kv_heads, int capacity, int sms);
+struct AttnPlan {
+  int splits;
+  int lead_q10;  // 0: even ranges
+};
+// The even splits, or a leading range when fewer (sequence, KV head) units
+// than CTA slots would leave slots idle for the whole launch.
+AttnPlan attention_decode_plan(int batch, int kv_heads, int capacity, int sms);
 // tickets ([B][Hkv] int, zeroed once; each launch leaves them zero): the
 // last split of each (sequence, KV head) merges the splits itself, no
 // combine launch (with one split the CTA writes O / l directly).  pdl:
@@ -66,8 +75,8 @@ struct AttnQkvIn {
   float eps;
 };
 cudaError_t launch_attention_decode_batched(const bf16* q, KvPlanes planes, const long long* position, int batch,
-                                            int query_heads, int kv_heads, int splits, float scale, float* ws,
-                                            bf16* out, cudaStream_t stream, int* tickets = nullptr,
+                                            int query_heads, int kv_heads, int splits, int lead_q10, float scale,
+                                            float* ws, bf16* out, cudaStream_t stream, int* tickets = nullptr,
                                             bool pdl = false, const AttnQkvIn* qkv = nullptr);
 
 // Vocabulary-split head: src [t][B][Vp] (rank r's logits of vocabulary rows

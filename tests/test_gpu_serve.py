@@ -67,8 +67,12 @@ def test_gemm_parts_matches_fp32_reference(M, N, K, epi):
 
 
 @pytest.mark.parametrize("B,Hq,Hkv,count,cap", [(3, 8, 2, 201, 256), (2, 32, 8, 1000, 1024), (4, 4, 1, 5, 64),
-                                                (1, 32, 8, 9216, 9216)])
+                                                (1, 32, 8, 9216, 9216), (32, 32, 8, 8000, 8192),
+                                                (32, 32, 8, 100, 8192)])
 def test_attention_decode_batched_matches_fp32_reference(B, Hq, Hkv, count, cap):
+    """The last two cases take the leading-range plan on a 148-SM B200 (256
+    (sequence, KV head) units on 296 CTA slots): a long first key range per
+    unit and a short second one; at 100 keys the second range is empty."""
     torch = _torch()
     g = torch.Generator(device="cuda").manual_seed(B * 100 + count)
     G = Hkv * 128
@@ -78,8 +82,10 @@ def test_attention_decode_batched_matches_fp32_reference(B, Hq, Hkv, count, cap)
     pos = torch.tensor([count - 1], device="cuda", dtype=torch.int64)
     out = torch.empty(B, Hq * 128, device="cuda", dtype=torch.bfloat16)
     L = dl.lib()
-    ws = torch.empty(L.dl_attention_decode_batched_workspace_bytes(B, Hq, Hkv, cap) // 4 + 1, device="cuda",
-                     dtype=torch.float32)
+    ws_bytes = L.dl_attention_decode_batched_workspace_bytes(B, Hq, Hkv, cap)
+    if B * Hkv == 256 and torch.cuda.get_device_properties(0).multi_processor_count == 148:
+        assert ws_bytes == B * Hq * 2 * 130 * 4  # two ranges per unit
+    ws = torch.empty(ws_bytes // 4 + 1, device="cuda", dtype=torch.float32)
     assert L.dl_attention_decode_batched(q.data_ptr(), kv.data_ptr(), 2 * cap * G, 0, cap * G, pos.data_ptr(), B, Hq,
                                          Hkv, cap, out.data_ptr(), ws.data_ptr(), None) == 0, L.dl_last_error()
     torch.cuda.synchronize()
@@ -172,6 +178,44 @@ def test_fused_decode_step_gives_the_same_bits_as_separate_kernels(capture_layer
     saved = 5 * cfg.layers - (1 if capture_layer >= 0 else 0)
     assert r0.kernels_per_decode_step - r1.kernels_per_decode_step == saved, (r0.kernels_per_decode_step,
                                                                                r1.kernels_per_decode_step)
+
+
+def test_leading_range_attention_plan_in_the_decode_step():
+    """56 sequences x 4 KV heads (224 units on 296 CTA slots of a 148-SM
+    B200) at capacity 2048 take the leading-range attention plan: the fused
+    step gives the same bits as the separate kernels, and the first decode
+    step's logits of three of the sequences match a batch-3 server (even
+    splits) within the fast-path tolerance."""
+    torch = _torch()
+    L = dl.lib()
+    cfg = _small_cfg(2)
+    B, P, cap, steps = 56, 1900, 2048, 4
+    if torch.cuda.get_device_properties(0).multi_processor_count == 148:
+        assert L.dl_attention_decode_batched_workspace_bytes(B, cfg.query_heads, cfg.kv_heads, cap) == \
+            B * cfg.query_heads * 2 * 130 * 4
+    prompts = np.stack([oracle.uniform_ids(P, 300 + b, 0, cfg.vocabulary) for b in range(B)])
+    greedy = dl.Settings()
+    runs = []
+    for fused in (True, False):
+        srv = Server(cfg, batch=B, capacity=cap, chunk_rows=512)
+        srv.init_random(17, 0.02)
+        srv.set_step_fusion(fused)
+        first = srv.prefill(prompts, greedy)
+        runs.append((first, srv.decode(steps, want_logits=True)))
+        srv.close()
+    (f1, r1), (f0, r0) = runs
+    assert np.array_equal(f1, f0)
+    assert np.array_equal(r1.tokens, r0.tokens)
+    assert np.array_equal(r1.logits, r0.logits)
+    small = Server(cfg, batch=3, capacity=cap, chunk_rows=512)
+    small.init_random(17, 0.02)
+    fs = small.prefill(prompts[:3], greedy)
+    rs = small.decode(1, want_logits=True)
+    small.close()
+    assert np.array_equal(fs, f1[:3])
+    for b in range(3):
+        ok, r = _close(rs.logits[0, b], r1.logits[0, b])
+        assert ok, (b, r)
 
 
 def test_server_greedy_tokens_are_the_argmax_of_its_logits():
