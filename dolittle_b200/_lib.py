@@ -144,6 +144,7 @@ SIGNATURES = {
     "dl_gemm_bf16_parts_workspace_bytes": (sz, [sz, sz, sz, sz]),
     "dl_gemm_bf16_parts": (C.c_int, [vp, sz, vp, vp, sz, sz, sz, sz, C.c_int, sz, vp, vp]),
     "dl_attention_decode_batched_workspace_bytes": (sz, [sz, sz, sz, sz]),
+    "dl_attention_decode_batched_plan": (C.c_int, [sz, sz, sz, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "dl_attention_decode_batched": (C.c_int, [vp, vp, sz, sz, sz, vp, sz, sz, sz, sz, vp, vp, vp]),
 }
 

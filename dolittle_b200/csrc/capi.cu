@@ -3,6 +3,7 @@
 // src/kernels/cuda/common.cuh:57-65): unsupported dtypes and shapes are
 // rejected, never silently converted.  Exceptions become dl_status codes and
 // a thread-local message.
+#include <climits>
 #include <cstring>
 #include <exception>
 #include <new>
@@ -756,6 +757,17 @@ DL_API dl_status dl_gemm_bf16_parts(const void* x, size_t ldx, const void* w, vo
   return cuda_status(dl::launch_gemm_splitk_epilogue(static_cast<const float*>(workspace), p, int(M), int(N), epilogue,
                                                      static_cast<bf16*>(y), int(ldy), nullptr, st(stream)),
                      "gemm parts epilogue");
+}
+
+DL_API dl_status dl_attention_decode_batched_plan(size_t batch, size_t kv_heads, size_t capacity, int sms,
+                                                  int* splits, int* lead_q10) {
+  if (!splits || !lead_q10 || !batch || !kv_heads || !capacity || sms < 1 || batch > 65535 || kv_heads > 65535 ||
+      capacity > size_t(INT_MAX))
+    return fail(DL_INVALID_ARGUMENT, "attention decode plan: null output, empty shape or size out of range");
+  const dl::AttnPlan plan = dl::attention_decode_plan(int(batch), int(kv_heads), int(capacity), sms);
+  *splits = plan.splits;
+  *lead_q10 = plan.lead_q10;
+  return DL_OK;
 }
 
 DL_API size_t dl_attention_decode_batched_workspace_bytes(size_t batch, size_t query_heads, size_t kv_heads,

@@ -450,6 +450,12 @@ DL_API dl_status dl_gemm_bf16_parts(const void* x, size_t ldx, const void* w, vo
  * dl_attention_decode_batched_workspace_bytes FP32. */
 DL_API size_t dl_attention_decode_batched_workspace_bytes(size_t batch, size_t query_heads, size_t kv_heads,
                                                           size_t capacity);
+/* The key ranges dl_attention_decode_batched (and the server's decode step)
+ * cut each (sequence, KV head) into on a device of `sms` SMs: *splits even
+ * ranges (*lead_q10 = 0), or two ranges whose first holds *lead_q10 / 1024
+ * of the keys, rounded up to 64-key tiles.  Host arithmetic only. */
+DL_API dl_status dl_attention_decode_batched_plan(size_t batch, size_t kv_heads, size_t capacity, int sms,
+                                                  int* splits, int* lead_q10);
 DL_API dl_status dl_attention_decode_batched(const void* query, const void* kv, size_t seq_stride,
                                              size_t k_offset, size_t v_offset, const int64_t* position,
                                              size_t batch, size_t query_heads, size_t kv_heads, size_t capacity,

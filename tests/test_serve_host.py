@@ -85,3 +85,39 @@ def _rank_main(rank, world, port):
 
 def test_nccl_id_reaches_every_rank():
     mp.spawn(_rank_main, args=(2, _free_port()), nprocs=2, join=True)
+
+
+def _plan(batch, kv_heads, capacity, sms=148):
+    import ctypes as C
+    splits, lead = C.c_int(-1), C.c_int(-1)
+    assert dl.lib().dl_attention_decode_batched_plan(batch, kv_heads, capacity, sms, C.byref(splits),
+                                                     C.byref(lead)) == 0
+    return splits.value, lead.value
+
+
+def test_attention_plan_choices():
+    """The batched decode attention's key ranges (host arithmetic, no GPU):
+    batch 32 x 8 KV heads is 256 units on 296 CTA slots of a 148-SM B200.
+    At 8K context a long first range per unit plus a short second one beats
+    even ranges; at 2K one range per unit stays; under two-way tensor
+    parallelism (4 local KV heads) two even ranges fill the slots."""
+    splits, lead = _plan(32, 8, 8192 + 32 * 6 + 8)  # the config-5 bench's capacity
+    assert splits == 2 and 850 < lead < 1000, (splits, lead)
+    assert _plan(32, 8, 2048 + 32 * 6 + 8) == (1, 0)
+    assert _plan(32, 4, 2048 + 32 * 6 + 8) == (2, 0)
+    assert _plan(56, 4, 2048)[0] == 2 and _plan(56, 4, 2048)[1] > 0  # the GPU test's server shape
+    # More units than slots: even ranges only.
+    for cap in (512, 2048, 8192, 32768):
+        assert _plan(128, 8, cap)[1] == 0
+    # One unit: many even ranges, never the leading form.
+    s1, l1 = _plan(1, 8, 9216)
+    assert l1 == 0 and s1 > 1
+
+
+def test_attention_plan_rejects_bad_arguments():
+    import ctypes as C
+    L = dl.lib()
+    out = C.c_int()
+    assert L.dl_attention_decode_batched_plan(32, 8, 2048, 148, None, C.byref(out)) != 0
+    assert L.dl_attention_decode_batched_plan(0, 8, 2048, 148, C.byref(out), C.byref(out)) != 0
+    assert L.dl_attention_decode_batched_plan(32, 8, 2048, 0, C.byref(out), C.byref(out)) != 0
